@@ -1,0 +1,179 @@
+/*
+ * wfk.h -- C ABI of libwfk.so, the B200 (sm_100a) implementation of WaveRT's
+ * per-layer DiT hot path.
+ *
+ * Conventions (all entry points):
+ *   - plain pointers and sizes only; device pointers are device addresses of
+ *     the current CUDA device, `stream` is a cudaStream_t passed as void*;
+ *   - every call is stream-ordered and returns 0 (WF_OK) or a WF_ERR_* code;
+ *     wf_last_error() gives the calling thread's message for the last
+ *     failure (the Python shim raises RuntimeError with it, the convention of
+ *     wave_rt/distributed/ipc.py:28-37);
+ *   - no entry point allocates device memory unless its comment says so; the
+ *     caller owns every buffer;
+ *   - strides are in elements, the innermost dimension is contiguous.
+ *
+ * Reference interfaces are cited as path:line inside SJTU-DENG-Lab/WaveForcing.
+ */
+#ifndef WFK_H_
+#define WFK_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WF_OK 0
+#define WF_ERR_INVALID_ARG 1
+#define WF_ERR_UNSUPPORTED 2
+#define WF_ERR_CUDA 3
+#define WF_ERR_TIMEOUT 4
+
+#define WF_DTYPE_BF16 0
+#define WF_DTYPE_E4M3 1
+#define WF_DTYPE_S8 2
+
+#define WF_SCALE_NONE 0
+#define WF_SCALE_TENSOR 1
+#define WF_SCALE_TOKEN 2
+
+/* ------------------------------------------------------------ library */
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* wf_last_error(void);
+
+/* ABI version (incremented on any signature change). */
+int wf_version(void);
+
+/* Reads and clears the device status word of the current device (bitmask of
+ * bounded waits that gave up; 0 = healthy).  Synchronises the device. */
+unsigned int wf_status_take(void);
+
+/* ---------------------------------------------------------- attention */
+
+/* O = softmax(Q K^T * softmax_scale) V, non-causal, NHD layout, D = 128.
+ * Replaces the attention call of the patched self-attention,
+ * wave_rt/runtime/backend.py:141-148 (SGLang torch_sdpa / flash_attn_func /
+ * sageattn on (roped_query, ctx_k, ctx_v)); block causality is given by which
+ * chunks the caller places in K/V (wave_rt/denoiser/exchange/paged.py:247-248).
+ * Shapes: q/o [batch, Lq, H, D], k/v [batch, Lk, H, D]; strides are
+ * {batch, token, head} in elements.  kv_dtype must be WF_DTYPE_BF16 (FP8 K/V
+ * pages are dequantised on receive by wf_kv_dequant); k_scale, v_scale and
+ * scale_mode are reserved and must be NULL/NULL/WF_SCALE_NONE.
+ * Requires 16-byte aligned base pointers and strides that are multiples of 8. */
+int wf_attn_fwd(const void* q, const void* k, const void* v, void* o, int batch, int Lq, int Lk, int H, int D,
+                const int64_t* q_stride, const int64_t* k_stride, const int64_t* v_stride,
+                const int64_t* o_stride, int kv_dtype, const float* k_scale, const float* v_scale,
+                int scale_mode, float softmax_scale, void* stream);
+
+/* ------------------------------------------------------- FP8 K/V codec */
+
+/* Quantise a bf16 [rows, cols] matrix (row stride x_row_stride) to e4m3fn
+ * codes [rows, cols] (dense) with the reference's dtype sequence
+ *   s = f32(clamp(bf16(amax|x| / 448), 1e-8)); code = e4m3(bf16(x / s))
+ * wave_rt/denoiser/exchange/common.py:143-150 (per-tensor, mode
+ * WF_SCALE_TENSOR: one scale in scales[0]) or the same sequence per row
+ * (mode WF_SCALE_TOKEN: scales[rows]).  Per-tensor mode needs a grid-wide
+ * amax and uses `workspace` (>= 4 bytes of device memory, caller-owned,
+ * overwritten); per-token mode ignores it. */
+int wf_kv_quant(const void* x, uint8_t* codes, float* scales, int64_t rows, int64_t cols, int64_t x_row_stride,
+                int mode, void* workspace, void* stream);
+
+/* Dequantise codes [rows, cols] to bf16 out (row stride out_row_stride):
+ * out = bf16(e4m3(code) * scale), the receive side of
+ * wave_rt/denoiser/exchange/common.py:162 and onesided.py:177-179
+ * (mode WF_SCALE_NONE: scale-free cast back, scales ignored). */
+int wf_kv_dequant(const uint8_t* codes, const float* scales, void* out, int64_t rows, int64_t cols,
+                  int64_t out_row_stride, int mode, void* stream);
+
+/* Per-token quantise K and V of one layer and write codes + scales straight
+ * into n_dst destination slots (local or peer device memory), the FP8 form of
+ * the layer-wise publish wave_rt/denoiser/exchange/paged.py:120-145.
+ * k, v: bf16 [rows, cols] with row strides; dst_codes_k[i]/dst_codes_v[i]:
+ * [rows, cols] u8; dst_scales_k[i]/dst_scales_v[i]: [rows] f32. */
+int wf_kv_quant_publish(const void* k, const void* v, int64_t rows, int64_t cols, int64_t k_row_stride,
+                        int64_t v_row_stride, uint8_t* const* dst_codes_k, uint8_t* const* dst_codes_v,
+                        float* const* dst_scales_k, float* const* dst_scales_v, int n_dst, void* stream);
+
+/* ------------------------------------------------------------- W8A8 */
+
+/* Per-output-channel weight quantisation (load time), the per-channel form of
+ * wave_rt/runtime/fp8.py:32-36: s[n] = clamp(amax|w[n,:]| / Q, 1e-8) in f32,
+ * q = e4m3(w / s) (qtype WF_DTYPE_E4M3, Q = 448) or rne-int8 clamp(+-127)
+ * (WF_DTYPE_S8, Q = 127).  w: bf16 [N, K]. */
+int wf_weight_quant(const void* w, void* wq, float* w_scale, int64_t N, int64_t K, int qtype, void* stream);
+
+/* Per-token dynamic activation quantisation, the per-row form of
+ * wave_rt/runtime/fp8.py:47-48 (bf16 scale math).  x: bf16 [M, K] with row
+ * stride x_row_stride -> xq [M, K] dense, x_scale [M]. */
+int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, int64_t K, int64_t x_row_stride, int qtype,
+                 void* stream);
+
+/* y[M, N] (bf16, row stride y_row_stride) = (xq[M, K] . wq[N, K]^T) * x_scale[m] * w_scale[n] + bias[n]
+ * on tcgen05 (kind::f8f6f4 for e4m3, kind::i8 for s8), replacing the
+ * torch._scaled_mm call of wave_rt/runtime/fp8.py:49-56.  scale_mode
+ * WF_SCALE_TENSOR reads x_scale[0] and w_scale[0] (the reference's
+ * per-tensor form), WF_SCALE_TOKEN reads x_scale[M] and w_scale[N].
+ * bias may be NULL.  K must be a multiple of 128 and N of 16. */
+int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq, const float* w_scale, const void* bias,
+                 void* y, int M, int N, int K, int64_t y_row_stride, int qtype, int scale_mode, void* stream);
+
+/* ---------------------------------------------------------------- RoPE */
+
+/* Interleaved (non-neox) rotary embedding, y = x * (cos + i sin) on complex
+ * pairs, f32 math, bf16 out: the anchor re-RoPE of
+ * wave_rt/denoiser/exchange/common.py:84-87 (SGLang _apply_rotary_emb with
+ * is_neox_style=False) and the q/k RoPE of wave_rt/runtime/backend.py:119-121.
+ * x, y: bf16 [L, H, D] with token strides (head stride D); cos/sin: f32
+ * [L, D/2].  y may alias x. */
+int wf_rope_apply(const void* x, void* y, const float* cos_t, const float* sin_t, int64_t L, int H, int D,
+                  int64_t x_tok_stride, int64_t y_tok_stride, void* stream);
+
+/* ------------------------------------------------ exchange primitives */
+
+/* IPC export of the allocation holding `p`; replaces ipc_export,
+ * wave_rt/distributed/ipc.py:147-152 (handle bytes + offset of p in it). */
+int wf_ipc_export(const void* p, uint8_t* handle64, uint64_t* offset);
+
+/* Opens a peer handle in the current context with lazy peer access;
+ * replaces ipc_open_handle, wave_rt/distributed/ipc.py:112-118. */
+int wf_ipc_open(const uint8_t* handle64, void** base);
+
+/* Closes a mapping opened by wf_ipc_open; replaces ipc_close_handle,
+ * wave_rt/distributed/ipc.py:135-136. */
+int wf_ipc_close(void* base);
+
+/* Enables peer access from the current device to `peer` (idempotent). */
+int wf_enable_peer(int peer);
+
+/* Stream-ordered 32-bit release write; replaces stream_write_u32,
+ * wave_rt/distributed/ipc.py:43-47. */
+int wf_stream_write_u32(void* stream, void* addr, uint32_t value);
+
+/* Stream-ordered unbounded acquire wait (*addr >= value); replaces
+ * stream_wait_u32, wave_rt/distributed/ipc.py:50-54.  Prefer wf_wait_flag. */
+int wf_stream_wait_u32(void* stream, const void* addr, uint32_t value);
+
+/* Bounded device-side acquire: a one-thread kernel on `stream` spins with
+ * ld.acquire.sys until *flag >= value or timeout_ns elapses.  On timeout it
+ * writes 1 to *timeout_out (device or host-mapped memory, may be NULL), raises
+ * the device status word and returns, leaving the stream usable.  Replaces the
+ * wait of wave_rt/denoiser/exchange/paged.py:147-154, which has no timeout. */
+int wf_wait_flag(const void* flag, uint32_t value, uint64_t timeout_ns, uint32_t* timeout_out, void* stream);
+
+/* Asynchronous device-to-device (or peer) copy of `bytes`; replaces
+ * memcpy_dtod_async, wave_rt/distributed/ipc.py:60-67. */
+int wf_memcpy_async(void* dst, const void* src, uint64_t bytes, void* stream);
+
+/* One layer's publish to n destinations: for each i, copy bytes from src to
+ * dsts[i] and then write `value` to flags[i] on the same stream (payload
+ * before flag), as wave_rt/denoiser/exchange/paged.py:134-141. */
+int wf_publish(void* const* dsts, const void* src, uint64_t bytes, void* const* flags, int n, uint32_t value,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WFK_H_ */

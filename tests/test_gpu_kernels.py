@@ -1,0 +1,369 @@
+"""Parity of the libwfk CUDA kernels with the CPU oracle (B200 only).
+
+Tolerances (stated per BASELINE north_star):
+  * codec codes and scales, W8A8 quantised operands: bit-exact;
+  * attention and GEMM outputs: max|out - ref| / max|ref| <= 1e-2 (bf16 out);
+  * RoPE: within 2 bf16 ulps of the float64 oracle (f32 vs f64 rotation).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as o_attn
+from oracle import codec as o_codec
+from oracle import rope as o_rope
+from oracle import w8a8 as o_w8a8
+from tests.conftest import bits_to_f32
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
+
+DEV = "cuda"
+
+
+def _kernels():
+    from waveforcing_b200 import kernels
+
+    return kernels
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
+
+
+def _bf16_gpu(x_np):
+    return torch.from_numpy(np.ascontiguousarray(x_np, np.float32)).to(DEV).to(torch.bfloat16)
+
+
+def _f32(t):
+    return t.float().cpu().numpy()
+
+
+# ------------------------------------------------------------------ attention
+ATTN_CASES = [
+    (128, 128, 1), (130, 300, 2), (5, 517, 3), (257, 1000, 2), (64, 64, 2), (1, 1, 1),
+    (300, 129, 4), (4680, 4680, 1),
+]
+
+
+@pytest.mark.parametrize("Lq,Lk,H", ATTN_CASES)
+def test_attention_matches_oracle(Lq, Lk, H):
+    K = _kernels()
+    rng = np.random.default_rng(Lq * 7 + Lk * 3 + H)
+    q = o_codec.bf16_round(rng.standard_normal((Lq, H, 128)).astype(np.float32))
+    k = o_codec.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    v = o_codec.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    out = K.attention(_bf16_gpu(q), _bf16_gpu(k), _bf16_gpu(v))
+    torch.cuda.synchronize()
+    ref = o_attn.sdpa_numpy(q, k, v)
+    assert _rel(_f32(out), ref) <= 1e-2
+
+
+def test_attention_golden(golden):
+    K = _kernels()
+    g = golden("sdpa.npz")
+    for i in range(int(g["n"])):
+        q, k, v = (bits_to_f32(g[f"c{i}_{t}"]) for t in "qkv")
+        out = K.attention(_bf16_gpu(q), _bf16_gpu(k), _bf16_gpu(v))
+        assert _rel(_f32(out), g[f"c{i}_o"]) <= 1e-2, i
+
+
+def test_attention_large_logits_rescale():
+    """Rows whose max grows late exercise the lazy O rescale path."""
+    K = _kernels()
+    rng = np.random.default_rng(5)
+    Lq, Lk, H = 200, 700, 2
+    q = o_codec.bf16_round((rng.standard_normal((Lq, H, 128)) * 3).astype(np.float32))
+    k = rng.standard_normal((Lk, H, 128)).astype(np.float32)
+    k[600:] *= 6.0  # late keys dominate
+    k = o_codec.bf16_round(k)
+    v = o_codec.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    out = K.attention(_bf16_gpu(q), _bf16_gpu(k), _bf16_gpu(v))
+    assert _rel(_f32(out), o_attn.sdpa_numpy(q, k, v)) <= 1e-2
+
+
+def test_attention_strided_views_and_batch():
+    """Non-contiguous slab prefixes (paged Kb[:active_len]) and batch > 1."""
+    K = _kernels()
+    torch.manual_seed(0)
+    slab_k = torch.randn(2, 900, 3, 128, device=DEV).to(torch.bfloat16)
+    slab_v = torch.randn(2, 900, 3, 128, device=DEV).to(torch.bfloat16)
+    q = torch.randn(2, 150, 3, 128, device=DEV).to(torch.bfloat16)
+    k, v = slab_k[:, :700], slab_v[:, :700]
+    out = K.attention(q, k, v)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q.float().transpose(1, 2), k.float().transpose(1, 2), v.float().transpose(1, 2)).transpose(1, 2)
+    assert (out.float() - ref).abs().max().item() / ref.abs().max().item() <= 1e-2
+
+
+def test_attention_config1_full_size():
+    """BASELINE config 1 shape (q 4680, K/V 14040, 12x128) against torch fp32 SDPA."""
+    K = _kernels()
+    g = torch.Generator(device="cpu").manual_seed(0)
+    q = (torch.randn(1, 4680, 12, 128, generator=g) / math.sqrt(128)).to(DEV)
+    k = (torch.randn(1, 14040, 12, 128, generator=g) / math.sqrt(128)).to(DEV)
+    v = (torch.randn(1, 14040, 12, 128, generator=g) / math.sqrt(128)).to(DEV)
+    qb, kb, vb = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    out = K.attention(qb, kb, vb)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        qb.float().transpose(1, 2), kb.float().transpose(1, 2), vb.float().transpose(1, 2)).transpose(1, 2)
+    rel = (out.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert rel <= 1e-2, rel
+
+
+def test_attention_rejects_bad_args():
+    K = _kernels()
+    q = torch.zeros(4, 1, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        K.attention(q, q, q)  # head_dim 64 unsupported
+    with pytest.raises(RuntimeError):
+        K.attention(q.cpu(), q.cpu(), q.cpu())
+
+
+# ---------------------------------------------------------------------- codec
+def _codec_inputs():
+    rng = np.random.default_rng(11)
+    yield "normal", rng.standard_normal((300, 1536)).astype(np.float32)
+    wide = rng.standard_normal((97, 1536)) * np.exp(rng.standard_normal((97, 1536)) * 4)
+    yield "wide", wide.astype(np.float32)
+    yield "tiny", (rng.standard_normal((33, 1536)) * 1e-9).astype(np.float32)
+    z = rng.standard_normal((17, 5120)).astype(np.float32)
+    z[3] = 0
+    yield "zero-row", z
+    yield "odd-cols", rng.standard_normal((21, 264)).astype(np.float32)
+
+
+@pytest.mark.parametrize("mode", ["token", "tensor"])
+def test_kv_quant_bit_exact(mode):
+    K = _kernels()
+    from waveforcing_b200._lib import WF_SCALE_TENSOR, WF_SCALE_TOKEN
+
+    for name, x in _codec_inputs():
+        xb = o_codec.bf16_round(x)
+        if mode == "token":
+            ref_c, ref_s = o_codec.quant_per_token(xb)
+            codes, scales = K.kv_quant(_bf16_gpu(xb), WF_SCALE_TOKEN)
+        else:
+            ref_c, ref_s = o_codec.quant_per_tensor(xb)
+            codes, scales = K.kv_quant(_bf16_gpu(xb), WF_SCALE_TENSOR)
+        assert np.array_equal(codes.cpu().numpy(), ref_c), name
+        assert np.array_equal(scales.cpu().numpy().reshape(-1), np.asarray(ref_s, np.float32).reshape(-1)), name
+
+
+def test_kv_quant_golden_reference_vectors(golden):
+    K = _kernels()
+    from waveforcing_b200._lib import WF_SCALE_TENSOR
+
+    g = golden("codec_per_tensor.npz")
+    for i in range(int(g["n"])):
+        x = bits_to_f32(g[f"c{i}_x"])
+        x2 = x.reshape(-1, x.shape[-1])
+        codes, scales = K.kv_quant(_bf16_gpu(x2), WF_SCALE_TENSOR)
+        assert np.array_equal(codes.cpu().numpy().reshape(g[f"c{i}_codes"].shape), g[f"c{i}_codes"]), i
+        assert scales.item() == float(g[f"c{i}_scale"]), i
+
+
+def test_kv_quant_all_bf16_values():
+    """Every finite bf16 pattern quantised under a fixed row amax."""
+    K = _kernels()
+    from waveforcing_b200._lib import WF_SCALE_TOKEN
+
+    b = np.arange(65536, dtype=np.uint32)
+    f = o_codec.bf16_from_bits(b)
+    f = f[np.isfinite(f)]
+    for amax in (1.0, 3.0e4, 7.5e-3, 1e-12):
+        vals = np.clip(f, -amax, amax)
+        n = (vals.size // 1536) * 1536
+        x = vals[:n].reshape(-1, 1536).copy()
+        x[:, 0] = amax
+        ref_c, ref_s = o_codec.quant_per_token(x)
+        codes, scales = K.kv_quant(_bf16_gpu(x), WF_SCALE_TOKEN)
+        got = codes.cpu().numpy()
+        bad = np.argwhere(got != ref_c)
+        assert np.array_equal(scales.cpu().numpy(), ref_s), amax
+        assert bad.size == 0, (amax, bad[:4].tolist(), x[tuple(bad[0])], got[tuple(bad[0])], ref_c[tuple(bad[0])])
+
+
+@pytest.mark.parametrize("mode", ["token", "tensor", "none"])
+def test_kv_dequant_bit_exact(mode):
+    K = _kernels()
+    from waveforcing_b200._lib import WF_SCALE_NONE, WF_SCALE_TENSOR, WF_SCALE_TOKEN
+
+    rng = np.random.default_rng(3)
+    x = o_codec.bf16_round(rng.standard_normal((129, 1536)).astype(np.float32) * 5)
+    if mode == "token":
+        c, s = o_codec.quant_per_token(x)
+        ref = o_codec.bf16_round(o_codec.dequant(c, s, True))
+        m = WF_SCALE_TOKEN
+    elif mode == "tensor":
+        c, s = o_codec.quant_per_tensor(x)
+        ref = o_codec.bf16_round(o_codec.dequant(c, s, False))
+        s = np.array([s], np.float32)
+        m = WF_SCALE_TENSOR
+    else:
+        c = o_codec.cast_scale_free(x)
+        s = None
+        ref = o_codec.e4m3_decode(c)
+        m = WF_SCALE_NONE
+    sc = torch.from_numpy(np.asarray(s, np.float32)).to(DEV) if s is not None else None
+    out = K.kv_dequant(torch.from_numpy(c).to(DEV), sc, m)
+    assert np.array_equal(_f32(out), ref)
+
+
+def test_kv_quant_publish_fans_out():
+    K = _kernels()
+    from waveforcing_b200._lib import WF_SCALE_TOKEN
+
+    torch.manual_seed(1)
+    k = torch.randn(300, 1536, device=DEV).to(torch.bfloat16)
+    v = torch.randn(300, 1536, device=DEV).to(torch.bfloat16) * 3
+    ck, sk = K.kv_quant(k, WF_SCALE_TOKEN)
+    cv, sv = K.kv_quant(v, WF_SCALE_TOKEN)
+    dst = [(torch.empty_like(ck), torch.empty_like(cv), torch.empty_like(sk), torch.empty_like(sv)) for _ in range(3)]
+    K.kv_quant_publish(k, v, [d[0].data_ptr() for d in dst], [d[1].data_ptr() for d in dst],
+                       [d[2].data_ptr() for d in dst], [d[3].data_ptr() for d in dst])
+    for d in dst:
+        assert torch.equal(d[0], ck) and torch.equal(d[1], cv)
+        assert torch.equal(d[2], sk) and torch.equal(d[3], sv)
+
+
+# ----------------------------------------------------------------------- W8A8
+@pytest.mark.parametrize("qtype", ["e4m3", "s8"])
+def test_quantisers_bit_exact(qtype):
+    K = _kernels()
+    from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
+
+    qt = WF_DTYPE_E4M3 if qtype == "e4m3" else WF_DTYPE_S8
+    rng = np.random.default_rng(2)
+    w = o_codec.bf16_round((rng.standard_normal((96, 256)) * 0.02).astype(np.float32))
+    x = o_codec.bf16_round((rng.standard_normal((70, 256)) * 2).astype(np.float32))
+    wq, ws = K.weight_quant(_bf16_gpu(w), qt)
+    xq, xs = K.act_quant(_bf16_gpu(x), qt)
+    rwq, rws = o_w8a8.quant_weight(w, qtype, per_channel=True)
+    rxq, rxs = o_w8a8.quant_act(x, qtype, per_token=True)
+    assert np.array_equal(ws.cpu().numpy(), rws)
+    assert np.array_equal(xs.cpu().numpy(), rxs)
+    assert np.array_equal(wq.cpu().numpy().view(rwq.dtype), rwq)
+    assert np.array_equal(xq.cpu().numpy().view(rxq.dtype), rxq)
+
+
+@pytest.mark.parametrize("qtype", ["e4m3", "s8"])
+@pytest.mark.parametrize("M,N,K_", [(128, 256, 128), (300, 512, 384), (4680, 1536, 1536), (77, 96, 256)])
+def test_gemm_w8a8_matches_oracle(qtype, M, N, K_):
+    K = _kernels()
+    from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
+
+    qt = WF_DTYPE_E4M3 if qtype == "e4m3" else WF_DTYPE_S8
+    rng = np.random.default_rng(M + N + K_)
+    w = o_codec.bf16_round((rng.standard_normal((N, K_)) * 0.02).astype(np.float32))
+    x = o_codec.bf16_round((rng.standard_normal((M, K_)) * 2).astype(np.float32))
+    b = o_codec.bf16_round((rng.standard_normal(N) * 0.1).astype(np.float32))
+    wq, ws = K.weight_quant(_bf16_gpu(w), qt)
+    xq, xs = K.act_quant(_bf16_gpu(x), qt)
+    y = K.gemm_w8a8(xq, xs, wq, ws, _bf16_gpu(b), qt)
+    rwq, rws = o_w8a8.quant_weight(w, qtype)
+    rxq, rxs = o_w8a8.quant_act(x, qtype)
+    ref = o_w8a8.gemm(rxq, rxs, rwq, rws, b, qtype)
+    assert _rel(_f32(y), ref) <= 1e-2
+
+
+def test_gemm_per_tensor_matches_reference_golden(golden):
+    """The reference's per-tensor WaveFp8Linear outputs, through our GEMM."""
+    K = _kernels()
+    from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_SCALE_TENSOR
+
+    g = golden("w8a8_per_tensor.npz")
+    for i in range(int(g["n"])):
+        x = bits_to_f32(g[f"c{i}_x"])
+        M, Kd = x.shape
+        if Kd % 16:
+            continue
+        wq = torch.from_numpy(g[f"c{i}_wq"]).to(DEV)
+        ws = torch.tensor([float(g[f"c{i}_ws"])], device=DEV, dtype=torch.float32)
+        xq, xs = o_w8a8.quant_act(x, "e4m3", per_token=False)
+        b = _bf16_gpu(bits_to_f32(g[f"c{i}_b"])) if f"c{i}_b" in g else None
+        y = K.gemm_w8a8(torch.from_numpy(xq).to(DEV), torch.tensor([float(xs)], device=DEV), wq, ws, b,
+                        WF_DTYPE_E4M3, WF_SCALE_TENSOR)
+        assert _rel(_f32(y), bits_to_f32(g[f"c{i}_y"])) <= 1e-2, i
+
+
+# ----------------------------------------------------------------------- RoPE
+def test_rope_matches_oracle(golden):
+    K = _kernels()
+    g = golden("rope.npz")
+    for i in range(int(g["n"])):
+        f, h, w, sf, n = [int(v) for v in g[f"c{i}_meta"]]
+        x = bits_to_f32(g[f"c{i}_x"])
+        cos, sin = o_rope.cos_sin_tables(f, h, w, sf)
+        y = K.rope_apply(_bf16_gpu(x), torch.from_numpy(cos).to(DEV), torch.from_numpy(sin).to(DEV))
+        ref = bits_to_f32(g[f"c{i}_y"])
+        ulp = np.abs(ref) * 2.0**-7 + 1e-30
+        assert np.all(np.abs(_f32(y) - ref) <= 2 * ulp + 1e-6), i
+
+
+# ------------------------------------------------------------- bounded waits
+def test_wait_flag_returns_when_set_and_times_out_when_not():
+    from waveforcing_b200 import _lib as L
+
+    lib = L.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    flag = torch.zeros(4, dtype=torch.int32, device=DEV)
+    tout = torch.zeros(2, dtype=torch.int32, device=DEV)
+    L.status_take()
+    # already satisfied (GEQ): returns immediately
+    flag[0] = 7
+    L.check(lib.wf_wait_flag(flag.data_ptr(), 7, 200_000_000, tout.data_ptr(), s), "wf_wait_flag")
+    torch.cuda.synchronize()
+    assert tout[0].item() == 0 and L.status_take() == 0
+    # never written: gives up after ~0.2 s, reports it, stream stays usable
+    L.check(lib.wf_wait_flag(flag[1:].data_ptr(), 1, 200_000_000, tout[1:].data_ptr(), s), "wf_wait_flag")
+    torch.cuda.synchronize()
+    assert tout[1].item() == 1
+    assert L.status_take() & (1 << 6)
+    assert (flag + 1).sum().item() == 7 + 4
+
+
+def test_stream_write_then_wait_value():
+    from waveforcing_b200 import _lib as L
+
+    lib = L.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    L.check(lib.wf_stream_write_u32(s, flag.data_ptr(), 5), "write")
+    L.check(lib.wf_stream_wait_u32(s, flag.data_ptr(), 5), "wait")
+    torch.cuda.synchronize()
+    assert flag.item() == 5
+
+
+def test_publish_payload_then_flag():
+    from waveforcing_b200 import _lib as L
+
+    lib = L.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    src = torch.arange(4096, dtype=torch.int32, device=DEV)
+    dsts = [torch.zeros_like(src) for _ in range(2)]
+    flags = torch.zeros(2, dtype=torch.int32, device=DEV)
+    L.check(lib.wf_publish(L.ptr_array([d.data_ptr() for d in dsts]), src.data_ptr(), src.numel() * 4,
+                           L.ptr_array([flags[i:].data_ptr() for i in range(2)]), 2, 9, s), "publish")
+    torch.cuda.synchronize()
+    assert all(torch.equal(d, src) for d in dsts) and flags.tolist() == [9, 9]
+
+
+def test_ipc_export_offset():
+    from waveforcing_b200 import _lib as L
+    import ctypes as C
+
+    base = torch.empty(1 << 20, dtype=torch.uint8, device=DEV)
+    view = base[4096:]
+    h = (C.c_uint8 * 64)()
+    off = C.c_uint64()
+    L.check(L.lib().wf_ipc_export(view.data_ptr(), h, C.byref(off)), "export")
+    h0 = (C.c_uint8 * 64)()
+    off0 = C.c_uint64()
+    L.check(L.lib().wf_ipc_export(base.data_ptr(), h0, C.byref(off0)), "export")
+    assert off.value - off0.value == 4096

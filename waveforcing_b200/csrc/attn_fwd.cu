@@ -1,0 +1,346 @@
+// tcgen05/TMEM flash attention forward (bf16, head_dim 128) for the chunk
+// self-attention of WaveRT's wavefront step (wave_rt/runtime/backend.py:141-148).
+//
+// One CTA computes a 128-query tile of one head against all Lk keys:
+//   warp 0       TMA producer: Q once, then K/V tiles (128 keys) into a
+//                3-stage ring, 128-byte swizzled, two 64-column boxes each
+//   warp 1       allocates 512 TMEM columns; lane 0 issues the MMAs:
+//                S_j = Q K_j^T   (kind::f16, A and B from shared memory)
+//                O  += P_j V_j   (kind::f16, A = P from TMEM, B = V MN-major)
+//   warps 4-7    softmax: thread t owns query row t (= TMEM lane t); reads
+//                S_j from TMEM, writes P_j (bf16) back to TMEM, rescales the
+//                O accumulator lazily (only when the running max grows by
+//                more than 2^8), and finally normalises O and stores it.
+// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+// S is double buffered so S_{j+1} is computed while row softmax of S_j runs.
+// Every wait is bounded (sm100.cuh mbar_wait); a timed-out wait raises the
+// status word and the CTA drains its in-flight work and exits.
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace wfk {
+namespace attn {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int HD = 128;
+constexpr int NS = 3;
+constexpr int TILE = BM * HD * 2;  // 32 KB bf16 tile
+constexpr int HALF = TILE / 2;     // one 64-column swizzle block (128 rows x 128 B)
+constexpr int NBARS = 1 + 3 * NS + 2 + 2 + 1 + 1;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + TILE * (1 + 2 * NS) + NBARS * 8 + 16;
+constexpr int THREADS = 256;
+
+constexpr uint32_t COL_S = 0, COL_O = 256, COL_P = 384;
+
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      status_raise(ST_DRAIN_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,
+                         long long o_head, long long o_batch, int Lq, int Lk, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + TILE;
+  uint8_t* sV = sK + NS * TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NS * TILE);
+  uint64_t* bar_q = bars;
+  uint64_t* full_k = bars + 1;
+  uint64_t* full_v = full_k + NS;
+  uint64_t* empty_kv = full_v + NS;
+  uint64_t* bar_s = empty_kv + NS;
+  uint64_t* bar_p = bar_s + 2;
+  uint64_t* bar_o = bar_p + 2;
+  uint64_t* bar_fin = bar_o + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_fin + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * BM;
+  const int h = blockIdx.y;
+  const int bz = blockIdx.z;
+  const int nk = (Lk + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full_k[s], 1);
+      mbar_init(&full_v[s], 1);
+      mbar_init(&empty_kv[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_s[i], 1);
+      mbar_init(&bar_p[i], 128);
+    }
+    mbar_init(bar_o, 1);
+    mbar_init(bar_fin, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(bar_q, TILE);
+      tma_load_4d(sQ, &tmQ, bar_q, 0, h, q0, bz);
+      tma_load_4d(sQ + HALF, &tmQ, bar_q, 64, h, q0, bz);
+      int issued = 0;
+      for (int j = 0; j < nk; ++j) {
+        const int s = j % NS;
+        if (j >= NS && !mbar_wait(&empty_kv[s], ((j / NS) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) break;
+        mbar_arrive_expect_tx(&full_k[s], TILE);
+        tma_load_4d(sK + s * TILE, &tmK, &full_k[s], 0, h, j * BN, bz);
+        tma_load_4d(sK + s * TILE + HALF, &tmK, &full_k[s], 64, h, j * BN, bz);
+        mbar_arrive_expect_tx(&full_v[s], TILE);
+        tma_load_4d(sV + s * TILE, &tmV, &full_v[s], 0, h, j * BN, bz);
+        tma_load_4d(sV + s * TILE + HALF, &tmV, &full_v[s], 64, h, j * BN, bz);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // Let the copies this thread issued land before the CTA exits.
+        mbar_wait_drain(bar_q, 0, 200000000ull);
+        for (int j = (issued > NS ? issued - NS : 0); j < issued; ++j) {
+          mbar_wait_drain(&full_k[j % NS], (j / NS) & 1, 200000000ull);
+          mbar_wait_drain(&full_v[j % NS], (j / NS) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ----------------------------------------------------------------- MMA
+      constexpr uint32_t idesc_qk = make_idesc(1, FMT_BF16, FMT_BF16, 0, BM, BN);
+      constexpr uint32_t idesc_pv = make_idesc(1, FMT_BF16, FMT_BF16, 1, BM, HD);
+      const uint32_t aQ = smem_u32(sQ);
+      bool ok = mbar_wait(bar_q, 0, abort_flag, ST_ATTN_MMA);
+      for (int j = 0; ok && j <= nk; ++j) {
+        if (j < nk) {
+          const int s = j % NS;
+          if (!mbar_wait(&full_k[s], (j / NS) & 1, abort_flag, ST_ATTN_MMA)) break;
+          tc_fence_after();
+          const uint32_t dS = tbase + COL_S + (j & 1) * BN;
+          const uint32_t aK = smem_u32(sK + s * TILE);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+            umma_f16_ss(dS, desc_sw128(aQ + off, 16, 1024), desc_sw128(aK + off, 16, 1024), idesc_qk, kk > 0);
+          }
+          umma_commit(&bar_s[j & 1]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          const int s = jj % NS;
+          if (!mbar_wait(&bar_p[jj & 1], (jj >> 1) & 1, abort_flag, ST_ATTN_MMA)) break;
+          if (!mbar_wait(&full_v[s], (jj / NS) & 1, abort_flag, ST_ATTN_MMA)) break;
+          tc_fence_after();
+          const uint32_t aV = smem_u32(sV + s * TILE);
+          const uint32_t tP = tbase + COL_P + (jj & 1) * (BN / 2);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            umma_f16_ts(tbase + COL_O, tP + kk * 8, desc_sw128(aV + kk * 2048, HALF, 1024), idesc_pv,
+                        (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_kv[s]);
+          umma_commit(bar_o);
+        }
+      }
+      // Nothing of ours may still be running when TMEM is released.
+      umma_commit(bar_fin);
+      mbar_wait_drain(bar_fin, 0, 200000000ull);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int wq = warp - 4;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      const int bsel = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_s[bsel], (j >> 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+      if (!ok) break;
+      tc_fence_after();
+      float s[BN];
+      {
+        uint32_t r[64];
+        tmem_ld32x32b_x64(tbase + lane_off + COL_S + bsel * BN, r);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
+        tmem_ld32x32b_x64(tbase + lane_off + COL_S + bsel * BN + 64, r);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(r[i]);
+      }
+      const int kvalid = Lk - j * BN;
+      if (kvalid < BN) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i)
+          if (i >= kvalid) s[i] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < BN; ++i) mx = fmaxf(mx, s[i]);
+      const float mx2 = mx * scale_log2;
+      float m_new = m_run;
+      bool grow = false;
+      if (j == 0) {
+        m_new = mx2;
+      } else if (mx2 > m_run + 8.f) {
+        m_new = mx2;
+        grow = true;
+      }
+      const float neg_m = -m_new;
+      float sum = 0.f;
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int i = 0; i < BN / 2; ++i) {
+        const float p0 = ex2_approx(fmaf(s[2 * i], scale_log2, neg_m));
+        const float p1 = ex2_approx(fmaf(s[2 * i + 1], scale_log2, neg_m));
+        sum += p0 + p1;
+        pk[i] = pack_bf16x2(p0, p1);
+      }
+      const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
+      if (__any_sync(0xffffffffu, grow)) {
+        // O may only be touched once PV_{j-1} has completed.
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (j - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t r[32];
+          tmem_ld32x32b_x32(tbase + lane_off + COL_O + c, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32x32b_x32(tbase + lane_off + COL_O + c, r);
+        }
+      }
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      tmem_st32x32b_x64(tbase + lane_off + COL_P + bsel * (BN / 2), pk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bar_p[bsel]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (nk - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.f / l_run;
+      const int qrow = q0 + row;
+      __nv_bfloat16* dst = out + (long long)bz * o_batch + (long long)qrow * o_tok + (long long)h * o_head;
+#pragma unroll
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t r[32];
+        tmem_ld32x32b_x32(tbase + lane_off + COL_O + c, r);
+        if (qrow < Lq) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+            w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+            w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+            w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+            d4[v] = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// Tensor map over a [batch, L, H, 128] bf16 tensor with {batch, token, head}
+// element strides; box = 64 head-dim columns x 1 head x 128 tokens.
+static int make_qkv_map(CUtensorMap* m, const void* p, int batch, int L, int H, const int64_t* st) {
+  const uint64_t gdim[4] = {(uint64_t)HD, (uint64_t)H, (uint64_t)L, (uint64_t)batch};
+  const uint64_t gstr[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2,
+                            (uint64_t)(batch > 1 ? st[0] : st[1] * (int64_t)L) * 2};
+  const uint32_t box[4] = {64, 1, (uint32_t)BM, 1};
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, p, gdim, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+static bool strides_ok(const int64_t* st, int batch) {
+  if (st == nullptr) return false;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] < 0 || (st[i] % 8) != 0) return false;
+  if (batch > 1 && st[0] == 0) return false;
+  return st[1] > 0 && st[2] > 0;
+}
+
+}  // namespace attn
+}  // namespace wfk
+
+extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o, int batch, int Lq, int Lk, int H,
+                           int D, const int64_t* q_stride, const int64_t* k_stride, const int64_t* v_stride,
+                           const int64_t* o_stride, int kv_dtype, const float* k_scale, const float* v_scale,
+                           int scale_mode, float softmax_scale, void* stream) {
+  using namespace wfk;
+  using namespace wfk::attn;
+  if (D != HD) return fail(WF_ERR_UNSUPPORTED, "wf_attn_fwd: head_dim %d unsupported (only 128)", D);
+  if (kv_dtype != WF_DTYPE_BF16 || k_scale != nullptr || v_scale != nullptr || scale_mode != WF_SCALE_NONE)
+    return fail(WF_ERR_UNSUPPORTED, "wf_attn_fwd: K/V must be bf16 (dequantise FP8 pages with wf_kv_dequant)");
+  if (batch < 1 || Lq < 1 || Lk < 1 || H < 1 || H > 65535 || batch > 65535)
+    return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: bad sizes batch=%d Lq=%d Lk=%d H=%d", batch, Lq, Lk, H);
+  if (!q || !k || !v || !o) return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: tensors must be 16-byte aligned");
+  if (!strides_ok(q_stride, batch) || !strides_ok(k_stride, batch) || !strides_ok(v_stride, batch) ||
+      !strides_ok(o_stride, batch))
+    return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: strides must be positive multiples of 8 elements");
+  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+    return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: softmax_scale must be positive");
+
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = make_qkv_map(&tq, q, batch, Lq, H, q_stride)) != WF_OK) return rc;
+  if ((rc = make_qkv_map(&tk, k, batch, Lk, H, k_stride)) != WF_OK) return rc;
+  if ((rc = make_qkv_map(&tv, v, batch, Lk, H, v_stride)) != WF_OK) return rc;
+
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  WFK_CUDA_TRY(cudaGetDevice(&dev));
+  if (configured_dev != dev) {
+    WFK_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    configured_dev = dev;
+  }
+  const dim3 grid((Lq + BM - 1) / BM, H, batch);
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  attn_fwd_bf16_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+      tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
+      (long long)o_stride[0], Lq, Lk, scale_log2);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" unsigned int wfk_status_take_attn(void) { return wfk::status_take_local(); }

@@ -1,0 +1,336 @@
+// W8A8 linear on tcgen05: y = (xq . wq^T) * x_scale[m] * w_scale[n] + bias[n]
+// replacing torch._scaled_mm in WaveFp8Linear (wave_rt/runtime/fp8.py:49-56).
+//
+//   xq [M, K] and wq [N, K] are 8-bit, K-contiguous; e4m3 uses
+//   tcgen05.mma kind::f8f6f4 (f32 accumulate), s8 uses kind::i8 (s32).
+//   CTA tile 128 x 256, K step 128 bytes (one 128-byte swizzle row), 4-stage
+//   TMA ring.  warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+//   warps 4-7 = epilogue (thread t owns accumulator row t = TMEM lane t):
+//   scale, bias, bf16 convert and store straight from registers.
+// Also here: load-time per-channel weight quantisation and per-token dynamic
+// activation quantisation (the per-row forms of fp8.py:32-36 and :47-48).
+#include <cuda_runtime.h>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace wfk {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes (= elements for 8-bit types)
+constexpr int NS = 4;
+constexpr int A_TILE = BM * BK;  // 16 KB
+constexpr int B_TILE = BN * BK;  // 32 KB
+constexpr int NBARS = 2 * NS + 2;
+constexpr int SMEM_BYTES = 1024 + NS * (A_TILE + B_TILE) + NBARS * 8 + 16;
+constexpr int THREADS = 256;
+
+__device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      status_raise(ST_DRAIN_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+template <bool IS_INT8>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const float* __restrict__ x_scale, const float* __restrict__ w_scale,
+                     const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y, int M, int N, int K,
+                     long long y_stride, int per_token) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + NS * A_TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + NS * B_TILE);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + NS;
+  uint64_t* done = empty + NS;
+  uint64_t* fin = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    mbar_init(fin, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int issued = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % NS;
+        if (kb >= NS && !mbar_wait(&empty[s], ((kb / NS) - 1) & 1, abort_flag, ST_GEMM_PRODUCER)) break;
+        mbar_arrive_expect_tx(&full[s], A_TILE + B_TILE);
+        tma_load_2d(sA + s * A_TILE, &tmA, &full[s], kb * BK, m0);
+        tma_load_2d(sB + s * B_TILE, &tmB, &full[s], kb * BK, n0);
+        issued = kb + 1;
+      }
+      if (*abort_flag)
+        for (int kb = (issued > NS ? issued - NS : 0); kb < issued; ++kb)
+          wait_drain(&full[kb % NS], (kb / NS) & 1, 200000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = IS_INT8 ? make_idesc(2, FMT_S8, FMT_S8, 0, BM, BN)
+                                         : make_idesc(1, FMT_E4M3, FMT_E4M3, 0, BM, BN);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % NS;
+        if (!mbar_wait(&full[s], (kb / NS) & 1, abort_flag, ST_GEMM_MMA)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(sA + s * A_TILE), b = smem_u32(sB + s * B_TILE);
+#pragma unroll
+        for (int kk = 0; kk < BK / 32; ++kk) {
+          const uint64_t da = desc_sw128(a + kk * 32, 16, 1024), db = desc_sw128(b + kk * 32, 16, 1024);
+          if constexpr (IS_INT8)
+            umma_i8_ss(tbase, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          else
+            umma_f8_ss(tbase, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(done);
+      umma_commit(fin);
+      wait_drain(fin, 0, 200000000ull);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    const int wq = warp - 4;
+    const int row = m0 + wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag, ST_GEMM_EPILOGUE, 20000000000ull));
+    if (ok) {
+      tc_fence_after();
+      const float sx = (row < M) ? (per_token ? __ldg(x_scale + row) : __ldg(x_scale)) : 0.f;
+      const float sw_t = per_token ? 0.f : __ldg(w_scale);
+      __nv_bfloat16* yrow = y + static_cast<long long>(row) * y_stride;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32x32b_x32(tbase + lane_off + c, r);
+        const int n = n0 + c;
+        if (row < M && n < N) {
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float acc = IS_INT8 ? static_cast<float>(static_cast<int>(r[i])) : __uint_as_float(r[i]);
+            const int ni = n + i < N ? n + i : N - 1;
+            const float sw = per_token ? __ldg(w_scale + ni) : sw_t;
+            const float b = bias ? __bfloat162float(bias[ni]) : 0.f;
+            f[i] = fmaf(acc * sx, sw, b);
+          }
+          if (n + 32 <= N) {
+            uint4* d4 = reinterpret_cast<uint4*>(yrow + n);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              d4[v] = make_uint4(pack_bf16x2(f[8 * v], f[8 * v + 1]), pack_bf16x2(f[8 * v + 2], f[8 * v + 3]),
+                                 pack_bf16x2(f[8 * v + 4], f[8 * v + 5]), pack_bf16x2(f[8 * v + 6], f[8 * v + 7]));
+          } else {
+            for (int i = 0; i < 32 && n + i < N; ++i) yrow[n + i] = __float2bfloat16_rn(f[i]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, BN);
+  }
+}
+
+// ----------------------------------------------------------- quantisers
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float warp_max(float m) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  return m;
+}
+
+// Per-output-channel weight quantisation, f32 math (fp8.py:32-36 per row).
+__global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, uint8_t* __restrict__ wq,
+                                    float* __restrict__ w_scale, int64_t N, int64_t K, int is_int8) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (n >= N) return;
+  const __nv_bfloat16* row = w + n * K;
+  float m = 0.f;
+  for (int64_t k = lane; k < K; k += 32) m = fmaxf(m, fabsf(__bfloat162float(row[k])));
+  m = warp_max(m);
+  const float qmax = is_int8 ? 127.f : 448.f;
+  float s = __fdiv_rn(m, qmax);
+  s = s < 1e-8f ? 1e-8f : s;
+  for (int64_t k = lane; k < K; k += 32) {
+    const float r = __fdiv_rn(__bfloat162float(row[k]), s);
+    uint8_t c;
+    if (is_int8) {
+      const float t = fminf(fmaxf(rintf(r), -127.f), 127.f);
+      c = static_cast<uint8_t>(static_cast<int8_t>(t));
+    } else {
+      uint16_t p;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(p) : "f"(0.f), "f"(fabsf(r)));
+      c = static_cast<uint8_t>((p & 0x7F) | ((__float_as_uint(r) >> 24) & 0x80u));
+    }
+    wq[n * K + k] = c;
+  }
+  if (lane == 0) w_scale[n] = s;
+}
+
+// Per-token activation quantisation with bf16 scale math (fp8.py:47-48 per row).
+__global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ xq,
+                                 float* __restrict__ x_scale, int64_t M, int64_t K, int64_t xs, int is_int8) {
+  const int lane = threadIdx.x & 31;
+  const int64_t m = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (m >= M) return;
+  const __nv_bfloat16* row = x + m * xs;
+  const uint4* r4 = reinterpret_cast<const uint4*>(row);
+  const int64_t nch = K / 8;
+  float amax = 0.f;
+  for (int64_t c = lane; c < nch; c += 32) {
+    const uint4 v = __ldg(r4 + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(w[i] << 16)), fabsf(__uint_as_float(w[i] & 0xFFFF0000u))));
+  }
+  amax = warp_max(amax);
+  const float qmax = is_int8 ? 127.f : 448.f;
+  float s = bf16r(__fdiv_rn(amax, qmax));
+  const float smin = bf16r(1e-8f);
+  s = s < smin ? smin : s;
+  for (int64_t c = lane; c < nch; c += 32) {
+    const uint4 v = __ldg(r4 + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t out[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float q0 = bf16r(__fdiv_rn(__uint_as_float(w[i] << 16), s));
+      const float q1 = bf16r(__fdiv_rn(__uint_as_float(w[i] & 0xFFFF0000u), s));
+      uint32_t pair;
+      if (is_int8) {
+        const int a = static_cast<int>(fminf(fmaxf(rintf(q0), -127.f), 127.f));
+        const int b = static_cast<int>(fminf(fmaxf(rintf(q1), -127.f), 127.f));
+        pair = (static_cast<uint32_t>(a) & 0xFF) | ((static_cast<uint32_t>(b) & 0xFF) << 8);
+      } else {
+        uint16_t p;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(p) : "f"(fabsf(q1)), "f"(fabsf(q0)));
+        pair = p | ((__float_as_uint(q0) >> 24) & 0x80u) | ((__float_as_uint(q1) >> 16) & 0x8000u);
+      }
+      out[i >> 1] |= pair << ((i & 1) * 16);
+    }
+    reinterpret_cast<uint2*>(xq + m * K)[c] = make_uint2(out[0], out[1]);
+  }
+  if (lane == 0) x_scale[m] = s;
+}
+
+static int make_map_2d(CUtensorMap* map, const void* p, int rows, int cols, int box_rows) {
+  const uint64_t gdim[2] = {(uint64_t)cols, (uint64_t)rows};
+  const uint64_t gstr[1] = {(uint64_t)cols};
+  const uint32_t box[2] = {(uint32_t)BK, (uint32_t)box_rows};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p, gdim, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace gemm
+}  // namespace wfk
+
+using namespace wfk;
+using namespace wfk::gemm;
+
+extern "C" int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq, const float* w_scale,
+                            const void* bias, void* y, int M, int N, int K, int64_t y_row_stride, int qtype,
+                            int scale_mode, void* stream) {
+  if (qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8)
+    return fail(WF_ERR_UNSUPPORTED, "wf_gemm_w8a8: qtype must be WF_DTYPE_E4M3 or WF_DTYPE_S8");
+  if (scale_mode != WF_SCALE_TENSOR && scale_mode != WF_SCALE_TOKEN)
+    return fail(WF_ERR_INVALID_ARG, "wf_gemm_w8a8: scale_mode must be WF_SCALE_TENSOR or WF_SCALE_TOKEN");
+  if (M < 1 || N < 16 || K < 16 || N % 16 || K % 16 || M > (1 << 30))
+    return fail(WF_ERR_INVALID_ARG, "wf_gemm_w8a8: need M>=1, N and K multiples of 16 (M=%d N=%d K=%d)", M, N, K);
+  if (!xq || !wq || !y || !x_scale || !w_scale || !aligned16(xq) || !aligned16(wq) || !aligned16(y) ||
+      y_row_stride < N || y_row_stride % 8)
+    return fail(WF_ERR_INVALID_ARG, "wf_gemm_w8a8: null/misaligned pointer or bad y stride");
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_map_2d(&ta, xq, M, K, BM)) != WF_OK) return rc;
+  if ((rc = make_map_2d(&tb, wq, N, K, BN)) != WF_OK) return rc;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  WFK_CUDA_TRY(cudaGetDevice(&dev));
+  if (configured_dev != dev) {
+    WFK_CUDA_TRY(cudaFuncSetAttribute(gemm_w8a8_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      SMEM_BYTES));
+    WFK_CUDA_TRY(cudaFuncSetAttribute(gemm_w8a8_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      SMEM_BYTES));
+    configured_dev = dev;
+  }
+  const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int per_token = scale_mode == WF_SCALE_TOKEN;
+  if (qtype == WF_DTYPE_S8)
+    gemm_w8a8_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, x_scale, w_scale,
+                                                             static_cast<const __nv_bfloat16*>(bias),
+                                                             static_cast<__nv_bfloat16*>(y), M, N, K,
+                                                             (long long)y_row_stride, per_token);
+  else
+    gemm_w8a8_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, x_scale, w_scale,
+                                                              static_cast<const __nv_bfloat16*>(bias),
+                                                              static_cast<__nv_bfloat16*>(y), M, N, K,
+                                                              (long long)y_row_stride, per_token);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_weight_quant(const void* w, void* wq, float* w_scale, int64_t N, int64_t K, int qtype,
+                               void* stream) {
+  if (!w || !wq || !w_scale || N < 1 || K < 1) return fail(WF_ERR_INVALID_ARG, "wf_weight_quant: bad arguments");
+  if (qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8) return fail(WF_ERR_UNSUPPORTED, "wf_weight_quant: qtype");
+  const unsigned blocks = static_cast<unsigned>((N + 7) / 8);
+  weight_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(w), static_cast<uint8_t*>(wq), w_scale, N, K, qtype == WF_DTYPE_S8);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, int64_t K, int64_t x_row_stride,
+                            int qtype, void* stream) {
+  if (!x || !xq || !x_scale || M < 0 || K < 8 || K % 8 || x_row_stride < K || x_row_stride % 8 || !aligned16(x) ||
+      (reinterpret_cast<uintptr_t>(xq) & 7))
+    return fail(WF_ERR_INVALID_ARG, "wf_act_quant: bad arguments");
+  if (qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8) return fail(WF_ERR_UNSUPPORTED, "wf_act_quant: qtype");
+  if (M == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((M + 7) / 8);
+  act_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<uint8_t*>(xq), x_scale, M, K, x_row_stride,
+      qtype == WF_DTYPE_S8);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" unsigned int wfk_status_take_gemm(void) { return wfk::status_take_local(); }

@@ -1,0 +1,377 @@
+// FP8 e4m3 K/V codec (HBM-bound), bit-exact to the reference's dtype sequence
+// (wave_rt/denoiser/exchange/common.py:143-164):
+//     s    = f32(clamp(bf16(amax|x| / 448), 1e-8))
+//     code = e4m3fn(bf16(x / s))          RNE, |v| > 464 -> NaN
+//     deq  = e4m3(code) * s
+// Layout: x is [rows, cols] bf16 with a row stride; codes are dense [rows, cols]
+// u8; per-token scales [rows] f32 (or one f32 for the per-tensor mode).
+//
+// Exactness notes.
+//  * x / s must be the correctly rounded f32 quotient before the bf16 rounding.
+//    With r = RN(1/s) (IEEE reciprocal, __frcp_rn) and q0 = RN(x r), one
+//    correction q = RN(q0 + RN(x - q0 s) r) is correctly rounded (Markstein's
+//    theorem); rows whose scale is not finite take the plain IEEE division.
+//  * The hardware e4m3 conversion saturates, torch's does not.  For a finite
+//    row amax the bf16 quotient is at most 450 in magnitude (s is amax/448
+//    rounded to bf16, so |x|/s <= 448.9 before rounding), where saturating and
+//    non-saturating RNE agree; non-finite rows use the exact software encoder.
+#include <cuda_runtime.h>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace wfk {
+namespace codec {
+
+constexpr int WARPS = 8;
+
+__device__ __forceinline__ float bf16_round_f(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float scale_from_amax(float amax) {
+  // bf16(amax / 448) with IEEE division, clamped below by bf16(1e-8).
+  const float s = bf16_round_f(__fdiv_rn(amax, 448.f));
+  const float smin = bf16_round_f(1e-8f);
+  return (s >= smin || s != s) ? s : smin;  // NaN propagates like torch.clamp
+}
+
+// Exact software e4m3fn encoder for a bf16-valued float (torch semantics).
+__device__ __forceinline__ uint32_t e4m3_encode_sw(float f) {
+  const uint32_t bits = __float_as_uint(f);
+  const uint32_t sign = (bits >> 24) & 0x80u;
+  const float a = fabsf(f);
+  if (!(a <= 464.f)) return 0x7Fu | sign;  // NaN, inf, or rounds past 448
+  if (a < 0.015625f) {                     // below 2^-6: subnormal grid 2^-9
+    return static_cast<uint32_t>(rintf(a * 512.f)) | sign;
+  }
+  const uint32_t ab = __float_as_uint(a);
+  int e = static_cast<int>((ab >> 23) & 0xFF) - 127;
+  uint32_t q = (ab >> 20) & 7u;
+  const uint32_t rem = ab & 0xFFFFFu;
+  if (rem > 0x80000u || (rem == 0x80000u && (q & 1u))) ++q;
+  if (q == 8u) {
+    q = 0;
+    ++e;
+  }
+  return ((static_cast<uint32_t>(e + 7) << 3) | q) | sign;
+}
+
+// Two bf16-valued floats -> two e4m3 codes (lo in bits 0-7).
+__device__ __forceinline__ uint32_t e4m3x2_hw(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+struct RowQuant {
+  float s;      // scale (as stored)
+  float r;      // RN(1/s)
+  bool finite;  // fast path valid
+};
+
+__device__ __forceinline__ RowQuant make_rowq(float amax) {
+  RowQuant q;
+  q.s = scale_from_amax(amax);
+  q.finite = isfinite(q.s);
+  q.r = __frcp_rn(q.s);
+  return q;
+}
+
+__device__ __forceinline__ float div_exact(float x, const RowQuant& q) {
+  if (!q.finite) return __fdiv_rn(x, q.s);
+  const float q0 = x * q.r;
+  const float e = fmaf(-q0, q.s, x);
+  return fmaf(e, q.r, q0);
+}
+
+// 8 bf16 (uint4) -> 8 codes (uint2)
+__device__ __forceinline__ uint2 quant8(const uint4& v, const RowQuant& q) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t out[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float x0 = __uint_as_float(w[i] << 16);
+    const float x1 = __uint_as_float(w[i] & 0xFFFF0000u);
+    const float b0 = bf16_round_f(div_exact(x0, q));
+    const float b1 = bf16_round_f(div_exact(x1, q));
+    uint32_t c;
+    if (q.finite) {
+      // magnitudes through the hardware convert, signs copied explicitly so
+      // values that round to zero keep torch's signed zero (0x80)
+      c = e4m3x2_hw(fabsf(b0), fabsf(b1)) | ((__float_as_uint(b0) >> 24) & 0x80u) |
+          ((__float_as_uint(b1) >> 16) & 0x8000u);
+    } else {
+      c = e4m3_encode_sw(b0) | (e4m3_encode_sw(b1) << 8);
+    }
+    out[i >> 1] |= c << ((i & 1) * 16);
+  }
+  return make_uint2(out[0], out[1]);
+}
+
+__device__ __forceinline__ float amax8(const uint4& v, float m) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float x0 = fabsf(__uint_as_float(w[i] << 16));
+    const float x1 = fabsf(__uint_as_float(w[i] & 0xFFFF0000u));
+    // NaN-propagating max (torch.amax propagates NaN)
+    m = (x0 > m || x0 != x0) ? x0 : m;
+    m = (x1 > m || x1 != x1) ? x1 : m;
+  }
+  return m;
+}
+
+__device__ __forceinline__ float warp_max_nan(float m) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, m, o);
+    m = (t > m || t != t) ? t : m;
+  }
+  return m;
+}
+
+// One warp per row; NCH 16-byte chunks per lane kept in registers (cols ==
+// NCH * 256), or NCH == 0 for any cols % 8 == 0 (two passes over the row).
+template <int NCH>
+__device__ __forceinline__ void quant_row(const __nv_bfloat16* __restrict__ xrow, int64_t cols, int lane,
+                                          uint8_t* const* dst_codes, float* const* dst_scales, int n_dst,
+                                          int64_t row) {
+  const uint4* x4 = reinterpret_cast<const uint4*>(xrow);
+  const int64_t nch = cols / 8;
+  float m = 0.f;
+  uint4 buf[NCH > 0 ? NCH : 1];
+  if constexpr (NCH > 0) {
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      buf[i] = __ldcs(x4 + lane + 32 * i);
+      m = amax8(buf[i], m);
+    }
+  } else {
+    for (int64_t c = lane; c < nch; c += 32) m = amax8(__ldg(x4 + c), m);
+  }
+  m = warp_max_nan(m);
+  const RowQuant q = make_rowq(m);
+  if constexpr (NCH > 0) {
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const uint2 c = quant8(buf[i], q);
+      for (int d = 0; d < n_dst; ++d) reinterpret_cast<uint2*>(dst_codes[d] + row * cols)[lane + 32 * i] = c;
+    }
+  } else {
+    for (int64_t c = lane; c < nch; c += 32) {
+      const uint2 cc = quant8(__ldg(x4 + c), q);
+      for (int d = 0; d < n_dst; ++d) reinterpret_cast<uint2*>(dst_codes[d] + row * cols)[c] = cc;
+    }
+  }
+  if (lane == 0)
+    for (int d = 0; d < n_dst; ++d) dst_scales[d][row] = q.s;
+}
+
+constexpr int MAX_DST = 8;
+struct DstList {
+  uint8_t* codes[MAX_DST];
+  float* scales[MAX_DST];
+};
+
+template <int NCH>
+__global__ void __launch_bounds__(WARPS * 32)
+    quant_token_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, int64_t row_stride,
+                       DstList dst, int n_dst) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  quant_row<NCH>(x + row * row_stride, cols, lane, dst.codes, dst.scales, n_dst, row);
+}
+
+// K and V of one layer in one launch: rows [0, rows) from k, [rows, 2 rows) from v.
+template <int NCH>
+__global__ void __launch_bounds__(WARPS * 32)
+    quant_publish_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, int64_t rows,
+                         int64_t cols, int64_t k_stride, int64_t v_stride, DstList dk, DstList dv, int n_dst) {
+  const int lane = threadIdx.x & 31;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5);
+  if (row >= 2 * rows) return;
+  if (row < rows) {
+    quant_row<NCH>(k + row * k_stride, cols, lane, dk.codes, dk.scales, n_dst, row);
+  } else {
+    row -= rows;
+    quant_row<NCH>(v + row * v_stride, cols, lane, dv.codes, dv.scales, n_dst, row);
+  }
+}
+
+// ------------------------------------------------------------ per-tensor
+__global__ void amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, int64_t row_stride,
+                            unsigned int* __restrict__ amax_bits) {
+  const int64_t nch = cols / 8;
+  const int64_t total = rows * nch;
+  float m = 0.f;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / nch, c = i - r * nch;
+    m = amax8(__ldg(reinterpret_cast<const uint4*>(x + r * row_stride) + c), m);
+  }
+  m = warp_max_nan(m);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    m = warp_max_nan(m);
+    // non-negative floats (and +NaN, which sorts above +inf) order like their bits
+    if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m) & 0x7FFFFFFFu);
+  }
+}
+
+__global__ void quant_tensor_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols,
+                                    int64_t row_stride, const unsigned int* __restrict__ amax_bits,
+                                    uint8_t* __restrict__ codes, float* __restrict__ scale_out) {
+  const RowQuant q = make_rowq(__uint_as_float(*amax_bits));
+  const int64_t nch = cols / 8;
+  const int64_t total = rows * nch;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / nch, c = i - r * nch;
+    const uint2 cc = quant8(__ldg(reinterpret_cast<const uint4*>(x + r * row_stride) + c), q);
+    reinterpret_cast<uint2*>(codes + r * cols)[c] = cc;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = q.s;
+}
+
+// ------------------------------------------------------------- dequant
+__global__ void dequant_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ scales,
+                               __nv_bfloat16* __restrict__ out, int64_t rows, int64_t cols, int64_t out_stride,
+                               int mode) {
+  const int64_t nch = cols / 8;
+  const int64_t total = rows * nch;
+  const float s_tensor = (mode == WF_SCALE_TENSOR) ? scales[0] : 1.f;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / nch, c = i - r * nch;
+    const float s = (mode == WF_SCALE_TOKEN) ? __ldg(scales + r) : s_tensor;
+    const uint2 cc = __ldcs(reinterpret_cast<const uint2*>(codes + r * cols) + c);
+    const uint32_t w[2] = {cc.x, cc.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint32_t lo2, hi2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo2) : "h"(static_cast<uint16_t>(w[j] & 0xFFFF)));
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi2) : "h"(static_cast<uint16_t>(w[j] >> 16)));
+      const float f0 = __half2float(__ushort_as_half(static_cast<unsigned short>(lo2 & 0xFFFF))) * s;
+      const float f1 = __half2float(__ushort_as_half(static_cast<unsigned short>(lo2 >> 16))) * s;
+      const float f2 = __half2float(__ushort_as_half(static_cast<unsigned short>(hi2 & 0xFFFF))) * s;
+      const float f3 = __half2float(__ushort_as_half(static_cast<unsigned short>(hi2 >> 16))) * s;
+      o[2 * j] = pack_bf16x2(f0, f1);
+      o[2 * j + 1] = pack_bf16x2(f2, f3);
+    }
+    reinterpret_cast<uint4*>(out + r * out_stride)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+static int grid_for(int64_t work_items, int threads) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t blocks = (work_items + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sms) * 16;
+  if (blocks > cap) blocks = cap;
+  return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+static bool rows_ok(const void* x, int64_t rows, int64_t cols, int64_t stride) {
+  return x && rows >= 0 && cols > 0 && cols % 8 == 0 && stride >= cols && stride % 8 == 0 && aligned16(x);
+}
+
+template <typename Launch>
+static void dispatch_nch(int64_t cols, Launch&& launch) {
+  if (cols == 1536)
+    launch(std::integral_constant<int, 6>());
+  else if (cols == 5120)
+    launch(std::integral_constant<int, 20>());
+  else if (cols == 3072)
+    launch(std::integral_constant<int, 12>());
+  else
+    launch(std::integral_constant<int, 0>());
+}
+
+}  // namespace codec
+}  // namespace wfk
+
+using namespace wfk;
+using namespace wfk::codec;
+
+extern "C" int wf_kv_quant(const void* x, uint8_t* codes, float* scales, int64_t rows, int64_t cols,
+                           int64_t x_row_stride, int mode, void* workspace, void* stream) {
+  if (!rows_ok(x, rows, cols, x_row_stride) || !codes || !scales || (reinterpret_cast<uintptr_t>(codes) & 7))
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_quant: bad arguments (cols %% 8, 16-byte x, 8-byte codes)");
+  if (rows == 0) return WF_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (mode == WF_SCALE_TOKEN) {
+    DstList d{};
+    d.codes[0] = codes;
+    d.scales[0] = scales;
+    const unsigned blocks = static_cast<unsigned>((rows + WARPS - 1) / WARPS);
+    dispatch_nch(cols, [&](auto nch) {
+      quant_token_kernel<decltype(nch)::value>
+          <<<blocks, WARPS * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride, d, 1);
+    });
+  } else if (mode == WF_SCALE_TENSOR) {
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 3))
+      return fail(WF_ERR_INVALID_ARG, "wf_kv_quant: per-tensor mode needs a 4-byte aligned workspace");
+    unsigned int* amax = static_cast<unsigned int*>(workspace);
+    WFK_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(unsigned int), s));
+    const int g = grid_for(rows * (cols / 8), 256);
+    amax_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride, amax);
+    quant_tensor_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride, amax,
+                                          codes, scales);
+  } else {
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_quant: mode must be WF_SCALE_TENSOR or WF_SCALE_TOKEN");
+  }
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_kv_dequant(const uint8_t* codes, const float* scales, void* out, int64_t rows, int64_t cols,
+                             int64_t out_row_stride, int mode, void* stream) {
+  if (!rows_ok(out, rows, cols, out_row_stride) || !codes || (reinterpret_cast<uintptr_t>(codes) & 7))
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_dequant: bad arguments");
+  if (mode != WF_SCALE_NONE && !scales) return fail(WF_ERR_INVALID_ARG, "wf_kv_dequant: scales required");
+  if (mode != WF_SCALE_NONE && mode != WF_SCALE_TENSOR && mode != WF_SCALE_TOKEN)
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_dequant: bad mode");
+  if (rows == 0) return WF_OK;
+  const int g = grid_for(rows * (cols / 8), 256);
+  dequant_kernel<<<g, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      codes, scales, static_cast<__nv_bfloat16*>(out), rows, cols, out_row_stride, mode);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_kv_quant_publish(const void* k, const void* v, int64_t rows, int64_t cols, int64_t k_row_stride,
+                                   int64_t v_row_stride, uint8_t* const* dst_codes_k, uint8_t* const* dst_codes_v,
+                                   float* const* dst_scales_k, float* const* dst_scales_v, int n_dst,
+                                   void* stream) {
+  if (!rows_ok(k, rows, cols, k_row_stride) || !rows_ok(v, rows, cols, v_row_stride))
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_quant_publish: bad K/V arguments");
+  if (n_dst < 1 || n_dst > MAX_DST || !dst_codes_k || !dst_codes_v || !dst_scales_k || !dst_scales_v)
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_quant_publish: 1..%d destinations required", MAX_DST);
+  DstList dk{}, dv{};
+  for (int i = 0; i < n_dst; ++i) {
+    if (!dst_codes_k[i] || !dst_codes_v[i] || !dst_scales_k[i] || !dst_scales_v[i] ||
+        (reinterpret_cast<uintptr_t>(dst_codes_k[i]) & 7) || (reinterpret_cast<uintptr_t>(dst_codes_v[i]) & 7))
+      return fail(WF_ERR_INVALID_ARG, "wf_kv_quant_publish: destination %d null or misaligned", i);
+    dk.codes[i] = dst_codes_k[i];
+    dk.scales[i] = dst_scales_k[i];
+    dv.codes[i] = dst_codes_v[i];
+    dv.scales[i] = dst_scales_v[i];
+  }
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((2 * rows + WARPS - 1) / WARPS);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dispatch_nch(cols, [&](auto nch) {
+    quant_publish_kernel<decltype(nch)::value><<<blocks, WARPS * 32, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), rows, cols, k_row_stride,
+        v_row_stride, dk, dv, n_dst);
+  });
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" unsigned int wfk_status_take_codec(void) { return wfk::status_take_local(); }

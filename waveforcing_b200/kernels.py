@@ -1,0 +1,169 @@
+"""torch-facing wrappers over the libwfk C ABI.
+
+Each wrapper validates dtype/device/layout, launches on the caller's current
+CUDA stream and raises on any error.  There is no CPU or library fallback:
+CPU tensors or a missing libwfk.so raise.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from waveforcing_b200 import _lib as L
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("waveforcing_b200 kernels need CUDA tensors (no CPU path exists)")
+
+
+def _strides_bthd(t: torch.Tensor):
+    """[B, L, H, D] or [L, H, D] -> (batch, L, H, D, {batch, token, head} strides)."""
+    if t.dim() == 3:
+        Lt, H, D = t.shape
+        return 1, Lt, H, D, (t.stride(0) * Lt, t.stride(0), t.stride(1))
+    if t.dim() == 4:
+        B, Lt, H, D = t.shape
+        return B, Lt, H, D, (t.stride(0), t.stride(1), t.stride(2))
+    raise ValueError(f"expected [B,L,H,D] or [L,H,D], got {tuple(t.shape)}")
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale) v on the tcgen05 kernel; NHD bf16, head_dim 128."""
+    _need_cuda(q, k, v)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise TypeError("attention: q, k, v must be bfloat16")
+    for t in (q, k, v):
+        if t.stride(-1) != 1:
+            raise ValueError("attention: last dim must be contiguous")
+    B, Lq, H, D, qs = _strides_bthd(q)
+    Bk, Lk, Hk, Dk, ks = _strides_bthd(k)
+    Bv, Lv, Hv, Dv, vs = _strides_bthd(v)
+    if (Bk, Hk, Dk) != (B, H, D) or (Bv, Lv, Hv, Dv) != (B, Lk, H, D):
+        raise ValueError(f"attention: shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    _, _, _, _, os_ = _strides_bthd(out)
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    L.check(
+        L.lib().wf_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, Lq, Lk, H, D,
+                            L.i64_array(qs), L.i64_array(ks), L.i64_array(vs), L.i64_array(os_),
+                            L.WF_DTYPE_BF16, None, None, L.WF_SCALE_NONE, scale, _stream()),
+        "wf_attn_fwd",
+    )
+    return out
+
+
+def _as_rows(x: torch.Tensor):
+    """View x as [rows, cols] with a row stride (last dim contiguous)."""
+    if x.dim() == 1:
+        return 1, x.shape[0], x.shape[0]
+    cols = x.shape[-1]
+    x2 = x.reshape(-1, cols) if not x.is_contiguous() else x.view(-1, cols)
+    return x2.shape[0], cols, x2.stride(0)
+
+
+def kv_quant(x: torch.Tensor, mode: int = L.WF_SCALE_TOKEN, codes: torch.Tensor | None = None,
+             scales: torch.Tensor | None = None, workspace: torch.Tensor | None = None):
+    """bf16 [rows, cols] -> (u8 codes [rows, cols], f32 scales [rows] or [1])."""
+    _need_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(-1) != 1:
+        raise ValueError("kv_quant: x must be a 2-D bf16 matrix with contiguous rows")
+    rows, cols = x.shape
+    if codes is None:
+        codes = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
+    if scales is None:
+        scales = torch.empty((rows if mode == L.WF_SCALE_TOKEN else 1,), dtype=torch.float32, device=x.device)
+    ws = 0
+    if mode == L.WF_SCALE_TENSOR:
+        if workspace is None:
+            workspace = torch.empty((1,), dtype=torch.int32, device=x.device)
+        ws = workspace.data_ptr()
+    L.check(L.lib().wf_kv_quant(x.data_ptr(), codes.data_ptr(), scales.data_ptr(), rows, cols, x.stride(0), mode,
+                                ws, _stream()), "wf_kv_quant")
+    return codes, scales
+
+
+def kv_dequant(codes: torch.Tensor, scales: torch.Tensor | None, mode: int = L.WF_SCALE_TOKEN,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(codes)
+    if codes.dtype != torch.uint8 or codes.dim() != 2 or not codes.is_contiguous():
+        raise ValueError("kv_dequant: codes must be a contiguous 2-D uint8 matrix")
+    rows, cols = codes.shape
+    if out is None:
+        out = torch.empty((rows, cols), dtype=torch.bfloat16, device=codes.device)
+    sp = scales.data_ptr() if scales is not None else 0
+    L.check(L.lib().wf_kv_dequant(codes.data_ptr(), sp, out.data_ptr(), rows, cols, out.stride(0), mode, _stream()),
+            "wf_kv_dequant")
+    return out
+
+
+def kv_quant_publish(k: torch.Tensor, v: torch.Tensor, dst_codes_k, dst_codes_v, dst_scales_k, dst_scales_v) -> None:
+    """Per-token quantise K and V [rows, cols] and write codes/scales to every
+    destination (device pointers as ints, local or peer)."""
+    _need_cuda(k, v)
+    rows, cols = k.shape
+    n = len(dst_codes_k)
+    L.check(L.lib().wf_kv_quant_publish(k.data_ptr(), v.data_ptr(), rows, cols, k.stride(0), v.stride(0),
+                                        L.ptr_array(dst_codes_k), L.ptr_array(dst_codes_v),
+                                        L.ptr_array(dst_scales_k), L.ptr_array(dst_scales_v), n, _stream()),
+            "wf_kv_quant_publish")
+
+
+def weight_quant(w: torch.Tensor, qtype: int = L.WF_DTYPE_E4M3):
+    """bf16 [N, K] -> (codes [N, K] uint8/int8 storage, f32 scales [N])."""
+    _need_cuda(w)
+    w = w.contiguous()
+    N, K = w.shape
+    wq = torch.empty((N, K), dtype=torch.uint8, device=w.device)
+    ws = torch.empty((N,), dtype=torch.float32, device=w.device)
+    L.check(L.lib().wf_weight_quant(w.data_ptr(), wq.data_ptr(), ws.data_ptr(), N, K, qtype, _stream()),
+            "wf_weight_quant")
+    return wq, ws
+
+
+def act_quant(x: torch.Tensor, qtype: int = L.WF_DTYPE_E4M3, xq: torch.Tensor | None = None,
+              xs: torch.Tensor | None = None):
+    _need_cuda(x)
+    M, K = x.shape
+    if xq is None:
+        xq = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    if xs is None:
+        xs = torch.empty((M,), dtype=torch.float32, device=x.device)
+    L.check(L.lib().wf_act_quant(x.data_ptr(), xq.data_ptr(), xs.data_ptr(), M, K, x.stride(0), qtype, _stream()),
+            "wf_act_quant")
+    return xq, xs
+
+
+def gemm_w8a8(xq, xs, wq, ws, bias=None, qtype: int = L.WF_DTYPE_E4M3, scale_mode: int = L.WF_SCALE_TOKEN,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(xq, wq)
+    M, K = xq.shape
+    N = wq.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
+    bp = bias.data_ptr() if bias is not None else 0
+    L.check(L.lib().wf_gemm_w8a8(xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(), bp, out.data_ptr(),
+                                 M, N, K, out.stride(0), qtype, scale_mode, _stream()), "wf_gemm_w8a8")
+    return out
+
+
+def rope_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor | None = None):
+    """Interleaved RoPE on bf16 [L, H, D] with f32 cos/sin [L, D/2]."""
+    _need_cuda(x, cos, sin)
+    if x.dim() == 4:
+        x = x[0]
+    Lt, H, D = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    L.check(L.lib().wf_rope_apply(x.data_ptr(), out.data_ptr(), cos.data_ptr(), sin.data_ptr(), Lt, H, D,
+                                  x.stride(0), out.stride(0), _stream()), "wf_rope_apply")
+    return out
