@@ -1,0 +1,369 @@
+"""Steady-state wavefront throughput of the WaveRT per-layer DiT hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {wf,reference}]
+                    [--preset 1.3b] [--kv fp8|bf16] [--w8a8 none|e4m3|int8]
+
+Workload (metric "steady FPS p50"): the 1.3B-shaped 5-step
+wavefront (steps 1000,800,600,400,200 + the clean-KV store stage) at 480x832
+(60x104 latents, 4680 tokens per 3-frame chunk), random-init bf16 weights,
+512-token N(0,1) text context, Gaussian noise from seed 0.  The rf_step+1
+stages are placed on the N ranks (merged when N < 6; ranks beyond 6 idle).
+One bench step = one steady-state tick (every stage active, anchor + 7 clean
+pages); each tick denoises one 3-latent-frame chunk = 12 output frames, so
+steady FPS = 12000 / p50(tick ms) over the timed ticks (the reference's
+definition, scripts/sweep_matrix.py:34-35,213-228, on the steady window).
+Ticks before the timed window fill the pipeline and are untimed.
+
+``value``  device-timed: noise resident in HBM, CUDA events on every rank,
+           per-tick max over ranks, p50.
+``e2e``    the same ticks driven from pinned HOST noise: each tick copies its
+           noise chunk host->device and reads the finished latent chunk back.
+``--impl reference``  the reference's torch CPU path (oracle port, all host
+           threads) on a bounded sample of one tick, extrapolated by FLOPs.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+FRAMES_PER_TICK = 12  # 3 latent frames -> 12 output frames per chunk
+METRIC = "steady FPS p50 (1.3B 5-step wavefront, 399 latent frames, 480x832)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="wf", choices=["wf", "reference"])
+    ap.add_argument("--preset", default="1.3b")
+    ap.add_argument("--kv", default="fp8", choices=["fp8", "bf16"])
+    ap.add_argument("--w8a8", default="none", choices=["none", "e4m3", "int8"])
+    ap.add_argument("--denoise-steps", default="1000,800,600,400,200")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------- util
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU side
+def cpu_reference_sample(preset: str, min_s: float = 10.0):
+    """Time the reference's torch CPU path on a bounded sample of one steady tick
+    and extrapolate by FLOPs.  Sample: stage 0's self-attention for one head
+    (q = one 4680-token chunk, K/V = its 8-chunk context), exactly the call of
+    naive_rt/rolling_forcing/wan/modules/attention.py:76-89, plus the
+    per-token FP8 K/V codec round trip of that head's slots and one FFN
+    linear on 512 rows.  Returns (fps, seconds, sample description, threads)."""
+    from oracle import attention as oattn
+    from waveforcing_b200.wavefront.dit import DiTConfig
+    from waveforcing_b200.wavefront.engine import stage_costs
+
+    cfg = DiTConfig.preset(preset)
+    T, D = cfg.tokens_per_chunk, cfg.head_dim
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, T, 1, D, generator=g) / math.sqrt(D)
+    k = torch.randn(1, 8 * T, 1, D, generator=g) / math.sqrt(D)
+    v = torch.randn(1, 8 * T, 1, D, generator=g) / math.sqrt(D)
+    x = torch.randn(512, cfg.dim, generator=g).to(torch.bfloat16)
+    w = (torch.randn(cfg.ffn, cfg.dim, generator=g) * 0.02).to(torch.bfloat16)
+    k0, v0 = k, v
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        # codec round trip on the received K/V rows of this head (torch CPU, the reference's ops)
+        kv = torch.cat([k0, v0], 1).to(torch.bfloat16)
+        s = (kv.abs().amax(dim=-1, keepdim=True) / 448.0).clamp(min=1e-8).float()
+        kvq = (kv / s).to(torch.float8_e4m3fn)
+        kv = (kvq.to(torch.bfloat16) * s).float()
+        k, v = kv[:, :8 * T], kv[:, 8 * T:]
+        oattn.sdpa_reference_torch(q, k, v)
+        torch.nn.functional.linear(x.float(), w.float())
+        reps += 1
+        if time.perf_counter() - t0 >= min_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    sample_flops = 4.0 * T * 8 * T * D + 2.0 * 512 * cfg.dim * cfg.ffn
+    # whole tick FLOPs: attention over every stage's context, all heads, all layers; all linears
+    ctx_chunks = [c - 2.9 for c in stage_costs(5)]
+    attn = sum(4.0 * T * c * T * cfg.dim for c in ctx_chunks) + 4.0 * T * 6 * cfg.text_len * cfg.dim
+    lin = 6 * 2.0 * T * (8 * cfg.dim * cfg.dim + 2 * cfg.dim * cfg.ffn)
+    tick_flops = cfg.layers * (attn + lin)
+    tick_s = dt * tick_flops / sample_flops
+    desc = (f"stage-0 self-attention of 1 head (q {T}, K/V {8 * T}) via F.scaled_dot_product_attention fp32 + "
+            f"per-token FP8 K/V round trip + one 512-row FFN linear; {dt:.2f}s per sample (mean of {reps}), x"
+            f"{tick_flops / sample_flops:.0f} by FLOPs to one steady tick")
+    return FRAMES_PER_TICK / tick_s, dt, desc, threads
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(max(0, args.warmup)):
+        cpu_reference_sample(args.preset, min_s=2.0)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps)):
+        fps, dt, desc, threads = cpu_reference_sample(args.preset)
+        vals.append(fps)
+    wall = time.perf_counter() - t0
+    fps = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": fps, "unit": "FPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * FRAMES_PER_TICK / fps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": f"{args.preset} 5-step wavefront steady tick, CPU torch path",
+                                        "sample_wall_s": wall / max(1, args.steps)},
+        "cpu_baseline": {"value": fps, "unit": "FPS", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": fps, "unit": "FPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU side
+def run_gpu_arm(args):
+    from waveforcing_b200 import kernels
+    from waveforcing_b200.runtime import backend
+    from waveforcing_b200.runtime.fp8 import quantize_transformer_w8a8
+    from waveforcing_b200.wavefront.dit import DiTConfig, WanDiT
+    from waveforcing_b200.wavefront.engine import EngineConfig, WavefrontEngine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=300))
+    torch.set_grad_enabled(False)
+    backend.select_backend("wf_b200")
+
+    steps_list = tuple(int(s) for s in args.denoise_steps.split(","))
+    S = len(steps_list)
+    fill = S + 8  # first tick with every stage active and anchor + 7 clean pages
+    n_ticks = fill + args.warmup + args.steps
+    cfg = DiTConfig.preset(args.preset)
+    # the 399-frame run; only its first n_ticks ticks are executed (fill, warm-up, timed steady window)
+    ecfg = EngineConfig(steps=steps_list, num_frames=399, fp8_kv=(args.kv == "fp8"))
+    if n_ticks > ecfg.num_blocks:
+        raise SystemExit(f"--steps/--warmup too large: {n_ticks} ticks > {ecfg.num_blocks} chunks")
+    model = WanDiT.random(cfg, dev, seed=0)
+    if args.w8a8 != "none":
+        quantize_transformer_w8a8(model, scope="all", qtype=args.w8a8, granularity="channel")
+    g = torch.Generator(device="cpu").manual_seed(0)
+    text = torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(dev)
+    model.set_text(text)
+
+    def make_engine(noise):
+        return WavefrontEngine(model, ecfg, rank=rank, world=world, device=dev, noise=noise)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(vals: list[float]) -> list[float]:
+        t = torch.tensor(vals, device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    # ---------------- device-resident run (value)
+    gn = torch.Generator(device="cpu").manual_seed(ecfg.seed)
+    noise_cpu = torch.randn((cfg.in_ch, ecfg.num_frames, cfg.lat_h, cfg.lat_w), generator=gn).to(torch.bfloat16)
+    eng = make_engine(noise_cpu.to(dev))
+    for t in range(fill + args.warmup):
+        eng.tick(t)
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    attn_sink: list = []
+    backend.set_attention_timer(attn_sink)
+    launches0 = kernels.LAUNCHES[0]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    evs[0].record()
+    for i in range(args.steps):
+        eng.tick(fill + args.warmup + i)
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    backend.set_attention_timer(None)
+    launches = kernels.LAUNCHES[0] - launches0
+    clocks = sampler.stop() if sampler else None
+    tick_ms = max_over_ranks([evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)])
+    total_ms = max_over_ranks([evs[0].elapsed_time(evs[-1])])[0]
+    p50 = statistics.median(tick_ms)
+    fps = FRAMES_PER_TICK * 1000.0 / p50
+    # attention roofline from the live events of the timed region (rank 0's GPU)
+    a_flops = sum(f for f, _, _ in attn_sink)
+    a_ms = sum(e0.elapsed_time(e1) for _, e0, e1 in attn_sink)
+    n_attn = len(attn_sink)
+    eng.close()
+    del eng
+    torch.cuda.empty_cache()
+
+    # ---------------- host-driven run (e2e)
+    e2e = None
+    if not args.no_e2e:
+        noise_host = noise_cpu.pin_memory()
+        eng = make_engine(noise_host)
+        for t in range(fill + args.warmup):
+            eng.tick(t)
+        out_host = torch.empty((cfg.in_ch, 3, cfg.lat_h, cfg.lat_w), dtype=torch.bfloat16).pin_memory()
+        barrier()
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        ev[0].record()
+        d2h = 0
+        for i in range(args.steps):
+            t = fill + args.warmup + i
+            eng.tick(t)  # copies its noise chunk from pinned host memory (engine.noise_chunk)
+            c = t - eng.store
+            if c in eng.final:
+                out_host.copy_(eng.final.pop(c), non_blocking=True)
+                d2h += out_host.numel() * out_host.element_size()
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+        barrier()
+        tms = max_over_ranks([ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)])
+        h2d = cfg.in_ch * 3 * cfg.lat_h * cfg.lat_w * 2 if 0 in eng.local else 0
+        tot = max_over_ranks([float(h2d), float(d2h) / max(1, args.steps)])
+        e2e = {"value": FRAMES_PER_TICK * 1000.0 / statistics.median(tms), "unit": "FPS",
+               "h2d_bytes_per_step": int(tot[0]), "d2h_bytes_per_step": int(tot[1])}
+        eng.close()
+        del eng
+
+    peaks, src = _peaks()
+    if rank == 0:
+        achieved = a_flops / (a_ms * 1e-3) / 1e12 if a_ms > 0 else None
+        peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "attention_traffic.json")
+        if os.path.exists(tp):
+            with open(tp) as f:
+                traffic = json.load(f).get("bytes_per_launch_scaled")
+        cpu = None
+        if world == 1:
+            torch.set_num_threads(os.cpu_count() or 1)
+            fps_cpu, dt, desc, threads = cpu_reference_sample(args.preset)
+            cpu = {"value": fps_cpu, "unit": "FPS", "cores": threads, "kind": "port", "sample": desc}
+        line = {
+            "metric": METRIC, "value": fps, "unit": "FPS", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "tick_ms_p50": p50,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) weights, N(0,1) text, seed-0 Gaussian noise)",
+            "config": {"workload": f"{args.preset} {S}-step wavefront + store, steady tick, stages merged onto "
+                                   f"{min(world, S + 1)} rank(s)",
+                       "model": f"Wan2.1-{args.preset}-shape", "tokens_per_chunk": cfg.tokens_per_chunk,
+                       "kv_transport": args.kv, "w8a8": args.w8a8, "world": world,
+                       "l2": "inputs larger than L2 (K/V slabs and weights, GBs per tick)",
+                       "parallelism": f"wavefront stages over {min(world, S + 1)} GPU(s)"},
+            "roofline": {"bound": "tensor", "kernel": "attn_fwd_bf16_kernel (self + cross attention)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+                         "launches": n_attn, "peak_source": f"{src} bf16_tflops_sustained"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+        from waveforcing_b200.wavefront.engine import place_stages
+
+        line["config"]["stage_rank"] = place_stages(S, world)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

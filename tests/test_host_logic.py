@@ -1,0 +1,118 @@
+"""Host-side logic of the wavefront path on CPU: stage placement, slot
+geometry (against the reference-generated golden), and the multi-process IPC
+handle exchange / close ordering over gloo with a fake IPC layer (the
+reference tests its close ordering the same way, tests/test_ipc_lifecycle.py)."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from waveforcing_b200.denoiser.exchange import paged
+from waveforcing_b200.wavefront.engine import place_stages, stage_costs
+
+
+def test_place_stages_contiguous_and_balanced():
+    assert place_stages(5, 8) == [0, 1, 2, 3, 4, 5]
+    assert place_stages(5, 6) == [0, 1, 2, 3, 4, 5]
+    assert place_stages(5, 1) == [0] * 6
+    for world in (2, 3, 4, 5):
+        pl = place_stages(5, world)
+        assert pl[0] == 0 and pl[-1] == world - 1
+        assert all(b - a in (0, 1) for a, b in zip(pl, pl[1:])), pl  # contiguous, ordered
+        cost = stage_costs(5)
+        loads = [sum(c for c, r in zip(cost, pl) if r == k) for k in range(world)]
+        assert max(loads) <= sum(cost) / world * 1.6, (world, loads)
+    assert place_stages(4, 2) == place_stages(4, 2)
+
+
+def test_tick_geometry_matches_reference_golden(golden):
+    recs = golden("geometry.json")
+    for r in recs:
+        if r["role"] != "denoise":
+            continue
+        g = paged.tick_geometry(r["rank"], r["tick"], r["act_ranks"], r["store_active"], r["rf_step"], 21, 3)
+        T = 4680
+        assert g["naw"] == r["naw"]
+        assert g["base_infl"] * T == r["self_off"] and g["naw"] * T == r["live_off"]
+        assert g["active_slots"] * T == r["active_len"]
+        assert g["recv"] == r["recv_srcs"]
+        assert [list(x) for x in g["send"]] == r["send_slots"]
+
+
+def test_slab_geometry_matches_reference():
+    # paged.py:26-30 for 5-step and 4-step, max_attn_frames 21
+    assert paged.slab_geometry(21, 5, 3) == (2, 8)
+    assert paged.slab_geometry(21, 4, 3) == (3, 8)
+
+
+# ------------------------------------------------------------- 2-rank gloo
+class _FakeIPC:
+    def __init__(self, rank, log):
+        self.rank, self.log, self.n = rank, log, 0
+
+    def ipc_export(self, t):
+        self.n += 1
+        return (bytes([self.rank, self.n]) + bytes(62), 0)
+
+    def ipc_open_handle(self, h):
+        ptr = 0x10000 * (h[0] + 1) + h[1] * 0x100
+        self.log.append(("open", ptr))
+        return ptr
+
+    def ipc_close_handle(self, ptr):
+        self.log.append(("close", ptr))
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    log = []
+    paged.ipc = _FakeIPC(rank, log)
+    try:
+        # 3-step wavefront (stages 0,1,2 + store 3) on 2 ranks: {0,1} on rank 0, {2,3} on rank 1
+        xp = paged.PagedTransport(device="cpu", rank=rank, world=world, stage_rank=[0, 0, 1, 1], rf_step=3, Ln=2,
+                                  T=4, H=1, D=8, fp8=False)
+        dst = {m: dict(d) for m, d in xp.dst.items()}
+        xp.close()
+        xp.close()  # idempotent
+        q.put((rank, sorted(dst), {m: d["local"] for m, d in dst.items()}, log))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_two_rank_handle_exchange_and_close_order():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, stages, local, log = q.get(timeout=120)
+        res[r] = (stages, local, log)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # rank 0 hosts consumer stages 0,1 (local); it publishes only from 0/1 to lower stages -> no remote opens
+    assert res[0][0] == [0, 1] and all(res[0][1].values())
+    assert res[0][2] == []
+    # rank 1 hosts stage 2 (consumer, local) and the store, which publishes to stages 0,1 on rank 0
+    assert res[1][0] == [0, 1, 2] and res[1][1] == {0: False, 1: False, 2: True}
+    opens = [p for op, p in res[1][2] if op == "open"]
+    closes = [p for op, p in res[1][2] if op == "close"]
+    assert opens and closes == list(reversed(opens))
+    assert len(set(opens)) == len(opens)  # every handle opened once

@@ -80,7 +80,9 @@ __device__ __forceinline__ float div_exact(float x, const RowQuant& q) {
   if (!q.finite) return __fdiv_rn(x, q.s);
   const float q0 = x * q.r;
   const float e = fmaf(-q0, q.s, x);
-  return fmaf(e, q.r, q0);
+  // s > 0, so the quotient carries x's sign; this keeps -0 / s == -0, which the
+  // correction step alone would turn into +0 (+0 + -0 rounds to +0)
+  return copysignf(fmaf(e, q.r, q0), x);
 }
 
 // 8 bf16 (uint4) -> 8 codes (uint2)

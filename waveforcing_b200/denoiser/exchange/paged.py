@@ -1,0 +1,376 @@
+"""Fixed-slot paged K/V exchange with FP8 transport and stage merging.
+
+Semantics follow wave_rt/denoiser/exchange/paged.py:
+  * slab sizing (naw, Wmax)        -- paged.py:26-30
+  * denoise slot geometry          -- paged.py:160-189
+  * publish: payload then flag     -- paged.py:120-145 (copy stream, release write)
+  * consumer wait                  -- paged.py:147-154 (here BOUNDED: a timed-out
+                                      wait raises instead of hanging the stream)
+  * assembled context Kb[:active]  -- paged.py:191-255; store side :257-310
+  * anchor re-RoPE + working set   -- wave_rt/denoiser/exchange/common.py:70-108
+  * drain                          -- wave_rt/denoiser/exchange/onesided.py:181-187
+The closures keep the reference's keyword contract and return (K, V) as
+[1, Lk, H, D] views, so ``PagedExchangeMixin`` drops into the reference's
+WaveDenoiser (methods ``_init_paged``, ``_make_denoise_exch_paged``,
+``_make_store_exch_paged``, ``_publish_paged``, ``_wait_paged_flag``,
+``_drain_publish``).
+
+What is new relative to the reference:
+  * stages merge onto fewer ranks: one ``PagedTransport`` per process owns the
+    slabs of every consumer stage it hosts; a publish to a stage on the same
+    GPU is a stream-ordered local write, to another GPU an IPC peer write
+    plus a release flag;
+  * FP8 e4m3 transport (the reference refuses FP8 with paged, paged.py:36-37):
+    slabs hold per-token codes + f32 scales written by one fused
+    quantise-and-publish kernel; the consumer dequantises the received slots
+    into a bf16 assembly buffer before attention.  Local pages (anchor,
+    working, self) stay bf16, so numerics do not depend on stage placement.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from waveforcing_b200 import _lib as L
+from waveforcing_b200 import kernels
+from waveforcing_b200.distributed import ipc
+
+
+def slab_geometry(max_attn_frames: int, rf_step: int, npb: int):
+    """paged.py:26-30 -> (naw_max, Wmax)."""
+    wmax_frames = max_attn_frames - rf_step * npb - npb
+    naw = 1 + max(0, wmax_frames // npb)
+    return naw, naw + 1 + rf_step
+
+
+def tick_geometry(stage, tick, act, store_active, rf_step, max_attn_frames, npb):
+    """paged.py:160-189 for consumer ``stage`` (all in chunk-slot units)."""
+    store = rf_step
+    clean_len = min(8, max(0, tick - store))
+    wmax_chunks = max(0, (max_attn_frames - len(act) * npb - npb) // npb)
+    naw = 0 if clean_len == 0 else 1 + min(wmax_chunks, clean_len - 1)
+    live = 1 if store_active else 0
+    base_infl = naw + live
+    infl = [n for n in act if n >= stage]
+    recv = [n for n in act if n > stage] + ([store] if store_active else [])
+    send = []
+    for m in act:
+        if m >= stage:
+            continue
+        send.append((m, base_infl + sum(1 for n in act if m <= n < stage)))
+    return dict(clean_len=clean_len, naw=naw, live=live, base_infl=base_infl, active_slots=base_infl + len(infl),
+                recv=recv, send=send)
+
+
+class PagedTransport:
+    """Slabs, flags and peer pointers for the stages one process hosts."""
+
+    def __init__(self, *, device, rank: int, world: int, stage_rank: list[int], rf_step: int, Ln: int, T: int,
+                 H: int, D: int, npb: int = 3, max_attn_frames: int = 21, GT: int = 2, fp8: bool = False,
+                 dtype=torch.bfloat16, timeout_s: float = 30.0, group=None) -> None:
+        self.device = torch.device(device)
+        self.rank, self.world = rank, world
+        self.stage_rank = list(stage_rank)  # stage -> rank, stages 0..rf_step (rf_step = store)
+        self.rf_step, self.store = rf_step, rf_step
+        self.Ln, self.T, self.H, self.D, self.npb = Ln, T, H, D, npb
+        self.max_attn_frames, self.GT, self.fp8, self.dtype = max_attn_frames, GT, fp8, dtype
+        self.timeout_s = timeout_s
+        self.group = group
+        self.naw_max, self.Wmax = slab_geometry(max_attn_frames, rf_step, npb)
+        self.local = [s for s in range(rf_step + 1) if self.stage_rank[s] == rank]
+        # a CPU device is accepted only to exercise the host-side bookkeeping in tests
+        self.copy_stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
+        self._pending: list = []
+        self._ipc_bases: list[int] = []
+        self._opened: dict = {}
+        self.slabs: dict = {}
+        self.flags: dict = {}
+        self.src_index: dict = {}
+        THD = T * H * D
+        W = self.Wmax * T
+        for m in self.local:
+            if m >= rf_step:
+                continue
+            srcs = list(range(m + 1, rf_step)) + [self.store]
+            self.src_index[m] = {s: i for i, s in enumerate(srcs)}
+            if fp8:
+                sl = dict(kc=torch.zeros((GT, Ln, W, H * D), device=self.device, dtype=torch.uint8),
+                          vc=torch.zeros((GT, Ln, W, H * D), device=self.device, dtype=torch.uint8),
+                          ks=torch.ones((GT, Ln, W), device=self.device, dtype=torch.float32),
+                          vs=torch.ones((GT, Ln, W), device=self.device, dtype=torch.float32),
+                          kb=torch.zeros((W, H, D), device=self.device, dtype=dtype),
+                          vb=torch.zeros((W, H, D), device=self.device, dtype=dtype))
+            else:
+                sl = dict(k=torch.zeros((GT, Ln, W, H, D), device=self.device, dtype=dtype),
+                          v=torch.zeros((GT, Ln, W, H, D), device=self.device, dtype=dtype))
+            self.slabs[m] = sl
+            self.flags[m] = torch.zeros((len(srcs), GT, Ln), device=self.device, dtype=torch.int32)
+        self.store_buf = None
+        if self.store in self.local:
+            cap = (1 + max(0, (max_attn_frames - 2 * npb) // npb) + 1) * T
+            self.store_buf = (torch.zeros((cap, H, D), device=self.device, dtype=dtype),
+                              torch.zeros((cap, H, D), device=self.device, dtype=dtype))
+        self.timeout_word = torch.zeros(1, device=self.device, dtype=torch.int32)
+        # destination tables: consumer stage -> dict of base pointers (local or peer)
+        self.dst: dict = {}
+        self._exchange_handles()
+
+    # ------------------------------------------------------------------ setup
+    def _exchange_handles(self) -> None:
+        mine = {}
+        for m, sl in self.slabs.items():
+            ent = {k: (ipc.ipc_export(t) if self.world > 1 else None) for k, t in sl.items()
+                   if k in ("k", "v", "kc", "vc", "ks", "vs")}
+            ent["flags"] = ipc.ipc_export(self.flags[m]) if self.world > 1 else None
+            mine[m] = ent
+        if self.world > 1:
+            gathered = [None] * self.world
+            dist.all_gather_object(gathered, (self.rank, mine), group=self.group)
+        else:
+            gathered = [(self.rank, mine)]
+        for rk, ents in gathered:
+            for m, ent in ents.items():
+                if rk == self.rank:
+                    sl = self.slabs[m]
+                    self.dst[m] = {k: sl[k].data_ptr() for k in ent if k != "flags"}
+                    self.dst[m]["flags"] = self.flags[m].data_ptr()
+                    self.dst[m]["local"] = True
+                elif any(s > m or s == self.store for s in self.local):
+                    d = {"local": False}
+                    for k, (h, off) in ent.items():
+                        d[k] = self._open(h) + off
+                    self.dst[m] = d
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+    def _open(self, h: bytes) -> int:
+        if h not in self._opened:
+            base = ipc.ipc_open_handle(h)
+            self._opened[h] = base
+            self._ipc_bases.append(base)
+        return self._opened[h]
+
+    def close(self, coordinated: bool = True) -> None:
+        """Release imported mappings (wave_rt/denoiser/engine.py:156-212): drain
+        the copy stream and the device, barrier, close every opened handle in
+        reverse order, barrier again; on an exception path (coordinated=False)
+        no collective is issued.  Idempotent."""
+        if getattr(self, "_closed", False):
+            return
+        self._closed = True
+        if self.copy_stream is not None:
+            self.copy_stream.synchronize()
+            torch.cuda.synchronize(self.device)
+        if coordinated and self.world > 1:
+            dist.barrier(group=self.group)
+        for base in reversed(self._ipc_bases):
+            ipc.ipc_close_handle(base)
+        self._ipc_bases.clear()
+        self._opened.clear()
+        if coordinated and self.world > 1:
+            dist.barrier(group=self.group)
+        self.dst.clear()
+
+    # ---------------------------------------------------------------- publish
+    def _slot_offsets(self, m, gen, layer, slot):
+        """Element offsets of (gen, layer, slot) in consumer m's slabs."""
+        W = self.Wmax * self.T
+        tok = (gen * self.Ln + layer) * W + slot * self.T
+        return tok
+
+    def publish(self, s: int, k: torch.Tensor, v: torch.Tensor, send, layer: int, gen: int, tick: int) -> None:
+        """Producer stage ``s`` publishes one layer's K, V [T, H, D] into each
+        consumer slot of ``send`` [(stage, slot)] (paged.py:120-145)."""
+        if not send:
+            return
+        T, HD = self.T, self.H * self.D
+        src_i = {m: self.src_index_of(m, s) for m, _ in send}
+        cur = torch.cuda.current_stream(self.device)
+        if self.fp8:
+            ck, cv, sk, sv = [], [], [], []
+            for m, slot in send:
+                d = self.dst[m]
+                tok = self._slot_offsets(m, gen, layer, slot)
+                ck.append(d["kc"] + tok * HD)
+                cv.append(d["vc"] + tok * HD)
+                sk.append(d["ks"] + tok * 4)
+                sv.append(d["vs"] + tok * 4)
+            kernels.kv_quant_publish(k.view(T, HD), v.view(T, HD), ck, cv, sk, sv)
+            for m, _slot in send:
+                d = self.dst[m]
+                if not d["local"]:
+                    fl = d["flags"] + ((src_i[m] * self.GT + gen) * self.Ln + layer) * 4
+                    ipc.stream_write_u32(cur.cuda_stream, fl, tick)
+            return
+        remote = []
+        for m, slot in send:
+            d = self.dst[m]
+            if d["local"]:
+                sl = self.slabs[m]
+                sl["k"][gen, layer, slot * T:(slot + 1) * T].copy_(k)
+                sl["v"][gen, layer, slot * T:(slot + 1) * T].copy_(v)
+            else:
+                remote.append((m, slot))
+        if not remote:
+            return
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        self.copy_stream.wait_event(ev)
+        sh = self.copy_stream.cuda_stream
+        nb = k.numel() * k.element_size()
+        for m, slot in remote:
+            d = self.dst[m]
+            off = self._slot_offsets(m, gen, layer, slot) * self.H * self.D * k.element_size()
+            ipc.memcpy_dtod_async(d["k"] + off, k.data_ptr(), nb, sh)
+            ipc.memcpy_dtod_async(d["v"] + off, v.data_ptr(), nb, sh)
+            fl = d["flags"] + ((src_i[m] * self.GT + gen) * self.Ln + layer) * 4
+            ipc.stream_write_u32(sh, fl, tick)
+        k.record_stream(self.copy_stream)
+        v.record_stream(self.copy_stream)
+        self._pending += [k, v]
+
+    def src_index_of(self, m: int, s: int) -> int:
+        srcs = list(range(m + 1, self.rf_step)) + [self.store]
+        return srcs.index(s)
+
+    def wait(self, m: int, src: int, layer: int, gen: int, tick: int) -> None:
+        """Bounded device-side acquire on src's flag for (gen, layer) (paged.py:147-154)."""
+        if self.stage_rank[src] == self.rank:
+            return  # same GPU: the publish precedes this read on the stream
+        i = self.src_index[m][src]
+        addr = self.flags[m][i, gen, layer].data_ptr()
+        ipc.wait_flag_bounded(torch.cuda.current_stream(self.device).cuda_stream, addr, tick, self.timeout_s,
+                              self.timeout_word.data_ptr())
+
+    def drain(self) -> None:
+        """onesided.py:181-187: order later work after this tick's publications."""
+        ev = torch.cuda.Event()
+        ev.record(self.copy_stream)
+        torch.cuda.current_stream(self.device).wait_event(ev)
+        self._pending = []
+
+    def check_timeouts(self) -> None:
+        """Raise if any bounded wait gave up (reads a device word; syncs)."""
+        if int(self.timeout_word.item()) != 0:
+            raise TimeoutError("paged exchange: a producer flag did not arrive within the timeout")
+
+    # ---------------------------------------------------------------- context
+    def anchor_working(self, clean_L, csf, qf, rope_fn):
+        """common.py:70-91 -> (list of K pages, list of V pages) as [T, H, D]."""
+        if not clean_L:
+            return [], []
+        npb = self.npb
+        wmax_chunks = max(0, (self.max_attn_frames - qf - npb) // npb)
+        anchor, rest = clean_L[0], clean_L[1:]
+        working = rest[-wmax_chunks:] if wmax_chunks > 0 else []
+        rope_start = csf - len(working) * npb - npb
+        ak = rope_fn(anchor["ku"], rope_start)
+        return [ak] + [w["kr"] for w in working], [anchor["v"]] + [w["v"] for w in working]
+
+    def make_denoise_exch(self, m: int, clean, act, tick_csf, tick_qf, store_active, tick, rope_fn,
+                          store_slot_sink: dict | None = None):
+        g = tick_geometry(m, tick, act, store_active, self.rf_step, self.max_attn_frames, self.npb)
+        if g["active_slots"] > self.Wmax:
+            raise RuntimeError(f"[paged stage {m}] active_slots={g['active_slots']} > Wmax={self.Wmax}")
+        T = self.T
+        gen = tick % self.GT
+        naw, base_infl, act_slots = g["naw"], g["base_infl"], g["active_slots"]
+        self_off, live_off, active_len = base_infl * T, naw * T, act_slots * T
+        recv, send = g["recv"], g["send"]
+        sl = self.slabs[m]
+
+        def exch(*, layer_idx, roped_query, roped_key, unroped_key, value, current_start, tokens_per_frame,
+                 post_patch_height, post_patch_width, dim, rope_num_heads, num_frames_per_block):
+            Lh = layer_idx
+            k = roped_key[0]
+            v = value[0]
+            self.publish(m, k, v, send, Lh, gen, tick)
+            if self.fp8:
+                Kb, Vb = sl["kb"], sl["vb"]
+            else:
+                Kb, Vb = sl["k"][gen, Lh], sl["v"][gen, Lh]
+            aK, aV = self.anchor_working(clean[Lh], tick_csf, tick_qf, rope_fn)
+            if len(aK) != naw:
+                raise RuntimeError(f"[paged stage {m}] anchor+working={len(aK)} != naw={naw} (t={tick})")
+            off = 0
+            for ak, av in zip(aK, aV):
+                Kb[off:off + T].copy_(ak)
+                Vb[off:off + T].copy_(av)
+                off += T
+            Kb[self_off:self_off + T].copy_(k)
+            Vb[self_off:self_off + T].copy_(v)
+            for src in recv:
+                self.wait(m, src, Lh, gen, tick)
+            if self.fp8:
+                HD = self.H * self.D
+                for a, b in ((naw, base_infl), (base_infl + 1, act_slots)):
+                    if b <= a:
+                        continue
+                    rows = slice(a * T, b * T)
+                    kernels.kv_dequant(sl["kc"][gen, Lh, rows], sl["ks"][gen, Lh, rows], L.WF_SCALE_TOKEN,
+                                       out=Kb[rows].view(-1, HD))
+                    kernels.kv_dequant(sl["vc"][gen, Lh, rows], sl["vs"][gen, Lh, rows], L.WF_SCALE_TOKEN,
+                                       out=Vb[rows].view(-1, HD))
+            if store_active and store_slot_sink is not None:
+                store_slot_sink[Lh] = (Kb[live_off:live_off + T].clone(), Vb[live_off:live_off + T].clone())
+            return Kb[:active_len].unsqueeze(0), Vb[:active_len].unsqueeze(0)
+
+        return exch
+
+    def make_store_exch(self, clean, store_kv: list, chunk: int, act, tick, rope_fn):
+        clean_len = min(8, max(0, tick - self.store))
+        wmax_chunks = max(0, (self.max_attn_frames - len(act) * self.npb - self.npb) // self.npb)
+        naw = 0 if clean_len == 0 else 1 + min(wmax_chunks, clean_len - 1)
+        send = [(m, naw) for m in act]
+        gen = tick % self.GT
+        T = self.T
+        Kbuf, Vbuf = self.store_buf
+
+        def exch(*, layer_idx, roped_query, roped_key, unroped_key, value, current_start, tokens_per_frame,
+                 post_patch_height, post_patch_width, dim, rope_num_heads, num_frames_per_block):
+            k = roped_key[0]
+            v = value[0]
+            self.publish(self.store, k, v, send, layer_idx, gen, tick)
+            aK, aV = self.anchor_working(clean[layer_idx], chunk * self.npb, self.npb, rope_fn)
+            off = 0
+            for ak, av in zip(aK, aV):
+                Kbuf[off:off + T].copy_(ak)
+                Vbuf[off:off + T].copy_(av)
+                off += T
+            Kbuf[off:off + T].copy_(k)
+            Vbuf[off:off + T].copy_(v)
+            store_kv[layer_idx] = (k.clone(), unroped_key[0].clone(), v.clone())
+            return Kbuf[:off + T].unsqueeze(0), Vbuf[:off + T].unsqueeze(0)
+
+        return exch
+
+
+class PagedExchangeMixin:
+    """Reference-named entry points (wave_rt/denoiser/exchange/paged.py) over
+    ``PagedTransport`` for a WaveDenoiser whose rank hosts one stage."""
+
+    def _init_paged(self) -> None:
+        self._pg = PagedTransport(device=self.device, rank=self.rank, world=self.world,
+                                  stage_rank=list(range(self.rf_step + 1)), rf_step=self.rf_step, Ln=self.Ln,
+                                  T=self.tokens_per_chunk, H=self._kv_shape[2], D=self._kv_shape[3], npb=self.npb,
+                                  max_attn_frames=self.max_attn_frames,
+                                  fp8=bool(getattr(self, "_paged_fp8", False)))
+        self._pg_naw, self._pg_wmax = self._pg.naw_max, self._pg.Wmax
+        self._os_gt = self._pg.GT
+
+    def _publish_paged(self, k, v, dst_slots, layer: int, gen: int, tick: int) -> None:
+        self._pg.publish(self.rank, k, v, dst_slots, layer, gen, tick)
+
+    def _wait_paged_flag(self, src: int, layer: int, gen: int, tick: int) -> None:
+        self._pg.wait(self.rank, src, layer, gen, tick)
+
+    def _make_denoise_exch_paged(self, clean, act_ranks, tick_csf, tick_qf, store_active):
+        return self._pg.make_denoise_exch(self.rank, clean, act_ranks, tick_csf, tick_qf, store_active,
+                                          self._cur_tick, self._wf_rope_fn, self._exch_store_slot)
+
+    def _make_store_exch_paged(self, clean, store_kv, c, act_ranks):
+        return self._pg.make_store_exch(clean, store_kv, c, act_ranks, self._cur_tick, self._wf_rope_fn)
+
+    def _drain_publish(self) -> None:
+        self._pg.drain()

@@ -13,8 +13,13 @@ import torch
 
 from waveforcing_b200 import _lib as L
 
+# Number of libwfk kernel launches issued through these wrappers (reported by
+# bench.py as gpu_launches for its timed region).
+LAUNCHES = [0]
+
 
 def _stream() -> int:
+    LAUNCHES[0] += 1
     return torch.cuda.current_stream().cuda_stream
 
 

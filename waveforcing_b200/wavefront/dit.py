@@ -1,0 +1,334 @@
+"""Wan2.1-shaped causal DiT: the caller of the hot path.
+
+The reference's DiT is SGLang's CausalWanTransformer3DModel (not vendored);
+its vendored statement is the naive Rolling-Forcing model, restated here:
+  * block           -- naive_rt/rolling_forcing/wan/modules/causal_model.py:309-420
+                       (6-vector modulation, LayerNorm eps 1e-6 without affine,
+                       RMSNorm on q/k over the full dim, GELU-tanh FFN)
+  * self-attention  -- the patched forward, wave_rt/runtime/backend.py:87-157:
+                       RoPE q/k, call the exchange closure, attention on
+                       (roped_query, ctx_k, ctx_v)
+  * cross-attention -- naive_rt/rolling_forcing/wan/modules/model.py:158-196
+                       (text K/V computed once and cached)
+  * embeddings/head -- causal_model.py:524-533 and :421-433
+  * x0 from flow    -- naive_rt/rolling_forcing/utils/wan_wrapper.py:169-193
+  * presets/init    -- wave_rt/runtime/dummy_model.py:25-59 (N(0, 0.02))
+
+Several chunk-stage tasks ("stages") run layer-interleaved in one call: the
+linears see all stages' tokens as one matrix, and the self-attention of each
+stage runs separately on its own assembled K/V context, highest stage first
+so a stage's publish precedes every local consumer's read.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from waveforcing_b200 import kernels
+from waveforcing_b200.runtime.backend import dispatch_attention
+
+PRESETS = {
+    "1.3b": dict(dim=1536, heads=12, layers=30, ffn=8960),
+    "5b": dict(dim=3072, heads=24, layers=30, ffn=13824),
+    "14b": dict(dim=5120, heads=40, layers=40, ffn=13824),
+}
+
+
+@dataclass
+class DiTConfig:
+    dim: int = 1536
+    heads: int = 12
+    layers: int = 30
+    ffn: int = 8960
+    text_len: int = 512
+    text_dim: int = 4096
+    freq_dim: int = 256
+    in_ch: int = 16
+    out_ch: int = 16
+    patch: tuple = (1, 2, 2)
+    eps: float = 1e-6
+    frames_per_block: int = 3
+    lat_h: int = 60
+    lat_w: int = 104
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.heads
+
+    @property
+    def pph(self) -> int:
+        return self.lat_h // self.patch[1]
+
+    @property
+    def ppw(self) -> int:
+        return self.lat_w // self.patch[2]
+
+    @property
+    def tokens_per_frame(self) -> int:
+        return self.pph * self.ppw
+
+    @property
+    def tokens_per_chunk(self) -> int:
+        return self.frames_per_block * self.tokens_per_frame
+
+    @classmethod
+    def preset(cls, name: str, **kw) -> "DiTConfig":
+        d = dict(PRESETS[name])
+        d.update(kw)
+        return cls(**d)
+
+
+def sinusoidal_embedding_1d(dim: int, position: torch.Tensor) -> torch.Tensor:
+    """naive_rt/rolling_forcing/wan/modules/model.py:14-26 (float64)."""
+    half = dim // 2
+    position = position.to(torch.float64)
+    sinusoid = torch.outer(position, torch.pow(10000, -torch.arange(half, device=position.device).to(position).div(half)))
+    return torch.cat([torch.cos(sinusoid), torch.sin(sinusoid)], dim=1)
+
+
+def rope_tables(cfg: DiTConfig, num_frames: int, start_frame: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """f32 cos/sin [F*h*w, head_dim/2] for frames [start, start+F) (causal_model.py:27-54, built in f64)."""
+    d = cfg.head_dim
+    c = d // 2
+    widths = [c - 2 * (c // 3), c // 3, c // 3]
+    dims = [d - 4 * (d // 6), 2 * (d // 6), 2 * (d // 6)]
+
+    def ang(pos, dd):
+        inv = 1.0 / torch.pow(10000.0, torch.arange(0, dd, 2, dtype=torch.float64, device=device) / dd)
+        return torch.outer(pos.to(torch.float64), inv)
+
+    fr = ang(torch.arange(start_frame, start_frame + num_frames, device=device), dims[0])
+    hh = ang(torch.arange(cfg.pph, device=device), dims[1])
+    ww = ang(torch.arange(cfg.ppw, device=device), dims[2])
+    f, h, w = num_frames, cfg.pph, cfg.ppw
+    a = torch.cat([fr[:, None, None, :].expand(f, h, w, widths[0]),
+                   hh[None, :, None, :].expand(f, h, w, widths[1]),
+                   ww[None, None, :, :].expand(f, h, w, widths[2])], dim=-1).reshape(f * h * w, c)
+    return torch.cos(a).float().contiguous(), torch.sin(a).float().contiguous()
+
+
+class RMSNorm(nn.Module):
+    """naive_rt/rolling_forcing/wan/modules/model.py:70-88."""
+
+    def __init__(self, dim: int, eps: float) -> None:
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)).type_as(x) * self.weight
+
+
+class Attn(nn.Module):
+    def __init__(self, dim: int, eps: float) -> None:
+        super().__init__()
+        self.q = nn.Linear(dim, dim)
+        self.k = nn.Linear(dim, dim)
+        self.v = nn.Linear(dim, dim)
+        self.o = nn.Linear(dim, dim)
+        self.norm_q = RMSNorm(dim, eps)
+        self.norm_k = RMSNorm(dim, eps)
+
+
+class FFN(nn.Module):
+    def __init__(self, dim: int, ffn: int) -> None:
+        super().__init__()
+        self.fc_in = nn.Linear(dim, ffn)
+        self.fc_out = nn.Linear(ffn, dim)
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: DiTConfig) -> None:
+        super().__init__()
+        self.self_attn = Attn(cfg.dim, cfg.eps)
+        self.cross_attn = Attn(cfg.dim, cfg.eps)
+        self.ffn = FFN(cfg.dim, cfg.ffn)
+        self.modulation = nn.Parameter(torch.randn(1, 6, cfg.dim) / cfg.dim**0.5)
+        self._wqkv = None
+        self._bqkv = None
+
+
+def _lin(mod, x):
+    """Apply a linear that may be nn.Linear or a (y, None)-returning W8A8 hook."""
+    y = mod(x)
+    return y[0] if isinstance(y, tuple) else y
+
+
+@dataclass
+class StageTask:
+    """One chunk-stage task: the noisy latent chunk and its denoising step."""
+
+    latent: torch.Tensor  # [C, F, H, W]
+    timestep: float  # model timestep (already warped)
+    start_frame: int
+    stage: int
+    exch: object = None  # closure with the wave_rt exchange contract
+
+
+class WanDiT(nn.Module):
+    def __init__(self, cfg: DiTConfig) -> None:
+        super().__init__()
+        self.cfg = cfg
+        d = cfg.dim
+        self.patch_embedding = nn.Linear(cfg.in_ch * math.prod(cfg.patch), d)
+        self.text_embedding = nn.Sequential(nn.Linear(cfg.text_dim, d), nn.GELU(approximate="tanh"), nn.Linear(d, d))
+        self.time_embedding = nn.Sequential(nn.Linear(cfg.freq_dim, d), nn.SiLU(), nn.Linear(d, d))
+        self.time_projection = nn.Sequential(nn.SiLU(), nn.Linear(d, d * 6))
+        self.blocks = nn.ModuleList([Block(cfg) for _ in range(cfg.layers)])
+        self.head_norm_mod = nn.Parameter(torch.randn(1, 2, d) / d**0.5)
+        self.head = nn.Linear(d, cfg.out_ch * math.prod(cfg.patch))
+        self._cross_kv = None
+
+    @classmethod
+    def random(cls, cfg: DiTConfig, device, dtype=torch.bfloat16, seed: int = 0) -> "WanDiT":
+        """dummy_model.py:44-59: every floating parameter ~ N(0, 0.02)."""
+        with torch.device("meta"):
+            m = cls(cfg)
+        m = m.to_empty(device=device)
+        g = torch.Generator(device=device).manual_seed(seed)
+        with torch.no_grad():
+            for p in m.parameters():
+                p.normal_(0.0, 0.02, generator=g)
+        return m.to(dtype)
+
+    # ------------------------------------------------------------ conditioning
+    @torch.no_grad()
+    def set_text(self, text: torch.Tensor) -> None:
+        """Embed [text_len, text_dim] once and cache every layer's cross K/V
+        (the crossattn_cache of causal_model.py / model.py:174-186)."""
+        cfg = self.cfg
+        ctx = self.text_embedding(text.to(self.patch_embedding.weight.dtype))
+        kv = []
+        for b in self.blocks:
+            k = b.cross_attn.norm_k(_lin(b.cross_attn.k, ctx)).view(1, -1, cfg.heads, cfg.head_dim)
+            v = _lin(b.cross_attn.v, ctx).view(1, -1, cfg.heads, cfg.head_dim)
+            kv.append((k.contiguous(), v.contiguous()))
+        self._cross_kv = kv
+
+    def time_mod(self, timestep: float, device):
+        """Per-stage modulation inputs: e [6, dim] f32 and e_head [2, dim] f32."""
+        t = torch.tensor([timestep], device=device)
+        e = self.time_embedding(sinusoidal_embedding_1d(self.cfg.freq_dim, t).to(self.patch_embedding.weight.dtype))
+        e0 = self.time_projection(e).float().view(6, self.cfg.dim)
+        return e0, e.float().view(1, self.cfg.dim)
+
+    def _fused_qkv(self, b: Block):
+        a = b.self_attn
+        if not all(type(m) is nn.Linear for m in (a.q, a.k, a.v)):
+            return None
+        if b._wqkv is None:
+            b._wqkv = torch.cat([a.q.weight, a.k.weight, a.v.weight], 0).contiguous()
+            b._bqkv = torch.cat([a.q.bias, a.k.bias, a.v.bias], 0).contiguous()
+        return b._wqkv, b._bqkv
+
+    # ----------------------------------------------------------------- forward
+    def patchify(self, latent: torch.Tensor) -> torch.Tensor:
+        """[C, F, H, W] -> [F*h*w, C*1*2*2] (the Conv3d patch embedding as a GEMM)."""
+        C, Fr, H, W = latent.shape
+        p1, p2 = self.cfg.patch[1], self.cfg.patch[2]
+        x = latent.reshape(C, Fr, H // p1, p1, W // p2, p2).permute(1, 2, 4, 0, 3, 5)
+        return x.reshape(Fr * (H // p1) * (W // p2), C * p1 * p2)
+
+    def unpatchify(self, x: torch.Tensor, Fr: int) -> torch.Tensor:
+        cfg = self.cfg
+        p1, p2 = cfg.patch[1], cfg.patch[2]
+        x = x.view(Fr, cfg.pph, cfg.ppw, cfg.out_ch, p1, p2).permute(3, 0, 1, 4, 2, 5)
+        return x.reshape(cfg.out_ch, Fr, cfg.pph * p1, cfg.ppw * p2)
+
+    @torch.no_grad()
+    def forward_stages(self, tasks: list[StageTask], layer_hook=None) -> list[torch.Tensor]:
+        """Run every task's 30/40-layer forward, layer-interleaved.  Returns the
+        flow prediction of each task as [C, F, H, W] (f32)."""
+        cfg = self.cfg
+        dev = self.patch_embedding.weight.device
+        dt = self.patch_embedding.weight.dtype
+        S = len(tasks)
+        T = cfg.tokens_per_chunk
+        H, D, dim = cfg.heads, cfg.head_dim, cfg.dim
+        order = sorted(range(S), key=lambda i: -tasks[i].stage)  # publish before consume
+        x = torch.cat([self.patchify(t.latent.to(dt)) for t in tasks], 0)
+        x = _lin(self.patch_embedding, x)  # [S*T, dim]
+        mods, heads_e = [], []
+        for t in tasks:
+            e0, eh = self.time_mod(t.timestep, dev)
+            mods.append(e0)
+            heads_e.append(eh)
+        mods = torch.stack(mods)  # [S, 6, dim] f32
+        ropes = [rope_tables(cfg, cfg.frames_per_block, t.start_frame, dev) for t in tasks]
+        xs = x.view(S, T, dim)
+        for li, b in enumerate(self.blocks):
+            e = (b.modulation.float() + mods).unbind(1)  # 6 x [S, dim]
+            h = F.layer_norm(xs.float(), (dim,), eps=cfg.eps)
+            h = (h * (1 + e[1][:, None]) + e[0][:, None]).to(dt).view(S * T, dim)
+            fq = self._fused_qkv(b)
+            if fq is not None:
+                qkv = F.linear(h, fq[0], fq[1])
+                q, k, v = qkv[:, :dim], qkv[:, dim:2 * dim], qkv[:, 2 * dim:]
+            else:
+                q, k, v = _lin(b.self_attn.q, h), _lin(b.self_attn.k, h), _lin(b.self_attn.v, h)
+            q = b.self_attn.norm_q(q).view(S, T, H, D)
+            k = b.self_attn.norm_k(k).view(S, T, H, D)
+            v = v.reshape(S, T, H, D)
+            o = torch.empty((S, T, H, D), device=dev, dtype=dt)
+            for i in order:
+                cos, sin = ropes[i]
+                rq = kernels.rope_apply(q[i], cos, sin)
+                rk = kernels.rope_apply(k[i], cos, sin)
+                tk = tasks[i]
+                if tk.exch is not None:
+                    K, V = tk.exch(layer_idx=li, roped_query=rq[None], roped_key=rk[None], unroped_key=k[i][None],
+                                   value=v[i][None], current_start=tk.start_frame * cfg.tokens_per_frame,
+                                   tokens_per_frame=cfg.tokens_per_frame, post_patch_height=cfg.pph,
+                                   post_patch_width=cfg.ppw, dim=dim, rope_num_heads=H,
+                                   num_frames_per_block=cfg.frames_per_block)
+                else:
+                    K, V = rk[None], v[i][None]
+                o[i] = dispatch_attention(rq[None], K, V)[0]
+            y = _lin(b.self_attn.o, o.view(S * T, dim)).view(S, T, dim)
+            xs = (xs.float() + y.float() * e[2][:, None]).to(dt)
+            # cross-attention: all stages share the text K/V -> one call
+            qc = b.cross_attn.norm_q(_lin(b.cross_attn.q, xs.view(S * T, dim))).view(1, S * T, H, D)
+            kc, vc = self._cross_kv[li]
+            oc = dispatch_attention(qc, kc, vc)
+            xs = xs + _lin(b.cross_attn.o, oc.view(S * T, dim)).view(S, T, dim)
+            h = F.layer_norm(xs.float(), (dim,), eps=cfg.eps)
+            h = (h * (1 + e[4][:, None]) + e[3][:, None]).to(dt).view(S * T, dim)
+            y = _lin(b.ffn.fc_out, F.gelu(_lin(b.ffn.fc_in, h), approximate="tanh")).view(S, T, dim)
+            xs = (xs.float() + y.float() * e[5][:, None]).to(dt)
+            if layer_hook is not None:
+                layer_hook(li)
+        eh = (self.head_norm_mod.float() + torch.stack(heads_e)).unbind(1)  # 2 x [S, dim]
+        h = F.layer_norm(xs.float(), (dim,), eps=cfg.eps)
+        h = (h * (1 + eh[1][:, None]) + eh[0][:, None]).to(dt)
+        out = _lin(self.head, h.view(S * T, dim)).view(S, T, -1)
+        return [self.unpatchify(out[i].float(), cfg.frames_per_block) for i in range(S)]
+
+
+class FlowMatch:
+    """Timestep warp, flow->x0 and re-noise of the reference pipeline:
+    FlowMatchScheduler(shift=8, sigma_min=0, extra_one_step=True) with 1000
+    train steps (naive_rt/rolling_forcing/utils/scheduler.py:106-176,
+    wan_wrapper.py:136-137, 169-193)."""
+
+    def __init__(self, shift: float = 8.0) -> None:
+        self.shift = shift
+
+    def sigma(self, step: float) -> float:
+        s = step / 1000.0
+        return self.shift * s / (1 + (self.shift - 1) * s)
+
+    def timestep(self, step: float) -> float:
+        return self.sigma(step) * 1000.0
+
+    def x0(self, flow: torch.Tensor, xt: torch.Tensor, step: float) -> torch.Tensor:
+        return (xt.double() - self.sigma(step) * flow.double()).to(xt.dtype)
+
+    def add_noise(self, x0: torch.Tensor, noise: torch.Tensor, step: float) -> torch.Tensor:
+        s = self.sigma(step)
+        return ((1 - s) * x0 + s * noise).type_as(noise)

@@ -1,0 +1,242 @@
+"""Wavefront tick engine with stage merging (the caller of the hot path).
+
+Schedule and data flow follow wave_rt/denoiser/engine.py:
+  * activity       -- _act_denoise/_act_store :214-219, roles :303-311
+  * one tick       -- :287-597: denoise/store forwards with the paged exchange
+                      closure installed, drain, clean-KV promotion (anchor
+                      broadcast at cid 0 :449-488, store slot otherwise
+                      :489-515), latent migration + deterministic re-noise
+                      :221-235, :516-555
+  * ticks          -- num_blocks + stages (engine.py:53 with world = stages)
+The reference needs one rank per stage (wave_rt/config.py:79-83).  Here
+``place_stages`` maps the rf_step denoise stages and the store onto any
+number of ranks: a rank may host several stages, runs them layer-interleaved
+(highest stage first, so local publishes precede local reads), and batches
+their linears.  Ranks beyond the stage count stay idle.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from waveforcing_b200 import kernels
+from waveforcing_b200.denoiser.exchange.paged import PagedTransport
+from waveforcing_b200.wavefront.dit import FlowMatch, StageTask, WanDiT, rope_tables
+
+
+@dataclass
+class EngineConfig:
+    steps: tuple = (1000, 800, 600, 400, 200)
+    num_frames: int = 399  # latent frames
+    npb: int = 3
+    max_attn_frames: int = 21
+    fp8_kv: bool = False
+    context_noise: float = 0.0
+    seed: int = 0
+    timeout_s: float = 60.0
+
+    @property
+    def rf_step(self) -> int:
+        return len(self.steps)
+
+    @property
+    def num_blocks(self) -> int:
+        return self.num_frames // self.npb
+
+
+# Relative attention+linear cost of each stage in steady state (K/V context in
+# chunks plus the linears), used to balance merged stages across ranks.
+def stage_costs(rf_step: int, max_attn_frames: int = 21, npb: int = 3) -> list[float]:
+    wmax = max(0, (max_attn_frames - rf_step * npb - npb) // npb)
+    naw = 1 + wmax
+    ctx = [naw + 1 + (rf_step - s) for s in range(rf_step)]  # live + self + higher stages
+    store_ctx = 1 + max(0, (max_attn_frames - 2 * npb) // npb) + 1
+    lin = 2.9  # linears ~ 2.9 chunk-equivalents of attention for the 1.3B shape
+    return [c + lin for c in ctx] + [store_ctx + lin]
+
+
+def place_stages(rf_step: int, world: int) -> list[int]:
+    """Contiguous, cost-balanced assignment of stages 0..rf_step to ranks."""
+    n = rf_step + 1
+    ranks = min(world, n)
+    if ranks == n:
+        return list(range(n))
+    cost = stage_costs(rf_step)
+    # exact partition of the ordered stages into `ranks` contiguous groups minimising the max load
+    best = None
+
+    def rec(start, k, acc):
+        nonlocal best
+        if k == 1:
+            parts = acc + [(start, n)]
+            mx = max(sum(cost[a:b]) for a, b in parts)
+            if best is None or mx < best[0]:
+                best = (mx, parts)
+            return
+        for end in range(start + 1, n - k + 2):
+            rec(end, k - 1, acc + [(start, end)])
+
+    rec(0, ranks, [])
+    out = [0] * n
+    for r, (a, b) in enumerate(best[1]):
+        for s in range(a, b):
+            out[s] = r
+    return out
+
+
+@dataclass
+class TickStats:
+    tick_ms: list = field(default_factory=list)
+
+
+class WavefrontEngine:
+    def __init__(self, model: WanDiT, cfg: EngineConfig, *, rank: int = 0, world: int = 1, device="cuda",
+                 group=None, noise: torch.Tensor | None = None) -> None:
+        self.m = model
+        self.cfg = cfg
+        self.rank, self.world = rank, world
+        self.device = torch.device(device)
+        self.group = group
+        self.S = cfg.rf_step
+        self.store = self.S
+        self.stage_rank = place_stages(self.S, world)
+        self.local = [s for s in range(self.S + 1) if self.stage_rank[s] == rank]
+        mc = model.cfg
+        self.Ln, self.T, self.H, self.D = mc.layers, mc.tokens_per_chunk, mc.heads, mc.head_dim
+        self.fm = FlowMatch()
+        self.xport = PagedTransport(device=self.device, rank=rank, world=world, stage_rank=self.stage_rank,
+                                    rf_step=self.S, Ln=self.Ln, T=self.T, H=self.H, D=self.D, npb=cfg.npb,
+                                    max_attn_frames=cfg.max_attn_frames, fp8=cfg.fp8_kv,
+                                    timeout_s=cfg.timeout_s, group=group)
+        self.clean = [[] for _ in range(self.Ln)]
+        self.inputs: dict = {}  # stage -> latent chunk [C, F, H, W] for the current tick
+        self.final: dict = {}  # chunk -> clean latent (store rank)
+        self._rope_cache: dict = {}
+        C = mc.in_ch
+        if noise is None:
+            g = torch.Generator(device="cpu").manual_seed(cfg.seed)
+            noise = torch.randn((C, cfg.num_frames, mc.lat_h, mc.lat_w), generator=g).to(torch.bfloat16)
+        self.noise = noise  # [C, F_total, H, W]; may live on the host (pinned) or the device
+        self.mig_shape = (self.S + 1, C, cfg.npb, mc.lat_h, mc.lat_w)
+
+    # ----------------------------------------------------------------- helpers
+    @property
+    def num_ticks(self) -> int:
+        return self.cfg.num_blocks + self.S
+
+    def act_denoise(self, n, t):
+        return 0 <= n < self.S and 0 <= t - n < self.cfg.num_blocks
+
+    def act_store(self, t):
+        return 0 <= t - self.store < self.cfg.num_blocks
+
+    def _rope(self, ku: torch.Tensor, start_frame: int) -> torch.Tensor:
+        tab = self._rope_cache.get(start_frame)
+        if tab is None:
+            tab = rope_tables(self.m.cfg, self.cfg.npb, start_frame, self.device)
+            self._rope_cache[start_frame] = tab
+        return kernels.rope_apply(ku, tab[0], tab[1])
+
+    def _append_clean(self, page: dict) -> None:
+        """common.py:110-114 per layer."""
+        for L in range(self.Ln):
+            cl = self.clean[L]
+            cl.append(page[L])
+            if len(cl) > 8:
+                cl[:] = cl[:1] + cl[-7:]
+
+    # -------------------------------------------------------------------- tick
+    def noise_chunk(self, c: int) -> torch.Tensor:
+        npb = self.cfg.npb
+        ch = self.noise[:, c * npb:(c + 1) * npb]
+        return ch.to(self.device, non_blocking=True).contiguous()
+
+    @torch.no_grad()
+    def tick(self, t: int) -> dict:
+        cfg, S = self.cfg, self.S
+        act = [n for n in range(S) if self.act_denoise(n, t)]
+        oldest = (t - max(act)) if act else 0
+        tick_csf, tick_qf = oldest * cfg.npb, len(act) * cfg.npb
+        store_active = self.act_store(t)
+        if 0 in self.local and self.act_denoise(0, t):
+            self.inputs[0] = self.noise_chunk(t)
+        tasks = []
+        store_kv = [None] * self.Ln
+        store_slot: dict = {}
+        for s in sorted(self.local, reverse=True):
+            if s < S and self.act_denoise(s, t):
+                c = t - s
+                exch = self.xport.make_denoise_exch(s, self.clean, act, tick_csf, tick_qf, store_active, t,
+                                                    self._rope, store_slot if not store_slot else None)
+                tasks.append(StageTask(self.inputs[s], self.fm.timestep(cfg.steps[s]), c * cfg.npb, s, exch))
+            elif s == self.store and store_active:
+                c = t - self.store
+                exch = self.xport.make_store_exch(self.clean, store_kv, c, act, t, self._rope)
+                tasks.append(StageTask(self.inputs[s], cfg.context_noise, c * cfg.npb, s, exch))
+        flows = self.m.forward_stages(tasks) if tasks else []
+        self.xport.drain()
+        out = {}
+        for task, flow in zip(tasks, flows):
+            if task.stage < S:
+                step = cfg.steps[task.stage]
+                out[task.stage] = self.fm.x0(flow, task.latent.float(), step).to(torch.bfloat16)
+            else:
+                self.final[task.start_frame // cfg.npb] = task.latent
+        self._promote(t, store_active, store_kv, store_slot, bool(tasks))
+        self._migrate(t, out)
+        return out
+
+    def _promote(self, t, store_active, store_kv, store_slot, had_task) -> None:
+        if not store_active:
+            return
+        cid = t - self.store
+        Ln = self.Ln
+        hosts_store = self.store in self.local
+        if cid == 0:
+            # anchor: the store's unroped key and value for every layer (engine.py:449-488)
+            if hosts_store:
+                blob = torch.stack([torch.stack([store_kv[L][1] for L in range(Ln)]),
+                                    torch.stack([store_kv[L][2] for L in range(Ln)])]).contiguous()
+            else:
+                blob = torch.empty((2, Ln, self.T, self.H, self.D), device=self.device, dtype=torch.bfloat16)
+            if self.world > 1:
+                dist.broadcast(blob, src=self.stage_rank[self.store], group=self.group)
+            self._append_clean([dict(ku=blob[0, L], v=blob[1, L], cid=cid) for L in range(Ln)])
+        elif hosts_store:
+            self._append_clean([dict(kr=store_kv[L][0], v=store_kv[L][2], cid=cid) for L in range(Ln)])
+        elif len(store_slot) == Ln:
+            self._append_clean([dict(kr=store_slot[L][0], v=store_slot[L][1], cid=cid) for L in range(Ln)])
+
+    def _renoise(self, x0, stage, chunk):
+        """engine.py:221-235: seed 1000*chunk+stage, re-noised to the next step."""
+        g = torch.Generator(device=self.device).manual_seed(1000 * chunk + stage)
+        nz = torch.randn(x0.shape, generator=g, device=self.device, dtype=torch.float32)
+        return self.fm.add_noise(x0.float(), nz, self.cfg.steps[stage + 1]).to(torch.bfloat16)
+
+    def _migrate(self, t, out: dict) -> None:
+        """Hand each denoise stage's result to the next stage (engine.py:516-555)."""
+        S = self.S
+        payload = {}
+        for s, x0 in out.items():
+            c = t - s
+            payload[s + 1] = self._renoise(x0, s, c) if s < S - 1 else x0
+        if self.world == 1:
+            self.inputs.update(payload)
+            return
+        buf = torch.zeros(self.mig_shape, device=self.device, dtype=torch.bfloat16)
+        for dst, x in payload.items():
+            buf[dst].copy_(x)
+        gathered = torch.empty((self.world,) + self.mig_shape, device=self.device, dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(gathered, buf, group=self.group)
+        for s in self.local:
+            if s >= 1:
+                src = self.stage_rank[s - 1]
+                if self.act_denoise(s, t + 1) or (s == self.store and self.act_store(t + 1)):
+                    self.inputs[s] = gathered[src, s].clone()
+
+    def close(self) -> None:
+        self.xport.close()
