@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--w8a8", default="none", choices=["none", "e4m3", "int8"])
     ap.add_argument("--denoise-steps", default="1000,800,600,400,200")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec"],
+                    help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
+    ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
     return ap.parse_args()
 
 
@@ -262,9 +265,11 @@ def run_gpu_arm(args):
     launches0 = kernels.LAUNCHES[0]
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     evs[0].record()
+    torch.cuda.nvtx.range_push("timed")
     for i in range(args.steps):
         eng.tick(fill + args.warmup + i)
         evs[i + 1].record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -276,9 +281,10 @@ def run_gpu_arm(args):
     p50 = statistics.median(tick_ms)
     fps = FRAMES_PER_TICK * 1000.0 / p50
     # attention roofline from the live events of the timed region (rank 0's GPU)
-    a_flops = sum(f for f, _, _ in attn_sink)
-    a_ms = sum(e0.elapsed_time(e1) for _, e0, e1 in attn_sink)
+    a_flops = sum(x[0] for x in attn_sink)
+    a_ms = sum(x[1].elapsed_time(x[2]) for x in attn_sink)
     n_attn = len(attn_sink)
+    a_bytes = sum(x[3] for x in attn_sink) / max(1, n_attn)
     eng.close()
     del eng
     torch.cuda.empty_cache()
@@ -321,8 +327,10 @@ def run_gpu_arm(args):
         traffic = None
         tp = os.path.join(ROOT, "profiles", "attention_traffic.json")
         if os.path.exists(tp):
+            # DRAM bytes of the captured r0 launch equal its algorithmic bytes (ratio in the
+            # profile); scale that ratio to the mean launch of this run
             with open(tp) as f:
-                traffic = json.load(f).get("bytes_per_launch_scaled")
+                traffic = a_bytes * json.load(f)["ratio_traffic_to_algorithmic"]
         cpu = None
         if world == 1:
             torch.set_num_threads(os.cpu_count() or 1)
@@ -357,9 +365,74 @@ def run_gpu_arm(args):
         dist.destroy_process_group()
 
 
+def run_kernel_bench(args):
+    """One hot-path kernel alone, CUDA-event timed, at the steady-state r0 shape:
+      attn  q [4680, H, 128] vs K/V [ctx*4680, H, 128] bf16 (r0 sees 8 chunks)
+      gemm  W8A8 e4m3 FFN fc_in [4680 x dim] x [ffn x dim]^T
+      codec per-token FP8 quantise-and-publish of one layer's K and V to 4 slots
+    Inputs exceed L2 (126 MB) for attn and codec; each launch reads them once."""
+    from waveforcing_b200 import _lib as L
+    from waveforcing_b200 import kernels
+    from waveforcing_b200.wavefront.dit import DiTConfig
+
+    cfg = DiTConfig.preset(args.preset)
+    dev = torch.device("cuda", 0)
+    T, H, D = cfg.tokens_per_chunk, cfg.heads, cfg.head_dim
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel == "attn":
+        Lk = args.ctx_chunks * T
+        q = torch.randn(1, T, H, D, device=dev, generator=g).bfloat16()
+        k = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
+        v = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
+        fn = lambda: kernels.attention(q, k, v)  # noqa: E731
+        work, unit, bound = 4.0 * T * Lk * H * D / 1e12, "TFLOP/s", "tensor"
+        name = f"attn_fwd q{T} kv{Lk} h{H}"
+    elif args.kernel == "gemm":
+        x = torch.randn(T, cfg.dim, device=dev, generator=g).bfloat16()
+        w = (torch.randn(cfg.ffn, cfg.dim, device=dev, generator=g) * 0.02).bfloat16()
+        wq, ws = kernels.weight_quant(w)
+        xq, xs = kernels.act_quant(x)
+        out = torch.empty(T, cfg.ffn, device=dev, dtype=torch.bfloat16)
+        fn = lambda: kernels.gemm_w8a8(xq, xs, wq, ws, None, out=out)  # noqa: E731
+        work, unit, bound = 2.0 * T * cfg.dim * cfg.ffn / 1e12, "TFLOP/s", "tensor"
+        name = f"gemm_w8a8 e4m3 {T}x{cfg.ffn}x{cfg.dim}"
+    else:
+        HD = H * D
+        kx = torch.randn(T, HD, device=dev, generator=g).bfloat16()
+        vx = torch.randn(T, HD, device=dev, generator=g).bfloat16()
+        n = 4
+        dst = [(torch.empty(T, HD, device=dev, dtype=torch.uint8), torch.empty(T, HD, device=dev, dtype=torch.uint8),
+                torch.empty(T, device=dev), torch.empty(T, device=dev)) for _ in range(n)]
+        fn = lambda: kernels.kv_quant_publish(kx, vx, [d[0].data_ptr() for d in dst], [d[1].data_ptr() for d in dst],  # noqa: E731
+                                              [d[2].data_ptr() for d in dst], [d[3].data_ptr() for d in dst])
+        work = (2 * T * HD * 2 + n * 2 * (T * HD + 4 * T)) / 1e9
+        unit, bound = "GB/s", "hbm"
+        name = f"kv_quant_publish {T}x{HD} to {n} slots"
+    for _ in range(max(3, args.warmup)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    peaks, src = _peaks()
+    peak = peaks["bf16_tflops"] if bound == "tensor" else peaks["hbm_gbs"]
+    if args.kernel == "gemm":
+        peak *= 2  # dense FP8 peak = 2x bf16 (nominal ratio; measured peak is bf16 only)
+    ach = work / (ms * 1e-3)
+    print(json.dumps({"kernel": name, "ms": ms, "achieved": ach, "unit": unit, "peak": peak,
+                      "frac": ach / peak, "peak_source": src + (" bf16 burst x2" if args.kernel == "gemm" else ""),
+                      "status": L.status_take()}), flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel_bench(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         run_gpu_arm(args)

@@ -130,6 +130,37 @@ int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq, const flo
 int wf_rope_apply(const void* x, void* y, const float* cos_t, const float* sin_t, int64_t L, int H, int D,
                   int64_t x_tok_stride, int64_t y_tok_stride, void* stream);
 
+/* ------------------------------------- fused Wan-block row kernels */
+/* Caller-side epilogues around the hot path, one warp per token row, f32 math,
+ * bf16 in/out.  dim must be 256, 1536, 3072 or 5120.  Row r belongs to stage
+ * r / rows_per_stage, which selects that stage's modulation / RoPE table. */
+
+/* out = LayerNorm(x) * (1 + scale[s]) + shift[s]  (no affine, eps), the
+ * modulated norms of naive_rt/rolling_forcing/wan/modules/causal_model.py:375-377
+ * and :405-408.  shift/scale: f32 [stages, dim] with row stride mod_stride. */
+int wf_ln_modulate(const void* x, int64_t x_stride, const float* shift, const float* scale, int64_t mod_stride,
+                   void* out, int64_t out_stride, int64_t rows, int64_t dim, int64_t rows_per_stage, float eps,
+                   void* stream);
+
+/* x = bf16(x + y * gate[s]) in place, the gated residuals of
+ * causal_model.py:383 and :411-413 (gate of ones for the cross-attention add). */
+int wf_gate_residual(void* x, int64_t x_stride, const void* y, int64_t y_stride, const float* gate,
+                     int64_t gate_stride, int64_t rows, int64_t dim, int64_t rows_per_stage, void* stream);
+
+/* From the fused QKV GEMM output qkv [rows, ld] (q at column 0, k at dim):
+ * RMSNorm over dim (rounded to bf16, then times the bf16 weight, as
+ * naive_rt/rolling_forcing/wan/modules/model.py:70-88) followed by interleaved
+ * RoPE with per-stage f32 tables cos/sin [stages * rows_per_stage, head_dim/2]
+ * (wave_rt/runtime/backend.py:119-121).  Writes roped q, roped k, and the
+ * normalised un-roped k (k_unroped may be NULL), each [rows, dim] dense. */
+int wf_qk_norm_rope(const void* qkv, int64_t ld, const void* wq, const void* wk, const float* cos_t,
+                    const float* sin_t, int head_dim, void* q_out, void* k_out, void* k_unroped, int64_t rows,
+                    int64_t dim, int64_t rows_per_stage, float eps, void* stream);
+
+/* out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), model.py:70-88. */
+int wf_rms_norm(const void* x, int64_t x_stride, const void* w, void* out, int64_t out_stride, int64_t rows,
+                int64_t dim, float eps, void* stream);
+
 /* ------------------------------------------------ exchange primitives */
 
 /* IPC export of the allocation holding `p`; replaces ipc_export,

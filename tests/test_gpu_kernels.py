@@ -367,3 +367,49 @@ def test_ipc_export_offset():
     off0 = C.c_uint64()
     L.check(L.lib().wf_ipc_export(base.data_ptr(), h0, C.byref(off0)), "export")
     assert off.value - off0.value == 4096
+
+
+# ------------------------------------------------------- fused block rows
+@pytest.mark.parametrize("dim", [256, 1536, 5120])
+def test_fused_rows_match_torch(dim):
+    import torch.nn.functional as F
+
+    K = _kernels()
+    torch.manual_seed(dim)
+    S, T, hd = 3, 40, 128
+    x = torch.randn(S * T, dim, device=DEV).bfloat16()
+    e = torch.randn(S, 6, dim, device=DEV) * 0.3
+    # LayerNorm + modulation
+    out = K.ln_modulate(x, e[:, 0], e[:, 1], T, 1e-6)
+    ref = (F.layer_norm(x.float().view(S, T, dim), (dim,), eps=1e-6) * (1 + e[:, 1][:, None]) + e[:, 0][:, None])
+    assert (out.float().view(S, T, dim) - ref).abs().max().item() <= 0.02 * ref.abs().max().item()
+    # gated residual
+    y = torch.randn(S * T, dim, device=DEV).bfloat16()
+    ref = (x.float().view(S, T, dim) + y.float().view(S, T, dim) * e[:, 2][:, None]).bfloat16().float()
+    got = K.gate_residual(x.clone(), y, e[:, 2], T).float().view(S, T, dim)
+    assert (got - ref).abs().max().item() <= 0.01 * ref.abs().max().item()
+    # RMSNorm (q, k) + RoPE from a fused QKV matrix
+    qkv = torch.randn(S * T, 3 * dim, device=DEV).bfloat16()
+    wq = (torch.randn(dim, device=DEV) * 0.5 + 1).bfloat16()
+    wk = (torch.randn(dim, device=DEV) * 0.5 + 1).bfloat16()
+    cos = torch.rand(S * T, hd // 2, device=DEV) * 2 - 1
+    sin = torch.sqrt(1 - cos * cos)
+    q, k, ku = K.qk_norm_rope(qkv, dim, wq, wk, cos, sin, hd, T, 1e-6)
+
+    def rms(t, w):
+        tf = t.float()
+        return (tf * torch.rsqrt(tf.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16() * w
+
+    def rope(t):
+        t = t.float().view(S * T, dim // hd, hd // 2, 2)
+        re, im = t[..., 0], t[..., 1]
+        c, s = cos[:, None, :], sin[:, None, :]
+        return torch.stack([re * c - im * s, re * s + im * c], -1).view(S * T, dim)
+
+    kn = rms(qkv[:, dim:2 * dim], wk)
+    assert torch.equal(ku, kn)
+    for got, want in ((q, rope(rms(qkv[:, :dim], wq))), (k, rope(kn))):
+        assert (got.float() - want).abs().max().item() <= 0.01 * want.abs().max().item()
+    # plain RMSNorm
+    r = K.rms_norm(x, wq, 1e-6)
+    assert (r.float() - rms(x, wq).float()).abs().max().item() <= 0.01 * r.float().abs().max().item()

@@ -58,3 +58,19 @@ def test_no_bounded_wait_gave_up():
 
     _run("wf_b200", True, steps=(1000, 500), num_frames=9)
     assert L.status_take() == 0
+
+
+def test_fused_rows_match_torch_ops_pipeline():
+    """The libwfk row kernels (norms, modulation, residuals, RoPE) against the
+    same block math written as plain torch ops, through the whole wavefront."""
+    from waveforcing_b200.wavefront import dit
+
+    orig = dit.WanDiT.forward_stages
+    try:
+        dit.WanDiT.forward_stages = lambda self, tasks, layer_hook=None, fused=True: orig(self, tasks, layer_hook,
+                                                                                          fused=False)
+        b = _run("wf_b200", False)
+    finally:
+        dit.WanDiT.forward_stages = orig
+    a = _run("wf_b200", False)
+    assert _cos(a, b) >= 0.999

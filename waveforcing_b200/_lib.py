@@ -45,6 +45,10 @@ _SIGS = {
     "wf_act_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "wf_gemm_w8a8": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
     "wf_rope_apply": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i64, _vp]),
+    "wf_ln_modulate": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _f32, _vp]),
+    "wf_gate_residual": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "wf_qk_norm_rope": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),
+    "wf_rms_norm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),
     "wf_ipc_export": (_i32, [_vp, C.POINTER(C.c_uint8), C.POINTER(_u64)]),
     "wf_ipc_open": (_i32, [C.POINTER(C.c_uint8), C.POINTER(_vp)]),
     "wf_ipc_close": (_i32, [_vp]),

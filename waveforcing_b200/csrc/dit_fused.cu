@@ -1,0 +1,299 @@
+// Fused elementwise stages of the Wan block around the hot path (one warp
+// per token row, f32 math, bf16 in/out), replacing chains of 4-8 torch ops:
+//   wf_ln_modulate   out = LN(x) * (1 + scale[s]) + shift[s]
+//                    naive_rt/rolling_forcing/wan/modules/causal_model.py:375-377, 405-408
+//   wf_gate_residual x += y * gate[s]                       causal_model.py:383, 411-413
+//   wf_qk_norm_rope  q, k from the fused QKV GEMM output:  RMSNorm over dim
+//                    (model.py:70-88, rounding to bf16 before the weight as
+//                    .type_as(x) * weight does), then interleaved RoPE per head
+//                    (wave_rt/runtime/backend.py:119-121) with per-stage tables.
+// s = row / rows_per_stage selects the stage's modulation vector / RoPE table.
+#include <cuda_runtime.h>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace wfk {
+namespace fused {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+
+__device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// NCH = dim / 256 chunks of 8 elements per lane
+template <int NCH>
+__global__ void __launch_bounds__(256) ln_modulate_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs,
+                                                          const float* __restrict__ shift,
+                                                          const float* __restrict__ scale, int64_t mod_stride,
+                                                          __nv_bfloat16* __restrict__ out, int64_t os, int64_t rows,
+                                                          int64_t rows_per_stage, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  constexpr int DIM = NCH * 256;
+  float v[NCH][8];
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * xs);
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    unpack8(__ldg(xr + lane + 32 * c), v[c]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[c][i];
+  }
+  const float mean = warp_sum(s) * (1.f / DIM);
+  float q = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = v[c][i] - mean;
+      q = fmaf(d, d, q);
+    }
+  const float rstd = rsqrtf(warp_sum(q) * (1.f / DIM) + eps);
+  const int64_t st = r / rows_per_stage;
+  const float4* sh4 = reinterpret_cast<const float4*>(shift + st * mod_stride);
+  const float4* sc4 = reinterpret_cast<const float4*>(scale + st * mod_stride);
+  uint4* orow = reinterpret_cast<uint4*>(out + r * os);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int e = (lane + 32 * c) * 2;  // float4 index of this chunk's first element
+    const float4 a0 = __ldg(sc4 + e), a1 = __ldg(sc4 + e + 1);
+    const float4 b0 = __ldg(sh4 + e), b1 = __ldg(sh4 + e + 1);
+    const float sc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float sf[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = fmaf((v[c][i] - mean) * rstd, 1.f + sc[i], sf[i]);
+    orow[lane + 32 * c] = pack8(o);
+  }
+}
+
+// x[r] = bf16(x[r] + y[r] * gate[stage])   (f32 math)
+template <int NCH>
+__global__ void __launch_bounds__(256) gate_residual_kernel(__nv_bfloat16* __restrict__ x, int64_t xs,
+                                                            const __nv_bfloat16* __restrict__ y, int64_t ys,
+                                                            const float* __restrict__ gate, int64_t gate_stride,
+                                                            int64_t rows, int64_t rows_per_stage) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int64_t st = r / rows_per_stage;
+  uint4* xr = reinterpret_cast<uint4*>(x + r * xs);
+  const uint4* yr = reinterpret_cast<const uint4*>(y + r * ys);
+  const float4* g4 = reinterpret_cast<const float4*>(gate + st * gate_stride);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float a[8], b[8];
+    unpack8(xr[lane + 32 * c], a);
+    unpack8(__ldg(yr + lane + 32 * c), b);
+    const int e = (lane + 32 * c) * 2;
+    const float4 g0 = __ldg(g4 + e), g1 = __ldg(g4 + e + 1);
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = fmaf(b[i], g[i], a[i]);
+    xr[lane + 32 * c] = pack8(a);
+  }
+}
+
+// One warp per (token, q|k) row of the fused QKV output [rows, 3*dim].
+// Writes roped q, roped k, and the normalised un-roped k.
+template <int NCH>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld,
+                                                           const __nv_bfloat16* __restrict__ wq,
+                                                           const __nv_bfloat16* __restrict__ wk,
+                                                           const float* __restrict__ cos_t,
+                                                           const float* __restrict__ sin_t, int head_dim,
+                                                           __nv_bfloat16* __restrict__ q_out,
+                                                           __nv_bfloat16* __restrict__ k_out,
+                                                           __nv_bfloat16* __restrict__ k_unroped, int64_t rows,
+                                                           int64_t rows_per_stage, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (wid >= 2 * rows) return;
+  const int64_t r = wid >> 1;
+  const bool is_k = wid & 1;
+  constexpr int DIM = NCH * 256;
+  const uint4* src = reinterpret_cast<const uint4*>(qkv + r * ld + (is_k ? DIM : 0));
+  const uint4* w4 = reinterpret_cast<const uint4*>(is_k ? wk : wq);
+  float v[NCH][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    unpack8(__ldg(src + lane + 32 * c), v[c]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+  }
+  const float rn = rsqrtf(warp_sum(ss) * (1.f / DIM) + eps);
+  const int64_t tok = r % rows_per_stage;
+  const int64_t st = r / rows_per_stage;
+  const int half = head_dim / 2;
+  const float* ct = cos_t + (st * rows_per_stage + tok) * half;
+  const float* stab = sin_t + (st * rows_per_stage + tok) * half;
+  __nv_bfloat16* dst = (is_k ? k_out : q_out) + r * DIM;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int e0 = (lane + 32 * c) * 8;  // element index within the row
+    float w[8];
+    unpack8(__ldg(w4 + lane + 32 * c), w);
+    float n[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = bf(bf(v[c][i] * rn) * w[i]);
+    if (is_k && k_unroped) reinterpret_cast<uint4*>(k_unroped + r * DIM)[lane + 32 * c] = pack8(n);
+    const int pd = (e0 % head_dim) / 2;  // first complex pair of this chunk within the head
+    const float4 cv = *reinterpret_cast<const float4*>(ct + pd);
+    const float4 sv = *reinterpret_cast<const float4*>(stab + pd);
+    const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
+    float o[8];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float re = n[2 * p], im = n[2 * p + 1];
+      o[2 * p] = fmaf(re, cc[p], -im * sn[p]);
+      o[2 * p + 1] = fmaf(re, sn[p], im * cc[p]);
+    }
+    reinterpret_cast<uint4*>(dst)[lane + 32 * c] = pack8(o);
+  }
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs,
+                                                       const __nv_bfloat16* __restrict__ w,
+                                                       __nv_bfloat16* __restrict__ out, int64_t os, int64_t rows,
+                                                       float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  constexpr int DIM = NCH * 256;
+  const uint4* src = reinterpret_cast<const uint4*>(x + r * xs);
+  float v[NCH][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    unpack8(__ldg(src + lane + 32 * c), v[c]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+  }
+  const float rn = rsqrtf(warp_sum(ss) * (1.f / DIM) + eps);
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float wv[8], o[8];
+    unpack8(__ldg(w4 + lane + 32 * c), wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = bf(v[c][i] * rn) * wv[i];
+    reinterpret_cast<uint4*>(out + r * os)[lane + 32 * c] = pack8(o);
+  }
+}
+
+template <typename F>
+static int by_dim(int64_t dim, F&& f) {
+  switch (dim) {
+    case 256: f(std::integral_constant<int, 1>()); return WF_OK;
+    case 1536: f(std::integral_constant<int, 6>()); return WF_OK;
+    case 3072: f(std::integral_constant<int, 12>()); return WF_OK;
+    case 5120: f(std::integral_constant<int, 20>()); return WF_OK;
+    default: return fail(WF_ERR_UNSUPPORTED, "fused row kernels support dim 256/1536/3072/5120, got %lld",
+                         (long long)dim);
+  }
+}
+
+}  // namespace fused
+}  // namespace wfk
+
+using namespace wfk;
+using namespace wfk::fused;
+
+extern "C" int wf_ln_modulate(const void* x, int64_t x_stride, const float* shift, const float* scale,
+                              int64_t mod_stride, void* out, int64_t out_stride, int64_t rows, int64_t dim,
+                              int64_t rows_per_stage, float eps, void* stream) {
+  if (!x || !shift || !scale || !out || rows < 0 || rows_per_stage < 1 || !aligned16(x) || !aligned16(out) ||
+      !aligned16(shift) || !aligned16(scale) || x_stride % 8 || out_stride % 8 || mod_stride % 4)
+    return fail(WF_ERR_INVALID_ARG, "wf_ln_modulate: bad arguments");
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = by_dim(dim, [&](auto n) {
+    ln_modulate_kernel<decltype(n)::value><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), x_stride, shift, scale, mod_stride, static_cast<__nv_bfloat16*>(out),
+        out_stride, rows, rows_per_stage, eps);
+  });
+  if (rc != WF_OK) return rc;
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_gate_residual(void* x, int64_t x_stride, const void* y, int64_t y_stride, const float* gate,
+                                int64_t gate_stride, int64_t rows, int64_t dim, int64_t rows_per_stage,
+                                void* stream) {
+  if (!x || !y || !gate || rows < 0 || rows_per_stage < 1 || !aligned16(x) || !aligned16(y) || !aligned16(gate) ||
+      x_stride % 8 || y_stride % 8 || gate_stride % 4)
+    return fail(WF_ERR_INVALID_ARG, "wf_gate_residual: bad arguments");
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = by_dim(dim, [&](auto n) {
+    gate_residual_kernel<decltype(n)::value><<<blocks, 256, 0, s>>>(
+        static_cast<__nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(y), y_stride, gate,
+        gate_stride, rows, rows_per_stage);
+  });
+  if (rc != WF_OK) return rc;
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_qk_norm_rope(const void* qkv, int64_t ld, const void* wq, const void* wk, const float* cos_t,
+                               const float* sin_t, int head_dim, void* q_out, void* k_out, void* k_unroped,
+                               int64_t rows, int64_t dim, int64_t rows_per_stage, float eps, void* stream) {
+  if (!qkv || !wq || !wk || !cos_t || !sin_t || !q_out || !k_out || rows < 0 || rows_per_stage < 1 ||
+      head_dim < 8 || head_dim % 8 || dim % head_dim || ld % 8 || !aligned16(qkv) || !aligned16(q_out) ||
+      !aligned16(k_out) || !aligned16(cos_t) || !aligned16(sin_t) || (k_unroped && !aligned16(k_unroped)))
+    return fail(WF_ERR_INVALID_ARG, "wf_qk_norm_rope: bad arguments");
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((2 * rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = by_dim(dim, [&](auto n) {
+    qk_norm_rope_kernel<decltype(n)::value><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(qkv), ld, static_cast<const __nv_bfloat16*>(wq),
+        static_cast<const __nv_bfloat16*>(wk), cos_t, sin_t, head_dim, static_cast<__nv_bfloat16*>(q_out),
+        static_cast<__nv_bfloat16*>(k_out), static_cast<__nv_bfloat16*>(k_unroped), rows, rows_per_stage, eps);
+  });
+  if (rc != WF_OK) return rc;
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_rms_norm(const void* x, int64_t x_stride, const void* w, void* out, int64_t out_stride,
+                           int64_t rows, int64_t dim, float eps, void* stream) {
+  if (!x || !w || !out || rows < 0 || !aligned16(x) || !aligned16(w) || !aligned16(out) || x_stride % 8 ||
+      out_stride % 8)
+    return fail(WF_ERR_INVALID_ARG, "wf_rms_norm: bad arguments");
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = by_dim(dim, [&](auto n) {
+    rms_norm_kernel<decltype(n)::value><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), x_stride,
+                                                               static_cast<const __nv_bfloat16*>(w),
+                                                               static_cast<__nv_bfloat16*>(out), out_stride, rows,
+                                                               eps);
+  });
+  if (rc != WF_OK) return rc;
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}

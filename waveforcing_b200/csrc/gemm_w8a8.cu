@@ -23,7 +23,7 @@ constexpr int BK = 128;  // bytes (= elements for 8-bit types)
 constexpr int NS = 4;
 constexpr int A_TILE = BM * BK;  // 16 KB
 constexpr int B_TILE = BN * BK;  // 32 KB
-constexpr int NBARS = 2 * NS + 2;
+constexpr int NBARS = 2 * NS + 5;
 constexpr int SMEM_BYTES = 1024 + NS * (A_TILE + B_TILE) + NBARS * 8 + 16;
 constexpr int THREADS = 256;
 
@@ -38,6 +38,10 @@ __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, uint6
   return true;
 }
 
+// Persistent: CTA c processes output tiles c, c + gridDim.x, ... (tile t ->
+// m-tile t % m_tiles, n-tile t / m_tiles, so CTAs running together share the
+// same weight tile in L2).  The TMEM accumulator is double buffered: the MMA
+// warp fills buffer (i & 1) while the epilogue drains the other one.
 template <bool IS_INT8>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -51,13 +55,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + NS * B_TILE);
   uint64_t* full = bars;
   uint64_t* empty = bars + NS;
-  uint64_t* done = empty + NS;
-  uint64_t* fin = done + 1;
+  uint64_t* acc_full = empty + NS;  // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint64_t* fin = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int n_total = m_tiles * n_tiles;
   const int nk = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -65,13 +72,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     mbar_init(fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -83,57 +93,83 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
+      int it = 0;  // global k-block counter across tiles
       int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % NS;
-        if (kb >= NS && !mbar_wait(&empty[s], ((kb / NS) - 1) & 1, abort_flag, ST_GEMM_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full[s], A_TILE + B_TILE);
-        tma_load_2d(sA + s * A_TILE, &tmA, &full[s], kb * BK, m0);
-        tma_load_2d(sB + s * B_TILE, &tmB, &full[s], kb * BK, n0);
-        issued = kb + 1;
+      for (int t = blockIdx.x; t < n_total && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % NS;
+          if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, abort_flag, ST_GEMM_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full[s], A_TILE + B_TILE);
+          tma_load_2d(sA + s * A_TILE, &tmA, &full[s], kb * BK, m0);
+          tma_load_2d(sB + s * B_TILE, &tmB, &full[s], kb * BK, n0);
+          issued = it + 1;
+        }
       }
       if (*abort_flag)
-        for (int kb = (issued > NS ? issued - NS : 0); kb < issued; ++kb)
-          wait_drain(&full[kb % NS], (kb / NS) & 1, 200000000ull);
+        for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
+          wait_drain(&full[i % NS], (i / NS) & 1, 200000000ull);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = IS_INT8 ? make_idesc(2, FMT_S8, FMT_S8, 0, BM, BN)
                                          : make_idesc(1, FMT_E4M3, FMT_E4M3, 0, BM, BN);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % NS;
-        if (!mbar_wait(&full[s], (kb / NS) & 1, abort_flag, ST_GEMM_MMA)) break;
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_total; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        // the epilogue must have drained this accumulator (tile local-2)
+        if (local >= 2 && !mbar_wait(&acc_empty[buf], ((local >> 1) - 1) & 1, abort_flag, ST_GEMM_MMA)) break;
         tc_fence_after();
-        const uint32_t a = smem_u32(sA + s * A_TILE), b = smem_u32(sB + s * B_TILE);
+        const uint32_t d = tbase + buf * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % NS;
+          if (!mbar_wait(&full[s], (it / NS) & 1, abort_flag, ST_GEMM_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sA + s * A_TILE), b = smem_u32(sB + s * B_TILE);
 #pragma unroll
-        for (int kk = 0; kk < BK / 32; ++kk) {
-          const uint64_t da = desc_sw128(a + kk * 32, 16, 1024), db = desc_sw128(b + kk * 32, 16, 1024);
-          if constexpr (IS_INT8)
-            umma_i8_ss(tbase, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          else
-            umma_f8_ss(tbase, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t da = desc_sw128(a + kk * 32, 16, 1024), db = desc_sw128(b + kk * 32, 16, 1024);
+            if constexpr (IS_INT8)
+              umma_i8_ss(d, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            else
+              umma_f8_ss(d, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&acc_full[buf]);
       }
-      umma_commit(done);
       umma_commit(fin);
       wait_drain(fin, 0, 200000000ull);
     }
     __syncwarp();
   } else if (warp >= 4) {
     const int wq = warp - 4;
-    const int row = m0 + wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag, ST_GEMM_EPILOGUE, 20000000000ull));
-    if (ok) {
+    const float sw_t = per_token ? 0.f : __ldg(w_scale);
+    int local = 0;
+    for (int t = blockIdx.x; t < n_total; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const bool ok =
+          __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (local >> 1) & 1, abort_flag, ST_GEMM_EPILOGUE));
+      if (!ok) break;
       tc_fence_after();
+      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      const int row = m0 + wq * 32 + lane;
       const float sx = (row < M) ? (per_token ? __ldg(x_scale + row) : __ldg(x_scale)) : 0.f;
-      const float sw_t = per_token ? 0.f : __ldg(w_scale);
       __nv_bfloat16* yrow = y + static_cast<long long>(row) * y_stride;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
-        tmem_ld32x32b_x32(tbase + lane_off + c, r);
+        tmem_ld32x32b_x32(tbase + buf * BN + lane_off + c, r);
+        if (c + 32 == BN) {
+          // every column of this accumulator is in registers: hand it back
+          tc_fence_before();
+          mbar_arrive(&acc_empty[buf]);
+        }
         const int n = n0 + c;
         if (row < M && n < N) {
           float f[32];
@@ -152,7 +188,9 @@ __global__ void __launch_bounds__(THREADS, 1)
               d4[v] = make_uint4(pack_bf16x2(f[8 * v], f[8 * v + 1]), pack_bf16x2(f[8 * v + 2], f[8 * v + 3]),
                                  pack_bf16x2(f[8 * v + 4], f[8 * v + 5]), pack_bf16x2(f[8 * v + 6], f[8 * v + 7]));
           } else {
-            for (int i = 0; i < 32 && n + i < N; ++i) yrow[n + i] = __float2bfloat16_rn(f[i]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n + i < N) yrow[n + i] = __float2bfloat16_rn(f[i]);
           }
         }
       }
@@ -162,7 +200,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tbase, BN);
+    tmem_dealloc(tbase, 2 * BN);
   }
 }
 
@@ -290,7 +328,10 @@ extern "C" int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq
                                       SMEM_BYTES));
     configured_dev = dev;
   }
-  const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM);
+  const dim3 grid(tiles < sms ? tiles : sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int per_token = scale_mode == WF_SCALE_TOKEN;
   if (qtype == WF_DTYPE_S8)

@@ -109,6 +109,12 @@ __device__ __forceinline__ uint2 quant8(const uint4& v, const RowQuant& q) {
   return make_uint2(out[0], out[1]);
 }
 
+// 16 bf16 (two uint4) -> 16 codes (uint4)
+__device__ __forceinline__ uint4 quant16(const uint4& a, const uint4& b, const RowQuant& q) {
+  const uint2 lo = quant8(a, q), hi = quant8(b, q);
+  return make_uint4(lo.x, lo.y, hi.x, hi.y);
+}
+
 __device__ __forceinline__ float amax8(const uint4& v, float m) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -197,6 +203,46 @@ __global__ void __launch_bounds__(WARPS * 32)
   } else {
     row -= rows;
     quant_row<NCH>(v + row * v_stride, cols, lane, dv.codes, dv.scales, n_dst, row);
+  }
+}
+
+// Publish v2: NDST destinations known at compile time (pointer table stays in
+// parameter space), each lane owns 16 consecutive elements per chunk so every
+// destination receives 16-byte code stores, and warps loop over rows.
+// NCH16 = cols / 512.
+template <int NCH16, int NDST>
+__global__ void __launch_bounds__(WARPS * 32)
+    quant_publish16_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, int64_t rows,
+                           int64_t k_stride, int64_t v_stride, DstList dk, DstList dv) {
+  constexpr int64_t COLS = NCH16 * 512;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * WARPS;
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5); w < 2 * rows; w += nwarps) {
+    const bool is_v = w >= rows;
+    const int64_t row = is_v ? w - rows : w;
+    const uint4* x4 = reinterpret_cast<const uint4*>((is_v ? v : k) + row * (is_v ? v_stride : k_stride));
+    uint4 buf[2 * NCH16];
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCH16; ++i) {
+      buf[2 * i] = __ldcs(x4 + 2 * (lane + 32 * i));
+      buf[2 * i + 1] = __ldcs(x4 + 2 * (lane + 32 * i) + 1);
+      m = amax8(buf[2 * i], m);
+      m = amax8(buf[2 * i + 1], m);
+    }
+    m = warp_max_nan(m);
+    const RowQuant q = make_rowq(m);
+    const DstList& d = is_v ? dv : dk;
+#pragma unroll
+    for (int i = 0; i < NCH16; ++i) {
+      const uint4 c = quant16(buf[2 * i], buf[2 * i + 1], q);
+#pragma unroll
+      for (int j = 0; j < NDST; ++j) reinterpret_cast<uint4*>(d.codes[j] + row * COLS)[lane + 32 * i] = c;
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < NDST; ++j) d.scales[j][row] = q.s;
+    }
   }
 }
 
@@ -365,13 +411,49 @@ extern "C" int wf_kv_quant_publish(const void* k, const void* v, int64_t rows, i
     dv.scales[i] = dst_scales_v[i];
   }
   if (rows == 0) return WF_OK;
-  const unsigned blocks = static_cast<unsigned>((2 * rows + WARPS - 1) / WARPS);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dispatch_nch(cols, [&](auto nch) {
-    quant_publish_kernel<decltype(nch)::value><<<blocks, WARPS * 32, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), rows, cols, k_row_stride,
-        v_row_stride, dk, dv, n_dst);
-  });
+  bool aligned = true;
+  for (int i = 0; i < n_dst; ++i)
+    aligned = aligned && aligned16(dst_codes_k[i]) && aligned16(dst_codes_v[i]);
+  const int nch16 = (cols % 512 == 0) ? static_cast<int>(cols / 512) : 0;
+  if (aligned && (nch16 == 3 || nch16 == 6 || nch16 == 10)) {
+    const int64_t want = (2 * rows + WARPS - 1) / WARPS;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t cap = static_cast<int64_t>(sms) * 6;
+    const unsigned blocks = static_cast<unsigned>(want < cap ? want : cap);
+    auto go = [&](auto nch, auto nd) {
+      quant_publish16_kernel<decltype(nch)::value, decltype(nd)::value><<<blocks, WARPS * 32, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), rows, k_row_stride,
+          v_row_stride, dk, dv);
+    };
+    auto by_n = [&](auto nch) {
+      switch (n_dst) {
+        case 1: go(nch, std::integral_constant<int, 1>()); break;
+        case 2: go(nch, std::integral_constant<int, 2>()); break;
+        case 3: go(nch, std::integral_constant<int, 3>()); break;
+        case 4: go(nch, std::integral_constant<int, 4>()); break;
+        case 5: go(nch, std::integral_constant<int, 5>()); break;
+        case 6: go(nch, std::integral_constant<int, 6>()); break;
+        case 7: go(nch, std::integral_constant<int, 7>()); break;
+        default: go(nch, std::integral_constant<int, 8>()); break;
+      }
+    };
+    if (nch16 == 3)
+      by_n(std::integral_constant<int, 3>());
+    else if (nch16 == 6)
+      by_n(std::integral_constant<int, 6>());
+    else
+      by_n(std::integral_constant<int, 10>());
+  } else {
+    const unsigned blocks = static_cast<unsigned>((2 * rows + WARPS - 1) / WARPS);
+    dispatch_nch(cols, [&](auto nch) {
+      quant_publish_kernel<decltype(nch)::value><<<blocks, WARPS * 32, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), rows, cols, k_row_stride,
+          v_row_stride, dk, dv, n_dst);
+    });
+  }
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

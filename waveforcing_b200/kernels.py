@@ -172,3 +172,52 @@ def rope_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch
     L.check(L.lib().wf_rope_apply(x.data_ptr(), out.data_ptr(), cos.data_ptr(), sin.data_ptr(), Lt, H, D,
                                   x.stride(0), out.stride(0), _stream()), "wf_rope_apply")
     return out
+
+
+# ------------------------------------------------------ fused Wan-block rows
+def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_per_stage: int, eps: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = LN(x) * (1 + scale[s]) + shift[s]; x bf16 [rows, dim], shift/scale f32 [S, dim] row-strided."""
+    _need_cuda(x)
+    rows, dim = x.shape
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    L.check(L.lib().wf_ln_modulate(x.data_ptr(), x.stride(0), shift.data_ptr(), scale.data_ptr(), shift.stride(0),
+                                   out.data_ptr(), out.stride(0), rows, dim, rows_per_stage, eps, _stream()),
+            "wf_ln_modulate")
+    return out
+
+
+def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, rows_per_stage: int) -> torch.Tensor:
+    """x += y * gate[s] in place (f32 math, bf16 storage)."""
+    _need_cuda(x, y)
+    rows, dim = x.shape
+    gs = gate.stride(0) if gate.dim() == 2 else 0
+    L.check(L.lib().wf_gate_residual(x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), gate.data_ptr(), gs,
+                                     rows, dim, rows_per_stage, _stream()), "wf_gate_residual")
+    return x
+
+
+def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor, cos: torch.Tensor,
+                 sin: torch.Tensor, head_dim: int, rows_per_stage: int, eps: float, want_unroped: bool = True):
+    """Fused RMSNorm(q), RMSNorm(k) + RoPE from the fused QKV GEMM output.
+    Returns (roped q, roped k, normalised un-roped k or None), each [rows, dim]."""
+    _need_cuda(qkv)
+    rows = qkv.shape[0]
+    q = torch.empty((rows, dim), device=qkv.device, dtype=torch.bfloat16)
+    k = torch.empty_like(q)
+    ku = torch.empty_like(q) if want_unroped else None
+    L.check(L.lib().wf_qk_norm_rope(qkv.data_ptr(), qkv.stride(0), wq.data_ptr(), wk.data_ptr(), cos.data_ptr(),
+                                    sin.data_ptr(), head_dim, q.data_ptr(), k.data_ptr(),
+                                    ku.data_ptr() if ku is not None else None, rows, dim, rows_per_stage, eps,
+                                    _stream()), "wf_qk_norm_rope")
+    return q, k, ku
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    _need_cuda(x)
+    rows, dim = x.shape
+    out = torch.empty((rows, dim), device=x.device, dtype=torch.bfloat16)
+    L.check(L.lib().wf_rms_norm(x.data_ptr(), x.stride(0), w.data_ptr(), out.data_ptr(), out.stride(0), rows, dim,
+                                eps, _stream()), "wf_rms_norm")
+    return out

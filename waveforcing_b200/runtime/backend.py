@@ -71,7 +71,7 @@ def _torch_sdpa(q, k, v):
 
 def set_attention_timer(sink: list | None) -> None:
     """When ``sink`` is a list, every dispatched attention appends
-    (flops, start_event, end_event) recorded on the current stream."""
+    (flops, start_event, end_event, algorithmic_bytes) recorded on the current stream."""
     _WAVE_STATE["attn_timer"] = sink
 
 
@@ -89,5 +89,7 @@ def dispatch_attention(roped_query: torch.Tensor, ctx_k: torch.Tensor, ctx_v: to
     if sink is not None:
         e1.record()
         B, Lq, H, D = roped_query.shape
-        sink.append((4.0 * B * Lq * ctx_k.shape[1] * H * D, e0, e1))
+        Lk = ctx_k.shape[1]
+        nbytes = 2.0 * B * H * D * (2 * Lq + 2 * Lk)  # read Q, K, V and write O once (bf16)
+        sink.append((4.0 * B * Lq * Lk * H * D, e0, e1, nbytes))
     return out

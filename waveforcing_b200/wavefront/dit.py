@@ -242,9 +242,11 @@ class WanDiT(nn.Module):
         return x.reshape(cfg.out_ch, Fr, cfg.pph * p1, cfg.ppw * p2)
 
     @torch.no_grad()
-    def forward_stages(self, tasks: list[StageTask], layer_hook=None) -> list[torch.Tensor]:
+    def forward_stages(self, tasks: list[StageTask], layer_hook=None, fused: bool = True) -> list[torch.Tensor]:
         """Run every task's 30/40-layer forward, layer-interleaved.  Returns the
-        flow prediction of each task as [C, F, H, W] (f32)."""
+        flow prediction of each task as [C, F, H, W] (f32).  ``fused`` selects
+        the libwfk row kernels for norms/modulation/residuals/RoPE; False runs
+        the same math as plain torch ops (used by the tests as a cross-check)."""
         cfg = self.cfg
         dev = self.patch_embedding.weight.device
         dt = self.patch_embedding.weight.dtype
@@ -261,52 +263,83 @@ class WanDiT(nn.Module):
             heads_e.append(eh)
         mods = torch.stack(mods)  # [S, 6, dim] f32
         ropes = [rope_tables(cfg, cfg.frames_per_block, t.start_frame, dev) for t in tasks]
-        xs = x.view(S, T, dim)
+        cos_all = torch.cat([r[0] for r in ropes], 0).contiguous()
+        sin_all = torch.cat([r[1] for r in ropes], 0).contiguous()
+        ones = torch.ones(dim, device=dev, dtype=torch.float32)
+        eps = cfg.eps
+        xs = x.view(S * T, dim).contiguous()
+
+        def ln_mod(inp, e_all, k_shift):
+            if fused:
+                return kernels.ln_modulate(inp, e_all[:, k_shift], e_all[:, k_shift + 1], T, eps)
+            e = e_all.unbind(1)
+            h = F.layer_norm(inp.float().view(S, T, dim), (dim,), eps=eps)
+            return (h * (1 + e[k_shift + 1][:, None]) + e[k_shift][:, None]).to(dt).view(S * T, dim)
+
+        def gate_add(inp, y, gate_all, k):
+            if fused:
+                return kernels.gate_residual(inp, y, gate_all[:, k] if gate_all is not None else ones,
+                                             T if gate_all is not None else S * T)
+            g = gate_all[:, k][:, None] if gate_all is not None else ones
+            return (inp.float().view(S, T, dim) + y.float().view(S, T, dim) * g).to(dt).view(S * T, dim)
+
         for li, b in enumerate(self.blocks):
-            e = (b.modulation.float() + mods).unbind(1)  # 6 x [S, dim]
-            h = F.layer_norm(xs.float(), (dim,), eps=cfg.eps)
-            h = (h * (1 + e[1][:, None]) + e[0][:, None]).to(dt).view(S * T, dim)
+            e_all = (b.modulation.float() + mods).contiguous()  # [S, 6, dim]
+            h = ln_mod(xs, e_all, 0)
             fq = self._fused_qkv(b)
-            if fq is not None:
+            if fused and fq is not None:
                 qkv = F.linear(h, fq[0], fq[1])
-                q, k, v = qkv[:, :dim], qkv[:, dim:2 * dim], qkv[:, 2 * dim:]
+                rq_all, rk_all, ku_all = kernels.qk_norm_rope(qkv, dim, b.self_attn.norm_q.weight,
+                                                              b.self_attn.norm_k.weight, cos_all, sin_all, D, T, eps)
+                v = qkv[:, 2 * dim:].reshape(S, T, H, D)
+                rq_all, rk_all, ku_all = (t.view(S, T, H, D) for t in (rq_all, rk_all, ku_all))
             else:
-                q, k, v = _lin(b.self_attn.q, h), _lin(b.self_attn.k, h), _lin(b.self_attn.v, h)
-            q = b.self_attn.norm_q(q).view(S, T, H, D)
-            k = b.self_attn.norm_k(k).view(S, T, H, D)
-            v = v.reshape(S, T, H, D)
+                if fq is not None:
+                    qkv = F.linear(h, fq[0], fq[1])
+                    q, k, v = qkv[:, :dim], qkv[:, dim:2 * dim], qkv[:, 2 * dim:]
+                else:
+                    q, k, v = _lin(b.self_attn.q, h), _lin(b.self_attn.k, h), _lin(b.self_attn.v, h)
+                q = b.self_attn.norm_q(q).view(S, T, H, D)
+                ku_all = b.self_attn.norm_k(k).view(S, T, H, D)
+                v = v.reshape(S, T, H, D)
+                rq_all = torch.stack([kernels.rope_apply(q[i], *ropes[i]) for i in range(S)])
+                rk_all = torch.stack([kernels.rope_apply(ku_all[i], *ropes[i]) for i in range(S)])
             o = torch.empty((S, T, H, D), device=dev, dtype=dt)
             for i in order:
-                cos, sin = ropes[i]
-                rq = kernels.rope_apply(q[i], cos, sin)
-                rk = kernels.rope_apply(k[i], cos, sin)
                 tk = tasks[i]
+                rq, rk = rq_all[i], rk_all[i]
                 if tk.exch is not None:
-                    K, V = tk.exch(layer_idx=li, roped_query=rq[None], roped_key=rk[None], unroped_key=k[i][None],
-                                   value=v[i][None], current_start=tk.start_frame * cfg.tokens_per_frame,
+                    K, V = tk.exch(layer_idx=li, roped_query=rq[None], roped_key=rk[None],
+                                   unroped_key=ku_all[i][None], value=v[i][None],
+                                   current_start=tk.start_frame * cfg.tokens_per_frame,
                                    tokens_per_frame=cfg.tokens_per_frame, post_patch_height=cfg.pph,
                                    post_patch_width=cfg.ppw, dim=dim, rope_num_heads=H,
                                    num_frames_per_block=cfg.frames_per_block)
                 else:
                     K, V = rk[None], v[i][None]
                 o[i] = dispatch_attention(rq[None], K, V)[0]
-            y = _lin(b.self_attn.o, o.view(S * T, dim)).view(S, T, dim)
-            xs = (xs.float() + y.float() * e[2][:, None]).to(dt)
+            y = _lin(b.self_attn.o, o.view(S * T, dim))
+            xs = gate_add(xs, y, e_all, 2)
             # cross-attention: all stages share the text K/V -> one call
-            qc = b.cross_attn.norm_q(_lin(b.cross_attn.q, xs.view(S * T, dim))).view(1, S * T, H, D)
+            qc = _lin(b.cross_attn.q, xs)
+            qc = (kernels.rms_norm(qc, b.cross_attn.norm_q.weight, eps) if fused
+                  else b.cross_attn.norm_q(qc)).view(1, S * T, H, D)
             kc, vc = self._cross_kv[li]
             oc = dispatch_attention(qc, kc, vc)
-            xs = xs + _lin(b.cross_attn.o, oc.view(S * T, dim)).view(S, T, dim)
-            h = F.layer_norm(xs.float(), (dim,), eps=cfg.eps)
-            h = (h * (1 + e[4][:, None]) + e[3][:, None]).to(dt).view(S * T, dim)
-            y = _lin(b.ffn.fc_out, F.gelu(_lin(b.ffn.fc_in, h), approximate="tanh")).view(S, T, dim)
-            xs = (xs.float() + y.float() * e[5][:, None]).to(dt)
+            xs = gate_add(xs, _lin(b.cross_attn.o, oc.view(S * T, dim)), None, 0)
+            h = ln_mod(xs, e_all, 3)
+            fi = b.ffn.fc_in
+            if fused and type(fi) is nn.Linear:
+                a = torch._addmm_activation(fi.bias, h, fi.weight.t(), use_gelu=True)  # cuBLASLt bias+GELU(tanh)
+            else:
+                a = F.gelu(_lin(fi, h), approximate="tanh")
+            y = _lin(b.ffn.fc_out, a)
+            xs = gate_add(xs, y, e_all, 5)
             if layer_hook is not None:
                 layer_hook(li)
-        eh = (self.head_norm_mod.float() + torch.stack(heads_e)).unbind(1)  # 2 x [S, dim]
-        h = F.layer_norm(xs.float(), (dim,), eps=cfg.eps)
-        h = (h * (1 + eh[1][:, None]) + eh[0][:, None]).to(dt)
-        out = _lin(self.head, h.view(S * T, dim)).view(S, T, -1)
+        eh = (self.head_norm_mod.float() + torch.stack(heads_e)).contiguous()  # [S, 2, dim]
+        h = ln_mod(xs, eh, 0)
+        out = _lin(self.head, h).view(S, T, -1)
         return [self.unpatchify(out[i].float(), cfg.frames_per_block) for i in range(S)]
 
 
