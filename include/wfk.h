@@ -67,6 +67,12 @@ int wf_attn_fwd(const void* q, const void* k, const void* v, void* o, int batch,
                 const int64_t* o_stride, int kv_dtype, const float* k_scale, const float* v_scale,
                 int scale_mode, float softmax_scale, void* stream);
 
+/* Diagnostic (no counterpart in the reference): evaluates the attention
+ * softmax's two exponential paths on x[n] -- the FMA-pipe polynomial
+ * (y_poly) and the MUFU ex2.approx (y_mufu) -- so their error bounds can be
+ * tested against exp2. */
+int wf_selftest_exp2(const float* x, float* y_poly, float* y_mufu, int n, void* stream);
+
 /* ------------------------------------------------------- FP8 K/V codec */
 
 /* Quantise a bf16 [rows, cols] matrix (row stride x_row_stride) to e4m3fn

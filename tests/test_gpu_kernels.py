@@ -413,3 +413,26 @@ def test_fused_rows_match_torch(dim):
     # plain RMSNorm
     r = K.rms_norm(x, wq, 1e-6)
     assert (r.float() - rms(x, wq).float()).abs().max().item() <= 0.01 * r.float().abs().max().item()
+
+
+def test_softmax_exp2_paths_error_bounds():
+    """The FMA-pipe polynomial 2^x used for part of the softmax stays within
+    1e-4 relative error of exp2 on the range the kernel feeds it ([-125, 8]),
+    the same order as the MUFU ex2.approx path it replaces."""
+    from waveforcing_b200 import _lib as L
+
+    x = torch.cat([torch.linspace(-125.0, 8.0, 400001, device=DEV), torch.tensor([-0.5, 0.5, 0.0, 7.99], device=DEV)])
+    yp = torch.empty_like(x)
+    ym = torch.empty_like(x)
+    L.check(L.lib().wf_selftest_exp2(x.data_ptr(), yp.data_ptr(), ym.data_ptr(), x.numel(),
+                                     torch.cuda.current_stream().cuda_stream), "wf_selftest_exp2")
+    ref = torch.exp2(x.double())
+    rel_p = ((yp.double() - ref).abs() / ref).max().item()
+    rel_m = ((ym.double() - ref).abs() / ref).max().item()
+    assert rel_p < 1e-4, rel_p
+    assert rel_m < 1e-4, rel_m
+    # masked scores (-inf) map to a tiny positive normal value, not NaN
+    z = torch.tensor([float("-inf"), -1000.0], device=DEV)
+    L.check(L.lib().wf_selftest_exp2(z.data_ptr(), yp.data_ptr(), ym.data_ptr(), 2,
+                                     torch.cuda.current_stream().cuda_stream), "wf_selftest_exp2")
+    assert torch.all(yp[:2] >= 0) and torch.all(yp[:2] < 1e-37)

@@ -215,16 +215,27 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_new = mx2;
         grow = true;
       }
-      const float neg_m = -m_new;
-      float sum = 0.f;
+      // P = 2^(s * scale_log2 - m): pairs through packed f32x2 FMAs; 3 of
+      // every 8 pairs take the FMA-pipe polynomial, the rest MUFU ex2, so the
+      // two pipes finish together and the softmax stays shorter than the MMAs
+      const float2 sc2 = make_float2(scale_log2, scale_log2);
+      const float2 nm2 = make_float2(-m_new, -m_new);
+      float2 sum2 = make_float2(0.f, 0.f);
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int i = 0; i < BN / 2; ++i) {
-        const float p0 = ex2_approx(fmaf(s[2 * i], scale_log2, neg_m));
-        const float p1 = ex2_approx(fmaf(s[2 * i + 1], scale_log2, neg_m));
-        sum += p0 + p1;
-        pk[i] = pack_bf16x2(p0, p1);
+        const float2 x = ffma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
+        float2 pr;
+        if ((i & 7) < 3) {
+          pr = exp2_poly2(x);
+        } else {
+          pr.x = ex2_approx(x.x);
+          pr.y = ex2_approx(x.y);
+        }
+        sum2 = fadd2(sum2, pr);
+        pk[i] = pack_bf16x2(pr.x, pr.y);
       }
+      const float sum = sum2.x + sum2.y;
       const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
       if (__any_sync(0xffffffffu, grow)) {
         // O may only be touched once PV_{j-1} has completed.
@@ -339,6 +350,34 @@ extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o,
   attn_fwd_bf16_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
       tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
       (long long)o_stride[0], Lq, Lk, scale_log2);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+namespace wfk {
+namespace attn {
+__global__ void exp2_selftest_kernel(const float* __restrict__ x, float* __restrict__ y_poly,
+                                     float* __restrict__ y_mufu, int n) {
+  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i + 1 >= n + 1) return;
+  const float2 in = make_float2(x[i], i + 1 < n ? x[i + 1] : 0.f);
+  const float2 p = exp2_poly2(in);
+  y_poly[i] = p.x;
+  y_mufu[i] = ex2_approx(in.x);
+  if (i + 1 < n) {
+    y_poly[i + 1] = p.y;
+    y_mufu[i + 1] = ex2_approx(in.y);
+  }
+}
+}  // namespace attn
+}  // namespace wfk
+
+extern "C" int wf_selftest_exp2(const float* x, float* y_poly, float* y_mufu, int n, void* stream) {
+  if (!x || !y_poly || !y_mufu || n < 0) return wfk::fail(WF_ERR_INVALID_ARG, "wf_selftest_exp2: bad arguments");
+  if (n == 0) return WF_OK;
+  const int pairs = (n + 1) / 2;
+  wfk::attn::exp2_selftest_kernel<<<(pairs + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y_poly,
+                                                                                                      y_mufu, n);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

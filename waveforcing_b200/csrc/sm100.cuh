@@ -195,6 +195,53 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// ------------------------------------------------ packed f32x2 arithmetic
+// Blackwell executes two f32 FMAs/adds per instruction on .b64 register pairs.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for a pair, on the FMA pipe: Cody-Waite split x = j + f with j = rint(x)
+// (magic-constant rounding), f in [-0.5, 0.5]; 2^f from a degree-3 polynomial
+// fitted here for minimax relative error on that interval (max rel. error
+// 7.5e-5, far below the bf16 rounding of P); 2^j is added to the exponent
+// field.  Inputs are clamped at -125 so the result stays a normal float
+// (2^-125 stands in for exp2 of masked, -inf, scores whose V rows are zero).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = fadd2(x, make_float2(kMagic, kMagic));
+  const float2 j = fadd2(t, make_float2(-kMagic, -kMagic));
+  const float2 f = ffma2(j, make_float2(-1.f, -1.f), x);
+  float2 p = ffma2(f, make_float2(0.055171627551317215f, 0.055171627551317215f),
+                   make_float2(0.2426111400127411f, 0.2426111400127411f));
+  p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  // (t_bits - magic_bits) = j; magic_bits << 23 vanishes mod 2^32
+  p.x = __uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23));
+  p.y = __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23));
+  return p;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

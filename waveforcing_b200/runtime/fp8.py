@@ -73,6 +73,26 @@ class WfW8A8Linear(nn.Module):
         return y.reshape(*shape[:-1], self.out_features), None
 
 
+def concat_w8a8(mods: list["WfW8A8Linear"]) -> "WfW8A8Linear":
+    """One W8A8 linear whose output is the concatenation of ``mods``' outputs
+    (shared input, per-channel scales): q/k/v become one GEMM on one
+    activation quantisation."""
+    a = mods[0]
+    if any(m.granularity != "channel" or m.qtype != a.qtype for m in mods):
+        raise ValueError("only per-channel W8A8 linears of one qtype concatenate")
+    out = WfW8A8Linear.__new__(WfW8A8Linear)
+    nn.Module.__init__(out)
+    out.qtype, out.granularity, out.out_dtype = a.qtype, "channel", a.out_dtype
+    out.in_features = a.in_features
+    out.out_features = sum(m.out_features for m in mods)
+    out.register_buffer("w_q", torch.cat([m.w_q for m in mods], 0).contiguous())
+    out.register_buffer("w_scale", torch.cat([m.w_scale for m in mods], 0).contiguous())
+    biases = [m.bias for m in mods]
+    out.register_buffer("bias", torch.cat(biases, 0).contiguous() if all(b is not None for b in biases) else None)
+    out._ws = None
+    return out
+
+
 _TARGET_SUFFIXES = ("ffn.fc_in", "ffn.fc_out")
 
 

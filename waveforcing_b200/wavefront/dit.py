@@ -219,13 +219,28 @@ class WanDiT(nn.Module):
         return e0, e.float().view(1, self.cfg.dim)
 
     def _fused_qkv(self, b: Block):
+        """One GEMM for q, k, v: concatenated bf16 weights, or one concatenated
+        per-channel W8A8 linear (a single activation quantisation)."""
         a = b.self_attn
-        if not all(type(m) is nn.Linear for m in (a.q, a.k, a.v)):
-            return None
         if b._wqkv is None:
-            b._wqkv = torch.cat([a.q.weight, a.k.weight, a.v.weight], 0).contiguous()
-            b._bqkv = torch.cat([a.q.bias, a.k.bias, a.v.bias], 0).contiguous()
+            if all(type(m) is nn.Linear for m in (a.q, a.k, a.v)):
+                b._wqkv = torch.cat([a.q.weight, a.k.weight, a.v.weight], 0).contiguous()
+                b._bqkv = torch.cat([a.q.bias, a.k.bias, a.v.bias], 0).contiguous()
+            else:
+                from waveforcing_b200.runtime.fp8 import WfW8A8Linear, concat_w8a8
+
+                if all(isinstance(m, WfW8A8Linear) and m.granularity == "channel" for m in (a.q, a.k, a.v)):
+                    b._wqkv = concat_w8a8([a.q, a.k, a.v])
+                else:
+                    return None
         return b._wqkv, b._bqkv
+
+    @staticmethod
+    def _qkv_gemm(fq, h):
+        w, bias = fq
+        if isinstance(w, torch.Tensor):
+            return F.linear(h, w, bias)
+        return _lin(w, h)
 
     # ----------------------------------------------------------------- forward
     def patchify(self, latent: torch.Tensor) -> torch.Tensor:
@@ -288,14 +303,14 @@ class WanDiT(nn.Module):
             h = ln_mod(xs, e_all, 0)
             fq = self._fused_qkv(b)
             if fused and fq is not None:
-                qkv = F.linear(h, fq[0], fq[1])
+                qkv = self._qkv_gemm(fq, h)
                 rq_all, rk_all, ku_all = kernels.qk_norm_rope(qkv, dim, b.self_attn.norm_q.weight,
                                                               b.self_attn.norm_k.weight, cos_all, sin_all, D, T, eps)
                 v = qkv[:, 2 * dim:].reshape(S, T, H, D)
                 rq_all, rk_all, ku_all = (t.view(S, T, H, D) for t in (rq_all, rk_all, ku_all))
             else:
                 if fq is not None:
-                    qkv = F.linear(h, fq[0], fq[1])
+                    qkv = self._qkv_gemm(fq, h)
                     q, k, v = qkv[:, :dim], qkv[:, dim:2 * dim], qkv[:, 2 * dim:]
                 else:
                     q, k, v = _lin(b.self_attn.q, h), _lin(b.self_attn.k, h), _lin(b.self_attn.v, h)
