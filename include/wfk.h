@@ -86,6 +86,24 @@ int wf_selftest_exp2(const float* x, float* y_poly, float* y_mufu, int n, void* 
 int wf_kv_quant(const void* x, uint8_t* codes, float* scales, int64_t rows, int64_t cols, int64_t x_row_stride,
                 int mode, void* workspace, void* stream);
 
+/* Allocation-free form of wf_kv_quant(..., WF_SCALE_TENSOR, ...).  It has no
+ * counterpart in the reference.  It exists for callers that cannot allocate
+ * device memory where they quantise: hosts reaching this library through a C
+ * FFI with no CUDA allocator of their own, processes whose device memory is
+ * already reserved by a framework's caching allocator (a raw cudaMalloc can
+ * fail there), and per-layer loops that must not pay cudaMalloc's implicit
+ * synchronisation.  Its grid-wide amax scratch is a fixed 16 KB device array
+ * inside libwfk (4096 partial maxima), which every GPU that loads the library
+ * holds until the process exits; it calls no cudaMalloc, cudaFree or
+ * allocating library routine.  Limit: rows * cols <= 33,554,432 elements
+ * (4096 x 8192); larger inputs are rejected with WF_ERR_INVALID_ARG.  The first
+ * call on a device resolves the array's device address (cudaGetSymbolAddress
+ * with that device current); make that first call before any stream capture.
+ * All calls on a device share the array: calls whose kernels overlap on the
+ * GPU race.  Codes and scale are bit-identical to wf_kv_quant's. */
+int wf_kv_quant_tensor_static(const void* x, uint8_t* codes, float* scale, int64_t rows, int64_t cols,
+                              int64_t x_row_stride, void* stream);
+
 /* Dequantise codes [rows, cols] to bf16 out (row stride out_row_stride):
  * out = bf16(e4m3(code) * scale), the receive side of
  * wave_rt/denoiser/exchange/common.py:162 and onesided.py:177-179

@@ -39,6 +39,7 @@ _SIGS = {
                            _vp, _vp, _i32, _f32, _vp]),
     "wf_selftest_exp2": (_i32, [_vp, _vp, _vp, _i32, _vp]),
     "wf_kv_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp]),
+    "wf_kv_quant_tensor_static": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "wf_kv_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "wf_kv_quant_publish": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, C.POINTER(_vp), C.POINTER(_vp),
                                    C.POINTER(_vp), C.POINTER(_vp), _i32, _vp]),

@@ -17,6 +17,8 @@
 //    non-saturating RNE agree; non-finite rows use the exact software encoder.
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "host_util.h"
 #include "sm100.cuh"
 
@@ -454,6 +456,127 @@ extern "C" int wf_kv_quant_publish(const void* k, const void* v, int64_t rows, i
           v_row_stride, dk, dv, n_dst);
     });
   }
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+// ------------------------------------------------ allocation-free variant
+// wf_kv_quant_tensor_static: the per-tensor quantiser with its grid-wide
+// reduction scratch in this file-scope device array instead of caller memory.
+// The amax pass writes one partial maximum per block of NOALLOC_SPAN
+// elements; the quantise pass reduces those partials.  Every partial the
+// second pass reads is written earlier by the same call, so nothing has to be
+// cleared between calls, and slots beyond the current call's block count
+// (left over from an earlier, larger call) are never read.  All calls on a
+// device share the array: two calls whose kernels overlap on the GPU (for
+// example on different streams) race and must be serialised by the caller.
+namespace wfk {
+namespace codec {
+
+constexpr int NOALLOC_PARTIALS = 4096;                                 // 16 KB per GPU
+constexpr int64_t NOALLOC_SPAN = 8192;                                 // elements per partial
+constexpr int64_t NOALLOC_MAX_ELEMS = NOALLOC_PARTIALS * NOALLOC_SPAN;  // 33,554,432
+static __device__ __align__(256) float g_noalloc_partials[NOALLOC_PARTIALS];
+
+// block b reduces chunks [b * 1024, (b + 1) * 1024) of 8 elements
+__global__ void __launch_bounds__(256) amax_partials_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                            int64_t cols, int64_t row_stride,
+                                                            float* __restrict__ partials) {
+  const int64_t nch = cols / 8;
+  const int64_t total = rows * nch;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (NOALLOC_SPAN / 8);
+  float m = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int64_t i = base + threadIdx.x + 256 * k;
+    if (i < total) {
+      const int64_t r = i / nch, c = i - r * nch;
+      m = amax8(__ldg(reinterpret_cast<const uint4*>(x + r * row_stride) + c), m);
+    }
+  }
+  m = warp_max_nan(m);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    m = warp_max_nan(m);
+    if (threadIdx.x == 0) partials[blockIdx.x] = m;
+  }
+}
+
+__global__ void __launch_bounds__(256) quant_from_partials_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                  int64_t rows, int64_t cols, int64_t row_stride,
+                                                                  const float* __restrict__ partials,
+                                                                  int nparts, uint8_t* __restrict__ codes,
+                                                                  float* __restrict__ scale_out) {
+  __shared__ float red[8];
+  float m = 0.f;
+  for (int i = threadIdx.x; i < nparts; i += 256) {
+    const float p = partials[i];
+    m = (p > m || p != p) ? p : m;
+  }
+  m = warp_max_nan(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red[0];
+  for (int w = 1; w < 8; ++w) m = (red[w] > m || red[w] != red[w]) ? red[w] : m;
+  const RowQuant q = make_rowq(m);
+  const int64_t nch = cols / 8;
+  const int64_t total = rows * nch;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / nch, c = i - r * nch;
+    const uint2 cc = quant8(__ldg(reinterpret_cast<const uint4*>(x + r * row_stride) + c), q);
+    reinterpret_cast<uint2*>(codes + r * cols)[c] = cc;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = q.s;
+}
+
+// Device address of g_noalloc_partials per device ordinal, resolved on the
+// first call made with that device current.
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[256] = {};
+
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  WFK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 256) return fail(WF_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || !p)
+      return fail(WF_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return WF_OK;
+}
+
+}  // namespace codec
+}  // namespace wfk
+
+extern "C" int wf_kv_quant_tensor_static(const void* x, uint8_t* codes, float* scale, int64_t rows, int64_t cols,
+                                         int64_t x_row_stride, void* stream) {
+  if (!rows_ok(x, rows, cols, x_row_stride) || !codes || !scale || (reinterpret_cast<uintptr_t>(codes) & 7))
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_quant_tensor_static: bad arguments (cols %% 8, 16-byte x, 8-byte codes)");
+  if (rows * cols > NOALLOC_MAX_ELEMS)
+    return fail(WF_ERR_INVALID_ARG,
+                "wf_kv_quant_tensor_static: %lld elements exceed the static scratch limit of %lld "
+                "(4096 partial maxima of 8192 elements); use wf_kv_quant with a workspace",
+                (long long)(rows * cols), (long long)NOALLOC_MAX_ELEMS);
+  if (rows == 0) return WF_OK;
+  float* partials = nullptr;
+  int rc = noalloc_scratch(&partials);
+  if (rc != WF_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nparts = static_cast<int>((rows * cols + NOALLOC_SPAN - 1) / NOALLOC_SPAN);
+  amax_partials_kernel<<<nparts, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride,
+                                              partials);
+  const int g = grid_for(rows * (cols / 8), 256);
+  quant_from_partials_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride,
+                                               partials, nparts, codes, scale);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }
