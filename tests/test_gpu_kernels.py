@@ -47,7 +47,7 @@ def _f32(t):
 # ------------------------------------------------------------------ attention
 ATTN_CASES = [
     (128, 128, 1), (130, 300, 2), (5, 517, 3), (257, 1000, 2), (64, 64, 2), (1, 1, 1),
-    (300, 129, 4), (4680, 4680, 1),
+    (300, 129, 4), (4680, 4680, 1), (200, 700, 40),
 ]
 
 
@@ -253,7 +253,8 @@ def test_quantisers_bit_exact(qtype):
 
 
 @pytest.mark.parametrize("qtype", ["e4m3", "s8"])
-@pytest.mark.parametrize("M,N,K_", [(128, 256, 128), (300, 512, 384), (4680, 1536, 1536), (77, 96, 256)])
+@pytest.mark.parametrize("M,N,K_", [(128, 256, 128), (300, 512, 384), (4680, 1536, 1536), (77, 96, 256),
+                                    (500, 13824, 5120), (300, 5120, 13824)])
 def test_gemm_w8a8_matches_oracle(qtype, M, N, K_):
     K = _kernels()
     from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
