@@ -261,13 +261,18 @@ def run_gpu_arm(args):
     if sampler:
         sampler.start()
     attn_sink: list = []
+    wait_sink: list = []
     backend.set_attention_timer(attn_sink)
+    eng.xport.wait_timer = wait_sink
     launches0 = kernels.LAUNCHES[0]
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    host_ms = []
     evs[0].record()
     torch.cuda.nvtx.range_push("timed")
     for i in range(args.steps):
+        h0 = time.perf_counter()
         eng.tick(fill + args.warmup + i)
+        host_ms.append((time.perf_counter() - h0) * 1e3)
         evs[i + 1].record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -285,6 +290,13 @@ def run_gpu_arm(args):
     a_ms = sum(x[1].elapsed_time(x[2]) for x in attn_sink)
     n_attn = len(attn_sink)
     a_bytes = sum(x[3] for x in attn_sink) / max(1, n_attn)
+    eng.xport.wait_timer = None
+    # exposed exchange: device time this rank's compute stream spent in remote flag waits
+    wait_ms_rank = sum(e0.elapsed_time(e1) for e0, e1 in wait_sink) / args.steps
+    wait_ms = max_over_ranks([wait_ms_rank])[0]
+    # the critical rank hosts stage 0 (the longest K/V context): its waits are the exposed exchange
+    crit = max_over_ranks([wait_ms_rank if 0 in eng.local else 0.0])[0]
+    host_p50 = max_over_ranks([statistics.median(host_ms)])[0]
     eng.close()
     del eng
     torch.cuda.empty_cache()
@@ -362,6 +374,12 @@ def run_gpu_arm(args):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "dit_fps": dit,
+            "exchange": {"critical_rank_wait_ms_per_tick": crit,
+                         "critical_frac_of_tick": crit / p50 if p50 else None,
+                         "max_rank_wait_ms_per_tick": wait_ms,
+                         "note": "device time consumer streams spent in bounded flag waits for remote K/V; "
+                                 "the critical rank hosts stage 0, lighter ranks wait for slower producers"},
+            "host_issue_ms_per_tick_p50": host_p50,
             "gpu_launches": launches,
             "clocks": clocks,
         }

@@ -112,6 +112,9 @@ class PagedTransport:
             self.store_buf = (torch.zeros((cap, H, D), device=self.device, dtype=dtype),
                               torch.zeros((cap, H, D), device=self.device, dtype=dtype))
         self.timeout_word = torch.zeros(1, device=self.device, dtype=torch.int32)
+        # when a list, every remote flag wait appends its (start, end) CUDA events:
+        # the exposed part of the exchange on this rank's compute stream
+        self.wait_timer = None
         # destination tables: consumer stage -> dict of base pointers (local or peer)
         self.dst: dict = {}
         self._exchange_handles()
@@ -240,8 +243,16 @@ class PagedTransport:
             return  # same GPU: the publish precedes this read on the stream
         i = self.src_index[m][src]
         addr = self.flags[m][i, gen, layer].data_ptr()
-        ipc.wait_flag_bounded(torch.cuda.current_stream(self.device).cuda_stream, addr, tick, self.timeout_s,
-                              self.timeout_word.data_ptr())
+        cur = torch.cuda.current_stream(self.device)
+        sink = self.wait_timer
+        if sink is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+        ipc.wait_flag_bounded(cur.cuda_stream, addr, tick, self.timeout_s, self.timeout_word.data_ptr())
+        if sink is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(cur)
+            sink.append((e0, e1))
 
     def drain(self) -> None:
         """onesided.py:181-187: order later work after this tick's publications."""

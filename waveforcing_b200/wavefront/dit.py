@@ -212,11 +212,20 @@ class WanDiT(nn.Module):
         self._cross_kv = kv
 
     def time_mod(self, timestep: float, device):
-        """Per-stage modulation inputs: e [6, dim] f32 and e_head [2, dim] f32."""
-        t = torch.tensor([timestep], device=device)
-        e = self.time_embedding(sinusoidal_embedding_1d(self.cfg.freq_dim, t).to(self.patch_embedding.weight.dtype))
-        e0 = self.time_projection(e).float().view(6, self.cfg.dim)
-        return e0, e.float().view(1, self.cfg.dim)
+        """Per-stage modulation inputs: e [6, dim] f32 and e_head [2, dim] f32.
+
+        Cached per timestep value: a wavefront stage always runs at the same
+        step, and building the step tensor from a host scalar would otherwise
+        block the host on the stream every tick."""
+        cache = self.__dict__.setdefault("_tmod_cache", {})
+        hit = cache.get(float(timestep))
+        if hit is None:
+            t = torch.full((1,), float(timestep), device=device, dtype=torch.float32)
+            e = self.time_embedding(sinusoidal_embedding_1d(self.cfg.freq_dim, t).to(self.patch_embedding.weight.dtype))
+            e0 = self.time_projection(e).float().view(6, self.cfg.dim)
+            hit = (e0, e.float().view(1, self.cfg.dim))
+            cache[float(timestep)] = hit
+        return hit
 
     def _fused_qkv(self, b: Block):
         """One GEMM for q, k, v: concatenated bf16 weights, or one concatenated
