@@ -82,7 +82,9 @@ int wf_selftest_exp2(const float* x, float* y_poly, float* y_mufu, int n, void* 
  * WF_SCALE_TENSOR: one scale in scales[0]) or the same sequence per row
  * (mode WF_SCALE_TOKEN: scales[rows]).  Per-tensor mode needs a grid-wide
  * amax and uses `workspace` (>= 4 bytes of device memory, caller-owned,
- * overwritten); per-token mode ignores it. */
+ * overwritten); per-token mode ignores it.  Mode WF_SCALE_NONE is the
+ * scale-free cast of the onesided exchange, code = e4m3fn(x)
+ * (wave_rt/denoiser/exchange/onesided.py:151-153); scales may be NULL. */
 int wf_kv_quant(const void* x, uint8_t* codes, float* scales, int64_t rows, int64_t cols, int64_t x_row_stride,
                 int mode, void* workspace, void* stream);
 

@@ -437,3 +437,21 @@ def test_softmax_exp2_paths_error_bounds():
     L.check(L.lib().wf_selftest_exp2(z.data_ptr(), yp.data_ptr(), ym.data_ptr(), 2,
                                      torch.cuda.current_stream().cuda_stream), "wf_selftest_exp2")
     assert torch.all(yp[:2] >= 0) and torch.all(yp[:2] < 1e-37)
+
+
+def test_kv_scale_free_cast_bit_exact():
+    """onesided.py:152 cast (no scale) over every finite bf16 pattern, NaN-producing range included."""
+    K = _kernels()
+    from waveforcing_b200._lib import WF_SCALE_NONE
+
+    b = np.arange(65536, dtype=np.uint32)
+    f = o_codec.bf16_from_bits(b)
+    f = f[np.isfinite(f)]
+    n = (f.size // 1536) * 1536
+    x = f[:n].reshape(-1, 1536)
+    codes, _ = K.kv_quant(_bf16_gpu(x), WF_SCALE_NONE)
+    ref = o_codec.cast_scale_free(x)
+    got = codes.cpu().numpy()
+    nan = (ref & 0x7F) == 0x7F
+    assert np.array_equal(got[~nan], ref[~nan])
+    assert np.all((got[nan] & 0x7F) == 0x7F)

@@ -248,6 +248,29 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 }
 
+// Scale-free cast of the onesided exchange (wave_rt/denoiser/exchange/onesided.py:152):
+// code = e4m3fn(x) for bf16 x with torch's non-saturating RNE (|x| > 464 -> NaN),
+// through the exact software encoder since no scale bounds the inputs.
+__global__ void cast_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols,
+                                 int64_t row_stride, uint8_t* __restrict__ codes) {
+  const int64_t nch = cols / 8;
+  const int64_t total = rows * nch;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / nch, c = i - r * nch;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + r * row_stride) + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t out[2] = {0, 0};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t c2 = e4m3_encode_sw(__uint_as_float(w[k] << 16)) |
+                          (e4m3_encode_sw(__uint_as_float(w[k] & 0xFFFF0000u)) << 8);
+      out[k >> 1] |= c2 << ((k & 1) * 16);
+    }
+    reinterpret_cast<uint2*>(codes + r * cols)[c] = make_uint2(out[0], out[1]);
+  }
+}
+
 // ------------------------------------------------------------ per-tensor
 __global__ void amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, int64_t row_stride,
                             unsigned int* __restrict__ amax_bits) {
@@ -350,7 +373,8 @@ using namespace wfk::codec;
 
 extern "C" int wf_kv_quant(const void* x, uint8_t* codes, float* scales, int64_t rows, int64_t cols,
                            int64_t x_row_stride, int mode, void* workspace, void* stream) {
-  if (!rows_ok(x, rows, cols, x_row_stride) || !codes || !scales || (reinterpret_cast<uintptr_t>(codes) & 7))
+  if (!rows_ok(x, rows, cols, x_row_stride) || !codes || (mode != WF_SCALE_NONE && !scales) ||
+      (reinterpret_cast<uintptr_t>(codes) & 7))
     return fail(WF_ERR_INVALID_ARG, "wf_kv_quant: bad arguments (cols %% 8, 16-byte x, 8-byte codes)");
   if (rows == 0) return WF_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -372,8 +396,11 @@ extern "C" int wf_kv_quant(const void* x, uint8_t* codes, float* scales, int64_t
     amax_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride, amax);
     quant_tensor_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride, amax,
                                           codes, scales);
+  } else if (mode == WF_SCALE_NONE) {
+    const int g = grid_for(rows * (cols / 8), 256);
+    cast_e4m3_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride, codes);
   } else {
-    return fail(WF_ERR_INVALID_ARG, "wf_kv_quant: mode must be WF_SCALE_TENSOR or WF_SCALE_TOKEN");
+    return fail(WF_ERR_INVALID_ARG, "wf_kv_quant: mode must be WF_SCALE_NONE, WF_SCALE_TENSOR or WF_SCALE_TOKEN");
   }
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;

@@ -85,15 +85,15 @@ def kv_quant(x: torch.Tensor, mode: int = L.WF_SCALE_TOKEN, codes: torch.Tensor 
     rows, cols = x.shape
     if codes is None:
         codes = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
-    if scales is None:
+    if scales is None and mode != L.WF_SCALE_NONE:
         scales = torch.empty((rows if mode == L.WF_SCALE_TOKEN else 1,), dtype=torch.float32, device=x.device)
     ws = 0
     if mode == L.WF_SCALE_TENSOR:
         if workspace is None:
             workspace = torch.empty((1,), dtype=torch.int32, device=x.device)
         ws = workspace.data_ptr()
-    L.check(L.lib().wf_kv_quant(x.data_ptr(), codes.data_ptr(), scales.data_ptr(), rows, cols, x.stride(0), mode,
-                                ws, _stream()), "wf_kv_quant")
+    L.check(L.lib().wf_kv_quant(x.data_ptr(), codes.data_ptr(), scales.data_ptr() if scales is not None else None,
+                                rows, cols, x.stride(0), mode, ws, _stream()), "wf_kv_quant")
     return codes, scales
 
 
