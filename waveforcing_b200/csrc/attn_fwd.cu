@@ -31,7 +31,7 @@ constexpr int HD = 128;
 constexpr int NS = 3;
 constexpr int TILE = BM * HD * 2;  // 32 KB bf16 tile
 constexpr int HALF = TILE / 2;     // one 64-column swizzle block (128 rows x 128 B)
-constexpr int NBARS = 1 + 3 * NS + 2 + 2 + 1 + 1;
+constexpr int NBARS = 1 + 3 * NS + 2 + 2 + 1 + 1 + 1;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + TILE * (1 + 2 * NS) + NBARS * 8 + 16;
 constexpr int THREADS = 256;
 
@@ -66,7 +66,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bar_p = bar_s + 2;
   uint64_t* bar_o = bar_p + 2;
   uint64_t* bar_fin = bar_o + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_fin + 1);
+  uint64_t* bar_last = bar_fin + 1;  // one phase: every PV of the CTA has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_last + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -89,6 +90,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(bar_o, 1);
     mbar_init(bar_fin, 1);
+    mbar_init(bar_last, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -169,6 +171,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           umma_commit(bar_o);
         }
       }
+      // The epilogue waits on its own one-phase barrier: a parity wait on bar_o
+      // could be two phases behind there (PV_{nk-2} and PV_{nk-1} both pending).
+      umma_commit(bar_last);
       // Nothing of ours may still be running when TMEM is released.
       umma_commit(bar_fin);
       mbar_wait_drain(bar_fin, 0, 200000000ull);
@@ -238,7 +243,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float sum = sum2.x + sum2.y;
       const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
       if (__any_sync(0xffffffffu, grow)) {
-        // O may only be touched once PV_{j-1} has completed.
+        // O may only be touched once PV_{j-1} has completed.  This parity wait
+        // is unambiguous: S_j's commit (one issuing thread, in order) already
+        // covered PV_{j-2}, and PV_j needs this thread's arrival.
         ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (j - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
         if (!ok) break;
         tc_fence_after();
@@ -258,7 +265,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       mbar_arrive(&bar_p[bsel]);
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (nk - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_last, 0, abort_flag, ST_ATTN_SOFTMAX));
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.f / l_run;
