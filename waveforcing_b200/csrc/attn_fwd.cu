@@ -1,18 +1,27 @@
 // tcgen05/TMEM flash attention forward (bf16, head_dim 128) for the chunk
 // self-attention of WaveRT's wavefront step (wave_rt/runtime/backend.py:141-148).
 //
-// One CTA computes a 128-query tile of one head against all Lk keys:
-//   warp 0       TMA producer: Q once, then K/V tiles (128 keys) into a
-//                3-stage ring, 128-byte swizzled, two 64-column boxes each
+// One CTA computes a 128-query tile of one head against all Lk keys, in
+// 256-key tiles:
+//   warp 0       TMA producer: Q once; K in 256-key tiles (2-stage ring, the
+//                K ring runs one tile ahead of V); V in 128-key halves
+//                (one slot per half); 128-byte swizzle, 64-column boxes
 //   warp 1       allocates 512 TMEM columns; lane 0 issues the MMAs:
-//                S_j = Q K_j^T   (kind::f16, A and B from shared memory)
-//                O  += P_j V_j   (kind::f16, A = P from TMEM, B = V MN-major)
-//   warps 4-7    softmax: thread t owns query row t (= TMEM lane t); reads
-//                S_j from TMEM, writes P_j (bf16) back to TMEM, rescales the
-//                O accumulator lazily (only when the running max grows by
-//                more than 2^8), and finally normalises O and stores it.
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
-// S is double buffered so S_{j+1} is computed while row softmax of S_j runs.
+//                S_j  = Q K_j^T  as one M=128, N=256 MMA per 16-wide k step
+//                O   += P_j V_j  as M=128, N=128 MMAs (A = P from TMEM,
+//                                B = V MN-major), 16 k steps per tile
+//   warps 4-7    softmax of keys [0,128) of each tile   (warpgroup 0)
+//   warps 8-11   softmax of keys [128,256) of each tile (warpgroup 1)
+//                thread t of a warpgroup owns query row t (= TMEM lane t);
+//                the two halves of a row agree on the row max through a
+//                shared-memory exchange; each warpgroup writes its half of
+//                P_j (bf16) to TMEM, rescales its 64 columns of O lazily
+//                (only when the running max grows by more than 2^8), and
+//                finally normalises and stores its 64 output columns.
+// TMEM columns: S [0,256)  P [256,384)  O [384,512).
+// S is released as soon as both warpgroups have read it into registers, so
+// QK^T of tile j+1 runs on the tensor pipe while P_j is being computed; P is
+// written only after PV_{j-1} has completed.
 // Every wait is bounded (sm100.cuh mbar_wait); a timed-out wait raises the
 // status word and the CTA drains its in-flight work and exits.
 #include <cuda_runtime.h>
@@ -25,17 +34,23 @@
 namespace wfk {
 namespace attn {
 
-constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BM = 128;          // queries per CTA
+constexpr int BN = 256;          // keys per tile
+constexpr int KH = 128;          // keys per softmax warpgroup / per V slot
 constexpr int HD = 128;
-constexpr int NS = 3;
-constexpr int TILE = BM * HD * 2;  // 32 KB bf16 tile
-constexpr int HALF = TILE / 2;     // one 64-column swizzle block (128 rows x 128 B)
-constexpr int NBARS = 1 + 3 * NS + 2 + 2 + 1 + 1 + 1;
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + TILE * (1 + 2 * NS) + NBARS * 8 + 16;
-constexpr int THREADS = 256;
+constexpr int NSK = 2;           // K ring depth (256-key tiles)
+constexpr int QTILE = BM * HD * 2;   // 32 KB
+constexpr int KTILE = BN * HD * 2;   // 64 KB: [d 0-63: 256 rows x 128 B][d 64-127]
+constexpr int KHALF = KTILE / 2;     // 32 KB
+constexpr int VSLOT = KH * HD * 2;   // 32 KB: [d 0-63: 128 rows x 128 B][d 64-127]
+constexpr int VHALF = VSLOT / 2;     // 16 KB
+constexpr int QHALF = QTILE / 2;     // 16 KB
+constexpr int BIG = QTILE + NSK * KTILE + 2 * VSLOT;  // 224 KB
+constexpr int NBARS = 1 + 2 * NSK + 4 + 7;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + BIG + NBARS * 8 + 2 * BM * 4 /*row exchange*/ + 16;
+constexpr int THREADS = 384;
 
-constexpr uint32_t COL_S = 0, COL_O = 256, COL_P = 384;
+constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;
 
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
@@ -55,19 +70,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
-  uint8_t* sK = smem + TILE;
-  uint8_t* sV = sK + NS * TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NS * TILE);
+  uint8_t* sK = sQ + QTILE;
+  uint8_t* sV = sK + NSK * KTILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * VSLOT);
   uint64_t* bar_q = bars;
   uint64_t* full_k = bars + 1;
-  uint64_t* full_v = full_k + NS;
-  uint64_t* empty_kv = full_v + NS;
-  uint64_t* bar_s = empty_kv + NS;
-  uint64_t* bar_p = bar_s + 2;
-  uint64_t* bar_o = bar_p + 2;
-  uint64_t* bar_fin = bar_o + 1;
-  uint64_t* bar_last = bar_fin + 1;  // one phase: every PV of the CTA has completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_last + 1);
+  uint64_t* empty_k = full_k + NSK;
+  uint64_t* full_v = empty_k + NSK;   // [2], one per 128-key half
+  uint64_t* empty_v = full_v + 2;     // [2]
+  uint64_t* bar_s = empty_v + 2;      // S_j complete
+  uint64_t* bar_sfree = bar_s + 1;    // both warpgroups have read S_j and exchanged the row max
+  uint64_t* bar_p = bar_sfree + 1;    // P_j written
+  uint64_t* bar_pv = bar_p + 1;       // PV_j complete
+  uint64_t* bar_xch = bar_pv + 1;     // row exchange between the warpgroups
+  uint64_t* bar_last = bar_xch + 1;   // one phase: every PV of the CTA has completed
+  uint64_t* bar_fin = bar_last + 1;
+  float* xch = reinterpret_cast<float*>(bar_fin + 1);  // [2][BM]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xch + 2 * BM);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -79,18 +98,21 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < NSK; ++s) {
       mbar_init(&full_k[s], 1);
+      mbar_init(&empty_k[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&full_v[s], 1);
-      mbar_init(&empty_kv[s], 1);
+      mbar_init(&empty_v[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar_s[i], 1);
-      mbar_init(&bar_p[i], 128);
-    }
-    mbar_init(bar_o, 1);
-    mbar_init(bar_fin, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_sfree, 256);
+    mbar_init(bar_p, 256);
+    mbar_init(bar_pv, 1);
+    mbar_init(bar_xch, 256);
     mbar_init(bar_last, 1);
+    mbar_init(bar_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -103,38 +125,71 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  // Register split: 384 threads launch with 168 registers each (64,512).
+  // Warpgroup 0 (producer, MMA, two idle warps) drops to 72 and the two
+  // softmax warpgroups rise to 216: 128 * 72 + 256 * 216 = 64,512.  The
+  // setmaxnreg sits at the top of each warpgroup's branch and the branches
+  // never rejoin (each ends with its own copy of the teardown), so no code
+  // runs at an ambiguous register count.
+  auto teardown = [&]() {
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tbase, 512);
+    }
+  };
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;\n" ::: "memory");
+    if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ producer
+      // Issue order: K_0, then per tile j: K_{j+1}, V_j (both halves).  K runs
+      // a tile ahead because QK^T_{j+1} is queued on the tensor pipe before
+      // PV_j, and V_j's slots only free up when PV_{j-1} completes.
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(bar_q, TILE);
+      mbar_arrive_expect_tx(bar_q, QTILE);
       tma_load_4d(sQ, &tmQ, bar_q, 0, h, q0, bz);
-      tma_load_4d(sQ + HALF, &tmQ, bar_q, 64, h, q0, bz);
-      int issued = 0;
-      for (int j = 0; j < nk; ++j) {
-        const int s = j % NS;
-        if (j >= NS && !mbar_wait(&empty_kv[s], ((j / NS) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full_k[s], TILE);
-        tma_load_4d(sK + s * TILE, &tmK, &full_k[s], 0, h, j * BN, bz);
-        tma_load_4d(sK + s * TILE + HALF, &tmK, &full_k[s], 64, h, j * BN, bz);
-        mbar_arrive_expect_tx(&full_v[s], TILE);
-        tma_load_4d(sV + s * TILE, &tmV, &full_v[s], 0, h, j * BN, bz);
-        tma_load_4d(sV + s * TILE + HALF, &tmV, &full_v[s], 64, h, j * BN, bz);
-        issued = j + 1;
+      tma_load_4d(sQ + QHALF, &tmQ, bar_q, 64, h, q0, bz);
+      int k_issued = 0, v_issued = 0;
+      bool run = true;
+      auto load_k = [&](int j) -> bool {
+        const int s = j % NSK;
+        if (j >= NSK && !mbar_wait(&empty_k[s], ((j / NSK) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) return false;
+        uint8_t* dst = sK + s * KTILE;
+        mbar_arrive_expect_tx(&full_k[s], KTILE);
+        tma_load_4d(dst, &tmK, &full_k[s], 0, h, j * BN, bz);
+        tma_load_4d(dst + KH * 128, &tmK, &full_k[s], 0, h, j * BN + KH, bz);
+        tma_load_4d(dst + KHALF, &tmK, &full_k[s], 64, h, j * BN, bz);
+        tma_load_4d(dst + KHALF + KH * 128, &tmK, &full_k[s], 64, h, j * BN + KH, bz);
+        k_issued = j + 1;
+        return true;
+      };
+      run = load_k(0);
+      for (int j = 0; run && j < nk; ++j) {
+        if (j + 1 < nk && !(run = load_k(j + 1))) break;
+        for (int half = 0; half < 2; ++half) {
+          if (j >= 1 && !mbar_wait(&empty_v[half], (j - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) {
+            run = false;
+            break;
+          }
+          uint8_t* dst = sV + half * VSLOT;
+          mbar_arrive_expect_tx(&full_v[half], VSLOT);
+          tma_load_4d(dst, &tmV, &full_v[half], 0, h, j * BN + half * KH, bz);
+          tma_load_4d(dst + VHALF, &tmV, &full_v[half], 64, h, j * BN + half * KH, bz);
+          v_issued = 2 * j + half + 1;
+        }
       }
       if (*abort_flag) {
         // Let the copies this thread issued land before the CTA exits.
         mbar_wait_drain(bar_q, 0, 200000000ull);
-        for (int j = (issued > NS ? issued - NS : 0); j < issued; ++j) {
-          mbar_wait_drain(&full_k[j % NS], (j / NS) & 1, 200000000ull);
-          mbar_wait_drain(&full_v[j % NS], (j / NS) & 1, 200000000ull);
-        }
+        for (int j = (k_issued > NSK ? k_issued - NSK : 0); j < k_issued; ++j)
+          mbar_wait_drain(&full_k[j % NSK], (j / NSK) & 1, 200000000ull);
+        for (int v = (v_issued > 2 ? v_issued - 2 : 0); v < v_issued; ++v)
+          mbar_wait_drain(&full_v[v & 1], (v >> 1) & 1, 200000000ull);
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       // ----------------------------------------------------------------- MMA
       constexpr uint32_t idesc_qk = make_idesc(1, FMT_BF16, FMT_BF16, 0, BM, BN);
       constexpr uint32_t idesc_pv = make_idesc(1, FMT_BF16, FMT_BF16, 1, BM, HD);
@@ -142,75 +197,99 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = mbar_wait(bar_q, 0, abort_flag, ST_ATTN_MMA);
       for (int j = 0; ok && j <= nk; ++j) {
         if (j < nk) {
-          const int s = j % NS;
-          if (!mbar_wait(&full_k[s], (j / NS) & 1, abort_flag, ST_ATTN_MMA)) break;
+          const int s = j % NSK;
+          if (!mbar_wait(&full_k[s], (j / NSK) & 1, abort_flag, ST_ATTN_MMA)) break;
+          // S is single-buffered: both warpgroups must have read S_{j-1}.
+          if (j >= 1 && !mbar_wait(bar_sfree, (j - 1) & 1, abort_flag, ST_ATTN_MMA)) break;
           tc_fence_after();
-          const uint32_t dS = tbase + COL_S + (j & 1) * BN;
-          const uint32_t aK = smem_u32(sK + s * TILE);
+          const uint32_t aK = smem_u32(sK + s * KTILE);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-            umma_f16_ss(dS, desc_sw128(aQ + off, 16, 1024), desc_sw128(aK + off, 16, 1024), idesc_qk, kk > 0);
+            const uint32_t qoff = (kk >> 2) * QHALF + (kk & 3) * 32;
+            const uint32_t koff = (kk >> 2) * KHALF + (kk & 3) * 32;
+            umma_f16_ss(tbase + COL_S, desc_sw128(aQ + qoff, 16, 1024), desc_sw128(aK + koff, 16, 1024), idesc_qk,
+                        kk > 0);
           }
-          umma_commit(&bar_s[j & 1]);
+          umma_commit(&empty_k[s]);
+          umma_commit(bar_s);
         }
         if (j >= 1) {
           const int jj = j - 1;
-          const int s = jj % NS;
-          if (!mbar_wait(&bar_p[jj & 1], (jj >> 1) & 1, abort_flag, ST_ATTN_MMA)) break;
-          if (!mbar_wait(&full_v[s], (jj / NS) & 1, abort_flag, ST_ATTN_MMA)) break;
-          tc_fence_after();
-          const uint32_t aV = smem_u32(sV + s * TILE);
-          const uint32_t tP = tbase + COL_P + (jj & 1) * (BN / 2);
+          if (!mbar_wait(bar_p, jj & 1, abort_flag, ST_ATTN_MMA)) break;
+          bool vok = true;
+          for (int half = 0; half < 2; ++half) {
+            if (!mbar_wait(&full_v[half], jj & 1, abort_flag, ST_ATTN_MMA)) {
+              vok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t aV = smem_u32(sV + half * VSLOT);
+            const uint32_t tP = tbase + COL_P + half * (KH / 2);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            umma_f16_ts(tbase + COL_O, tP + kk * 8, desc_sw128(aV + kk * 2048, HALF, 1024), idesc_pv,
-                        (jj > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < KH / 16; ++kk) {
+              umma_f16_ts(tbase + COL_O, tP + kk * 8, desc_sw128(aV + kk * 2048, VHALF, 1024), idesc_pv,
+                          (jj > 0 || half > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&empty_v[half]);
           }
-          umma_commit(&empty_kv[s]);
-          umma_commit(bar_o);
+          if (!vok) break;
+          umma_commit(bar_pv);
         }
       }
-      // The epilogue waits on its own one-phase barrier: a parity wait on bar_o
-      // could be two phases behind there (PV_{nk-2} and PV_{nk-1} both pending).
+      // The epilogue waits on its own one-phase barrier: a parity wait on
+      // bar_pv could be two phases behind there.
       umma_commit(bar_last);
       // Nothing of ours may still be running when TMEM is released.
       umma_commit(bar_fin);
       mbar_wait_drain(bar_fin, 0, 200000000ull);
     }
     __syncwarp();
-  } else if (warp >= 4) {
+    teardown();
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;\n" ::: "memory");
     // ------------------------------------------------------------ softmax
-    const int wq = warp - 4;
+    const int wg = (warp - 4) >> 2;  // 0: keys [0,128) of a tile, 1: keys [128,256)
+    const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    float* my_x = xch + wg * BM + row;
+    const float* other_x = xch + (wg ^ 1) * BM + row;
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
-      const int bsel = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_s[bsel], (j >> 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_s, j & 1, abort_flag, ST_ATTN_SOFTMAX));
       if (!ok) break;
       tc_fence_after();
-      float s[BN];
+      float s[KH];
       {
         uint32_t r[64];
-        tmem_ld32x32b_x64(tbase + lane_off + COL_S + bsel * BN, r);
+        tmem_ld32x32b_x64(tbase + lane_off + COL_S + wg * KH, r);
 #pragma unroll
         for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
-        tmem_ld32x32b_x64(tbase + lane_off + COL_S + bsel * BN + 64, r);
+        tmem_ld32x32b_x64(tbase + lane_off + COL_S + wg * KH + 64, r);
 #pragma unroll
         for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(r[i]);
       }
-      const int kvalid = Lk - j * BN;
-      if (kvalid < BN) {
+      const int kvalid = Lk - j * BN - wg * KH;
+      if (kvalid < KH) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i)
+        for (int i = 0; i < KH; ++i)
           if (i >= kvalid) s[i] = -INFINITY;
       }
       float mx = s[0];
 #pragma unroll
-      for (int i = 1; i < BN; ++i) mx = fmaxf(mx, s[i]);
+      for (int i = 1; i < KH; ++i) mx = fmaxf(mx, s[i]);
+      // Row max across the two halves.  The exchange slot is reused every
+      // tile: QK^T_{j+1} (and with it this thread's next write) waits on
+      // bar_sfree, which every thread passes only after its read below.
+      *my_x = mx;
+      mbar_arrive(bar_xch);
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_xch, j & 1, abort_flag, ST_ATTN_SOFTMAX));
+      if (!ok) break;
+      mx = fmaxf(mx, *other_x);
+      tc_fence_before();
+      mbar_arrive(bar_sfree);
       const float mx2 = mx * scale_log2;
       float m_new = m_run;
       bool grow = false;
@@ -222,13 +301,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // P = 2^(s * scale_log2 - m): pairs through packed f32x2 FMAs; 3 of
       // every 8 pairs take the FMA-pipe polynomial, the rest MUFU ex2, so the
-      // two pipes finish together and the softmax stays shorter than the MMAs
+      // two pipes finish together.
       const float2 sc2 = make_float2(scale_log2, scale_log2);
       const float2 nm2 = make_float2(-m_new, -m_new);
       float2 sum2 = make_float2(0.f, 0.f);
-      uint32_t pk[BN / 2];
+      uint32_t pk[KH / 2];
 #pragma unroll
-      for (int i = 0; i < BN / 2; ++i) {
+      for (int i = 0; i < KH / 2; ++i) {
         const float2 x = ffma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
         float2 pr;
         if ((i & 7) < 3) {
@@ -242,39 +321,49 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const float sum = sum2.x + sum2.y;
       const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
-      if (__any_sync(0xffffffffu, grow)) {
-        // O may only be touched once PV_{j-1} has completed.  This parity wait
-        // is unambiguous: S_j's commit (one issuing thread, in order) already
-        // covered PV_{j-2}, and PV_j needs this thread's arrival.
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (j - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+      // P and O may only be written once PV_{j-1} has completed.  This parity
+      // wait is unambiguous: S_j's commit (one issuing thread, in order)
+      // already covered PV_{j-2}, and PV_j needs this thread's arrival.
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_pv, (j - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
         if (!ok) break;
         tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-        for (int c = 0; c < HD; c += 32) {
+        for (int c = 0; c < HD / 2; c += 32) {
           uint32_t r[32];
-          tmem_ld32x32b_x32(tbase + lane_off + COL_O + c, r);
+          tmem_ld32x32b_x32(tbase + lane_off + COL_O + wg * (HD / 2) + c, r);
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32x32b_x32(tbase + lane_off + COL_O + c, r);
+          tmem_st32x32b_x32(tbase + lane_off + COL_O + wg * (HD / 2) + c, r);
         }
       }
       l_run = l_run * alpha + sum;
       m_run = m_new;
-      tmem_st32x32b_x64(tbase + lane_off + COL_P + bsel * (BN / 2), pk);
+      tmem_st32x32b_x64(tbase + lane_off + COL_P + wg * (KH / 2), pk);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bar_p[bsel]);
+      mbar_arrive(bar_p);
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_last, 0, abort_flag, ST_ATTN_SOFTMAX));
     if (ok) {
+      // Row sum across the two halves (same slot: every thread read the last
+      // max before arriving on bar_p, and bar_last follows every PV).
+      *my_x = l_run;
+      mbar_arrive(bar_xch);
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_xch, nk & 1, abort_flag, ST_ATTN_SOFTMAX));
+    }
+    if (ok) {
       tc_fence_after();
-      const float inv_l = 1.f / l_run;
+      const float inv_l = 1.f / (l_run + *other_x);
       const int qrow = q0 + row;
-      __nv_bfloat16* dst = out + (long long)bz * o_batch + (long long)qrow * o_tok + (long long)h * o_head;
+      __nv_bfloat16* dst =
+          out + (long long)bz * o_batch + (long long)qrow * o_tok + (long long)h * o_head + wg * (HD / 2);
 #pragma unroll
-      for (int c = 0; c < HD; c += 32) {
+      for (int c = 0; c < HD / 2; c += 32) {
         uint32_t r[32];
-        tmem_ld32x32b_x32(tbase + lane_off + COL_O + c, r);
+        tmem_ld32x32b_x32(tbase + lane_off + COL_O + wg * (HD / 2) + c, r);
         if (qrow < Lq) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
@@ -289,12 +378,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tbase, 512);
+    teardown();
   }
 }
 
@@ -304,7 +388,7 @@ static int make_qkv_map(CUtensorMap* m, const void* p, int batch, int L, int H, 
   const uint64_t gdim[4] = {(uint64_t)HD, (uint64_t)H, (uint64_t)L, (uint64_t)batch};
   const uint64_t gstr[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2,
                             (uint64_t)(batch > 1 ? st[0] : st[1] * (int64_t)L) * 2};
-  const uint32_t box[4] = {64, 1, (uint32_t)BM, 1};
+  const uint32_t box[4] = {64, 1, 128, 1};
   return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, p, gdim, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
