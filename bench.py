@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--w8a8", default="none", choices=["none", "e4m3", "int8"])
     ap.add_argument("--denoise-steps", default="1000,800,600,400,200")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec"],
+    ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec", "dequant"],
                     help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
     return ap.parse_args()
@@ -397,7 +397,12 @@ def run_kernel_bench(args):
       attn  q [4680, H, 128] vs K/V [ctx*4680, H, 128] bf16 (r0 sees 8 chunks)
       gemm  W8A8 e4m3 FFN fc_in [4680 x dim] x [ffn x dim]^T
       codec per-token FP8 quantise-and-publish of one layer's K and V to 4 slots
-    Inputs exceed L2 (126 MB) for attn and codec; each launch reads them once."""
+      dequant per-token FP8 dequantise of one layer's 5 received K and V slots
+              into the bf16 context buffer (one launch for K, one for V)
+    The launches rotate over independent buffer sets whose total footprint
+    exceeds L2 (126 MB), so each launch reads its inputs from HBM, and `steps`
+    launches are captured in one CUDA graph so that host-side argument
+    marshalling stays out of the timed region."""
     from waveforcing_b200 import _lib as L
     from waveforcing_b200 import kernels
     from waveforcing_b200.wavefront.dit import DiTConfig
@@ -406,45 +411,82 @@ def run_kernel_bench(args):
     dev = torch.device("cuda", 0)
     T, H, D = cfg.tokens_per_chunk, cfg.heads, cfg.head_dim
     g = torch.Generator(device=dev).manual_seed(0)
+    l2 = 126e6
+
+    def n_sets(set_bytes):
+        return max(2, int(math.ceil(1.5 * l2 / set_bytes)))
+
+    fns = []
     if args.kernel == "attn":
         Lk = args.ctx_chunks * T
-        q = torch.randn(1, T, H, D, device=dev, generator=g).bfloat16()
-        k = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
-        v = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
-        fn = lambda: kernels.attention(q, k, v)  # noqa: E731
+        set_bytes = 2 * (2 * T + 2 * Lk) * H * D
+        for _ in range(n_sets(set_bytes)):
+            q = torch.randn(1, T, H, D, device=dev, generator=g).bfloat16()
+            k = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
+            v = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
+            o = torch.empty_like(q)
+            fns.append(lambda q=q, k=k, v=v, o=o: kernels.attention(q, k, v, out=o))
         work, unit, bound = 4.0 * T * Lk * H * D / 1e12, "TFLOP/s", "tensor"
         name = f"attn_fwd q{T} kv{Lk} h{H}"
     elif args.kernel == "gemm":
-        x = torch.randn(T, cfg.dim, device=dev, generator=g).bfloat16()
-        w = (torch.randn(cfg.ffn, cfg.dim, device=dev, generator=g) * 0.02).bfloat16()
-        wq, ws = kernels.weight_quant(w)
-        xq, xs = kernels.act_quant(x)
-        out = torch.empty(T, cfg.ffn, device=dev, dtype=torch.bfloat16)
-        fn = lambda: kernels.gemm_w8a8(xq, xs, wq, ws, None, out=out)  # noqa: E731
+        set_bytes = T * cfg.dim + cfg.ffn * cfg.dim + 2 * T * cfg.ffn
+        for _ in range(n_sets(set_bytes)):
+            x = torch.randn(T, cfg.dim, device=dev, generator=g).bfloat16()
+            w = (torch.randn(cfg.ffn, cfg.dim, device=dev, generator=g) * 0.02).bfloat16()
+            wq, ws = kernels.weight_quant(w)
+            xq, xs = kernels.act_quant(x)
+            out = torch.empty(T, cfg.ffn, device=dev, dtype=torch.bfloat16)
+            fns.append(lambda xq=xq, xs=xs, wq=wq, ws=ws, out=out: kernels.gemm_w8a8(xq, xs, wq, ws, None, out=out))
         work, unit, bound = 2.0 * T * cfg.dim * cfg.ffn / 1e12, "TFLOP/s", "tensor"
         name = f"gemm_w8a8 e4m3 {T}x{cfg.ffn}x{cfg.dim}"
+    elif args.kernel == "dequant":
+        HD = H * D
+        R = 5 * T
+        set_bytes = 2 * (R * HD * 3 + 4 * R)
+        for _ in range(n_sets(set_bytes)):
+            kc = torch.randint(0, 256, (R, HD), device=dev, dtype=torch.uint8, generator=g)
+            kc[(kc & 0x7F) == 0x7F] = 0  # no NaN codes
+            vc = kc.roll(1, 0)
+            ks = torch.rand(R, device=dev, generator=g) + 0.5
+            vs = ks.flip(0)
+            ko = torch.empty(R, HD, device=dev, dtype=torch.bfloat16)
+            vo = torch.empty_like(ko)
+            fns.append(lambda kc=kc, ks=ks, ko=ko: kernels.kv_dequant(kc, ks, L.WF_SCALE_TOKEN, out=ko))
+            fns.append(lambda vc=vc, vs=vs, vo=vo: kernels.kv_dequant(vc, vs, L.WF_SCALE_TOKEN, out=vo))
+        work = (R * HD * 3 + 4 * R) / 1e9  # per launch (one of K or V)
+        unit, bound = "GB/s", "hbm"
+        name = f"kv_dequant {R}x{HD} per launch (K and V alternate)"
     else:
         HD = H * D
-        kx = torch.randn(T, HD, device=dev, generator=g).bfloat16()
-        vx = torch.randn(T, HD, device=dev, generator=g).bfloat16()
         n = 4
-        dst = [(torch.empty(T, HD, device=dev, dtype=torch.uint8), torch.empty(T, HD, device=dev, dtype=torch.uint8),
-                torch.empty(T, device=dev), torch.empty(T, device=dev)) for _ in range(n)]
-        fn = lambda: kernels.kv_quant_publish(kx, vx, [d[0].data_ptr() for d in dst], [d[1].data_ptr() for d in dst],  # noqa: E731
-                                              [d[2].data_ptr() for d in dst], [d[3].data_ptr() for d in dst])
+        set_bytes = 2 * T * HD * 2 + n * 2 * (T * HD + 4 * T)
+        for _ in range(n_sets(set_bytes)):
+            kx = torch.randn(T, HD, device=dev, generator=g).bfloat16()
+            vx = torch.randn(T, HD, device=dev, generator=g).bfloat16()
+            dst = [(torch.empty(T, HD, device=dev, dtype=torch.uint8), torch.empty(T, HD, device=dev, dtype=torch.uint8),
+                    torch.empty(T, device=dev), torch.empty(T, device=dev)) for _ in range(n)]
+            ptrs = [[d[i].data_ptr() for d in dst] for i in range(4)]
+            fns.append(lambda kx=kx, vx=vx, ptrs=ptrs, dst=dst: kernels.kv_quant_publish(kx, vx, *ptrs))
         work = (2 * T * HD * 2 + n * 2 * (T * HD + 4 * T)) / 1e9
         unit, bound = "GB/s", "hbm"
         name = f"kv_quant_publish {T}x{HD} to {n} slots"
-    for _ in range(max(3, args.warmup)):
-        fn()
+    for i in range(max(3, args.warmup)):
+        fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    launches = max(args.steps, len(fns))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(launches):
+            fns[i % len(fns)]()
+    graph.replay()  # warm the graph itself
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        fn()
+    graph.replay()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / launches
+    del graph
     peaks, src = _peaks()
     peak = peaks["bf16_tflops"] if bound == "tensor" else peaks["hbm_gbs"]
     if args.kernel == "gemm":
@@ -452,7 +494,7 @@ def run_kernel_bench(args):
     ach = work / (ms * 1e-3)
     print(json.dumps({"kernel": name, "ms": ms, "achieved": ach, "unit": unit, "peak": peak,
                       "frac": ach / peak, "peak_source": src + (" bf16 burst x2" if args.kernel == "gemm" else ""),
-                      "status": L.status_take()}), flush=True)
+                      "launches": launches, "buffer_sets": len(fns), "status": L.status_take()}), flush=True)
 
 
 def main():

@@ -232,6 +232,37 @@ def test_kv_quant_publish_fans_out():
         assert torch.equal(d[2], sk) and torch.equal(d[3], sv)
 
 
+@pytest.mark.parametrize("n_dst", [1, 4, 5])
+def test_kv_quant_publish_matches_oracle(n_dst):
+    """The fused publish against the row-wise restatement, including a row
+    with a NaN (non-finite scale path), zero rows, -0 and huge values.  (A
+    row holding inf is left out: inf / inf gives a NaN whose sign bit differs
+    between x86 and CUDA, so the code byte is platform-defined.)"""
+    K = _kernels()
+    rng = np.random.default_rng(7 + n_dst)
+    k = rng.standard_normal((261, 1536)).astype(np.float32)
+    v = (rng.standard_normal((261, 1536)) * np.exp(rng.standard_normal((261, 1536)) * 3)).astype(np.float32)
+    k[9, 3] = np.nan
+    v[11] = 0.0
+    v[12] = -0.0
+    v[13, ::7] = -0.0
+    k[20] *= 3e37
+    k, v = o_codec.bf16_round(k), o_codec.bf16_round(v)
+    ref_ck, ref_sk = o_codec.quant_per_token(k)
+    ref_cv, ref_sv = o_codec.quant_per_token(v)
+    kg, vg = _bf16_gpu(k), _bf16_gpu(v)
+    dst = [(torch.empty(261, 1536, dtype=torch.uint8, device=DEV), torch.empty(261, 1536, dtype=torch.uint8, device=DEV),
+            torch.empty(261, device=DEV), torch.empty(261, device=DEV)) for _ in range(n_dst)]
+    K.kv_quant_publish(kg, vg, [d[0].data_ptr() for d in dst], [d[1].data_ptr() for d in dst],
+                       [d[2].data_ptr() for d in dst], [d[3].data_ptr() for d in dst])
+    torch.cuda.synchronize()
+    for d in dst:
+        assert np.array_equal(d[0].cpu().numpy(), ref_ck) and np.array_equal(d[1].cpu().numpy(), ref_cv)
+        # scales: equal values (a NaN scale's payload bits are platform-defined)
+        assert np.array_equal(d[2].cpu().numpy(), np.asarray(ref_sk, np.float32), equal_nan=True)
+        assert np.array_equal(d[3].cpu().numpy(), np.asarray(ref_sv, np.float32), equal_nan=True)
+
+
 # ----------------------------------------------------------------------- W8A8
 @pytest.mark.parametrize("qtype", ["e4m3", "s8"])
 def test_quantisers_bit_exact(qtype):

@@ -7,10 +7,17 @@
 // u8; per-token scales [rows] f32 (or one f32 for the per-tensor mode).
 //
 // Exactness notes.
-//  * x / s must be the correctly rounded f32 quotient before the bf16 rounding.
-//    With r = RN(1/s) (IEEE reciprocal, __frcp_rn) and q0 = RN(x r), one
-//    correction q = RN(q0 + RN(x - q0 s) r) is correctly rounded (Markstein's
-//    theorem); rows whose scale is not finite take the plain IEEE division.
+//  * The reference rounds x / s to f32 and then to bf16.  x and s are both
+//    bf16 (8-bit significands A, B), so x / s = (A / B) 2^k is never a bf16
+//    rounding midpoint (that would need B / gcd(A, B) to be a power of two of
+//    at least 2^8) and lies at least 2^-17 (relative) away from every
+//    midpoint.  RN(x * RN(1/s)) is within 2^-23 of x / s, so its bf16 rounding
+//    equals the bf16 rounding of the correctly rounded quotient: the fast path
+//    is one multiply by the row's reciprocal.  Rows whose scale is not finite
+//    take the IEEE division and the software encoder.
+//  * bf16 and e4m3 round-to-nearest are symmetric, so the fast path rounds
+//    |x| / s and ORs x's sign into each code afterwards (torch keeps -0 as
+//    0x80; the hardware conversion of a value that rounds to zero does not).
 //  * The hardware e4m3 conversion saturates, torch's does not.  For a finite
 //    row amax the bf16 quotient is at most 450 in magnitude (s is amax/448
 //    rounded to bf16, so |x|/s <= 448.9 before rounding), where saturating and
@@ -78,34 +85,33 @@ __device__ __forceinline__ RowQuant make_rowq(float amax) {
   return q;
 }
 
-__device__ __forceinline__ float div_exact(float x, const RowQuant& q) {
-  if (!q.finite) return __fdiv_rn(x, q.s);
-  const float q0 = x * q.r;
-  const float e = fmaf(-q0, q.s, x);
-  // s > 0, so the quotient carries x's sign; this keeps -0 / s == -0, which the
-  // correction step alone would turn into +0 (+0 + -0 rounds to +0)
-  return copysignf(fmaf(e, q.r, q0), x);
+// Two bf16 magnitudes (one bf16x2 word, signs ignored) -> two e4m3 codes of
+// bf16(|x| * r) in the low 16 bits.
+__device__ __forceinline__ uint32_t e4m3x2_mag(uint32_t w, float r) {
+  const uint32_t a = w & 0x7FFF7FFFu;
+  const float2 p = fmul2(make_float2(__uint_as_float(a << 16), __uint_as_float(a & 0xFFFF0000u)), make_float2(r, r));
+  const __nv_bfloat162 b = __floats2bfloat162_rn(p.x, p.y);
+  const uint32_t bb = *reinterpret_cast<const uint32_t*>(&b);
+  return e4m3x2_hw(__uint_as_float(bb << 16), __uint_as_float(bb & 0xFFFF0000u));
+}
+
+// Four bf16 (two bf16x2 words) -> four codes, fast path (finite scale).
+__device__ __forceinline__ uint32_t quant4_fast(uint32_t w0, uint32_t w1, float r) {
+  const uint32_t mag = __byte_perm(e4m3x2_mag(w0, r), e4m3x2_mag(w1, r), 0x5410);
+  // the sign bits of the four bf16 (bit 15 / 31 of each word) into bit 7 of each code byte
+  return mag | (__byte_perm(w0, w1, 0x7531) & 0x80808080u);
 }
 
 // 8 bf16 (uint4) -> 8 codes (uint2)
 __device__ __forceinline__ uint2 quant8(const uint4& v, const RowQuant& q) {
+  if (q.finite) return make_uint2(quant4_fast(v.x, v.y, q.r), quant4_fast(v.z, v.w, q.r));
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   uint32_t out[2] = {0, 0};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float x0 = __uint_as_float(w[i] << 16);
-    const float x1 = __uint_as_float(w[i] & 0xFFFF0000u);
-    const float b0 = bf16_round_f(div_exact(x0, q));
-    const float b1 = bf16_round_f(div_exact(x1, q));
-    uint32_t c;
-    if (q.finite) {
-      // magnitudes through the hardware convert, signs copied explicitly so
-      // values that round to zero keep torch's signed zero (0x80)
-      c = e4m3x2_hw(fabsf(b0), fabsf(b1)) | ((__float_as_uint(b0) >> 24) & 0x80u) |
-          ((__float_as_uint(b1) >> 16) & 0x8000u);
-    } else {
-      c = e4m3_encode_sw(b0) | (e4m3_encode_sw(b1) << 8);
-    }
+    const float b0 = bf16_round_f(__fdiv_rn(__uint_as_float(w[i] << 16), q.s));
+    const float b1 = bf16_round_f(__fdiv_rn(__uint_as_float(w[i] & 0xFFFF0000u), q.s));
+    const uint32_t c = e4m3_encode_sw(b0) | (e4m3_encode_sw(b1) << 8);
     out[i >> 1] |= c << ((i & 1) * 16);
   }
   return make_uint2(out[0], out[1]);
@@ -130,6 +136,28 @@ __device__ __forceinline__ float amax8(const uint4& v, float m) {
   return m;
 }
 
+// Running maximum of |x| over bf16x2 words, kept as two u16 lanes of bf16
+// magnitude bits.  Non-negative floats, +inf and NaN order like their bit
+// patterns, so the integer maximum is torch.amax's NaN-propagating maximum.
+__device__ __forceinline__ uint32_t vmax_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t amax8_bits(const uint4& v, uint32_t m2) {
+  m2 = vmax_u16x2(m2, v.x & 0x7FFF7FFFu);
+  m2 = vmax_u16x2(m2, v.y & 0x7FFF7FFFu);
+  m2 = vmax_u16x2(m2, v.z & 0x7FFF7FFFu);
+  return vmax_u16x2(m2, v.w & 0x7FFF7FFFu);
+}
+
+// Warp-wide maximum of packed magnitudes -> f32 amax (bf16-valued).
+__device__ __forceinline__ float warp_amax_bits(uint32_t m2) {
+  const uint32_t m = __reduce_max_sync(0xffffffffu, max(m2 & 0xFFFFu, m2 >> 16));
+  return __uint_as_float(m << 16);
+}
+
 __device__ __forceinline__ float warp_max_nan(float m) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -147,19 +175,18 @@ __device__ __forceinline__ void quant_row(const __nv_bfloat16* __restrict__ xrow
                                           int64_t row) {
   const uint4* x4 = reinterpret_cast<const uint4*>(xrow);
   const int64_t nch = cols / 8;
-  float m = 0.f;
+  uint32_t m2 = 0;
   uint4 buf[NCH > 0 ? NCH : 1];
   if constexpr (NCH > 0) {
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
       buf[i] = __ldcs(x4 + lane + 32 * i);
-      m = amax8(buf[i], m);
+      m2 = amax8_bits(buf[i], m2);
     }
   } else {
-    for (int64_t c = lane; c < nch; c += 32) m = amax8(__ldg(x4 + c), m);
+    for (int64_t c = lane; c < nch; c += 32) m2 = amax8_bits(__ldg(x4 + c), m2);
   }
-  m = warp_max_nan(m);
-  const RowQuant q = make_rowq(m);
+  const RowQuant q = make_rowq(warp_amax_bits(m2));
   if constexpr (NCH > 0) {
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
@@ -224,16 +251,15 @@ __global__ void __launch_bounds__(WARPS * 32)
     const int64_t row = is_v ? w - rows : w;
     const uint4* x4 = reinterpret_cast<const uint4*>((is_v ? v : k) + row * (is_v ? v_stride : k_stride));
     uint4 buf[2 * NCH16];
-    float m = 0.f;
+    uint32_t m2 = 0;
 #pragma unroll
     for (int i = 0; i < NCH16; ++i) {
       buf[2 * i] = __ldcs(x4 + 2 * (lane + 32 * i));
       buf[2 * i + 1] = __ldcs(x4 + 2 * (lane + 32 * i) + 1);
-      m = amax8(buf[2 * i], m);
-      m = amax8(buf[2 * i + 1], m);
+      m2 = amax8_bits(buf[2 * i], m2);
+      m2 = amax8_bits(buf[2 * i + 1], m2);
     }
-    m = warp_max_nan(m);
-    const RowQuant q = make_rowq(m);
+    const RowQuant q = make_rowq(warp_amax_bits(m2));
     const DstList& d = is_v ? dv : dk;
 #pragma unroll
     for (int i = 0; i < NCH16; ++i) {
@@ -339,6 +365,49 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ codes, const float* _
   }
 }
 
+// 8 codes (uint2) -> 8 bf16 (uint4) of e4m3(code) * s: the e4m3 value is
+// exact in f16 and f32, the f32 product rounds once to bf16.
+__device__ __forceinline__ uint4 dequant8(const uint2& c, float s) {
+  const uint32_t w[2] = {c.x, c.y};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t f2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(f2) : "h"(static_cast<uint16_t>(h ? w[j] >> 16 : w[j] & 0xFFFF)));
+      const float2 p = fmul2(make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(f2 & 0xFFFF))),
+                                         __half2float(__ushort_as_half(static_cast<unsigned short>(f2 >> 16)))),
+                             make_float2(s, s));
+      o[2 * j + h] = pack_bf16x2(p.x, p.y);
+    }
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Warp per row, NCH8 chunks of 8 codes per lane (cols = NCH8 * 256): lane l
+// handles chunks l, l + 32, ... so each warp load covers 256 contiguous code
+// bytes and each warp store 512 contiguous output bytes.
+template <int NCH8>
+__global__ void __launch_bounds__(WARPS * 32)
+    dequant_row_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ scales,
+                       __nv_bfloat16* __restrict__ out, int64_t rows, int64_t out_stride, int mode) {
+  constexpr int64_t COLS = NCH8 * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * WARPS;
+  const float s_tensor = (mode == WF_SCALE_TENSOR) ? scales[0] : 1.f;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5); r < rows; r += nwarps) {
+    const float s = (mode == WF_SCALE_TOKEN) ? __ldg(scales + r) : s_tensor;
+    const uint2* c2 = reinterpret_cast<const uint2*>(codes + r * COLS);
+    uint4* o4 = reinterpret_cast<uint4*>(out + r * out_stride);
+    uint2 c[NCH8];
+#pragma unroll
+    for (int i = 0; i < NCH8; ++i) c[i] = __ldcs(c2 + lane + 32 * i);
+#pragma unroll
+    for (int i = 0; i < NCH8; ++i) o4[lane + 32 * i] = dequant8(c[i], s);
+  }
+}
+
 static int grid_for(int64_t work_items, int threads) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -414,9 +483,25 @@ extern "C" int wf_kv_dequant(const uint8_t* codes, const float* scales, void* ou
   if (mode != WF_SCALE_NONE && mode != WF_SCALE_TENSOR && mode != WF_SCALE_TOKEN)
     return fail(WF_ERR_INVALID_ARG, "wf_kv_dequant: bad mode");
   if (rows == 0) return WF_OK;
-  const int g = grid_for(rows * (cols / 8), 256);
-  dequant_kernel<<<g, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      codes, scales, static_cast<__nv_bfloat16*>(out), rows, cols, out_row_stride, mode);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool fast = (cols == 1536 || cols == 5120) && aligned16(out) && out_row_stride % 8 == 0;
+  if (fast) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = (rows + WARPS - 1) / WARPS;
+    const int64_t cap = static_cast<int64_t>(sms) * 8;
+    const unsigned blocks = static_cast<unsigned>(want < cap ? want : cap);
+    auto bf = static_cast<__nv_bfloat16*>(out);
+    if (cols == 1536)
+      dequant_row_kernel<6><<<blocks, WARPS * 32, 0, s>>>(codes, scales, bf, rows, out_row_stride, mode);
+    else
+      dequant_row_kernel<20><<<blocks, WARPS * 32, 0, s>>>(codes, scales, bf, rows, out_row_stride, mode);
+  } else {
+    const int g = grid_for(rows * (cols / 8), 256);
+    dequant_kernel<<<g, 256, 0, s>>>(codes, scales, static_cast<__nv_bfloat16*>(out), rows, cols, out_row_stride,
+                                     mode);
+  }
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }
