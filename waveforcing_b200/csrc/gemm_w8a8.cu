@@ -6,7 +6,8 @@
 //   CTA tile 128 x 256, K step 128 bytes (one 128-byte swizzle row), 4-stage
 //   TMA ring.  warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
 //   warps 4-7 = epilogue (thread t owns accumulator row t = TMEM lane t):
-//   scale, bias, bf16 convert and store straight from registers.
+//   scale and bias from per-tile shared-memory copies, bf16 convert into a
+//   double-buffered 128 x 64 swizzled staging tile, TMA bulk store.
 // Also here: load-time per-channel weight quantisation and per-token dynamic
 // activation quantisation (the per-row forms of fp8.py:32-36 and :47-48).
 #include <cuda_runtime.h>
@@ -23,9 +24,13 @@ constexpr int BK = 128;  // bytes (= elements for 8-bit types)
 constexpr int NS = 4;
 constexpr int A_TILE = BM * BK;  // 16 KB
 constexpr int B_TILE = BN * BK;  // 32 KB
+constexpr int OUT_COLS = 64;               // bf16 columns per staging tile (128 bytes)
+constexpr int OUT_TILE = BM * OUT_COLS * 2;  // 16 KB
 constexpr int NBARS = 2 * NS + 5;
-constexpr int SMEM_BYTES = 1024 + NS * (A_TILE + B_TILE) + NBARS * 8 + 16;
+constexpr int SMEM_BYTES = 1024 + NS * (A_TILE + B_TILE) + 2 * OUT_TILE + BN * 4 /*w_scale*/ + BN * 2 /*bias*/ +
+                           16 /*flags*/ + NBARS * 8 + 16;
 constexpr int THREADS = 256;
+constexpr uint32_t EPI_BAR = 1;  // named barrier of the four epilogue warps
 
 __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
@@ -46,13 +51,17 @@ template <bool IS_INT8>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const float* __restrict__ x_scale, const float* __restrict__ w_scale,
-                     const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y, int M, int N, int K,
-                     long long y_stride, int per_token) {
+                     const __nv_bfloat16* __restrict__ bias, const __grid_constant__ CUtensorMap tmY, int M, int N,
+                     int K, int per_token) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + NS * A_TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + NS * B_TILE);
+  uint8_t* sOut = sB + NS * B_TILE;                                    // [2][OUT_TILE], 1024-aligned
+  float* sSW = reinterpret_cast<float*>(sOut + 2 * OUT_TILE);          // [BN]
+  __nv_bfloat16* sBias = reinterpret_cast<__nv_bfloat16*>(sSW + BN);  // [BN]
+  int* sOk = reinterpret_cast<int*>(sBias + BN);                       // [4]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOk + 4);
   uint64_t* full = bars;
   uint64_t* empty = bars + NS;
   uint64_t* acc_full = empty + NS;  // [2]
@@ -147,54 +156,76 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    // Per tile: the four warps agree (through sOk and the named barrier) on
+    // whether the accumulator arrived, so either all of them run the tile or
+    // none does and no named barrier is left waiting.  Per 64-column group:
+    // TMEM -> registers -> scale/bias -> bf16 into staging buffer (grp & 1),
+    // then one thread stores the 128 x 64 box with TMA.  Before the barrier
+    // that precedes store grp, that thread waits until store grp-1 has read
+    // its buffer, so the next group can refill it.
+    const int et = threadIdx.x - 128;  // epilogue thread = accumulator row = TMEM lane
     const int wq = warp - 4;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const float sw_t = per_token ? 0.f : __ldg(w_scale);
-    int local = 0;
+    const __nv_bfloat16 zero_b = __float2bfloat16_rn(0.f);
+    int local = 0, grp = 0;
     for (int t = blockIdx.x; t < n_total; t += gridDim.x, ++local) {
       const int buf = local & 1;
-      const bool ok =
+      const bool okw =
           __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (local >> 1) & 1, abort_flag, ST_GEMM_EPILOGUE));
-      if (!ok) break;
-      tc_fence_after();
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
-      const int row = m0 + wq * 32 + lane;
+      for (int j = et; j < BN; j += 128) {
+        const int n = n0 + j < N ? n0 + j : N - 1;
+        sSW[j] = per_token ? __ldg(w_scale + n) : sw_t;
+        sBias[j] = bias ? bias[n] : zero_b;
+      }
+      if (lane == 0) sOk[wq] = okw ? 1 : 0;
+      named_bar_sync(EPI_BAR, 128);
+      if (!(sOk[0] & sOk[1] & sOk[2] & sOk[3])) break;
+      tc_fence_after();
+      const int row = m0 + et;
       const float sx = (row < M) ? (per_token ? __ldg(x_scale + row) : __ldg(x_scale)) : 0.f;
-      __nv_bfloat16* yrow = y + static_cast<long long>(row) * y_stride;
+      const float2 sx2 = make_float2(sx, sx);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32x32b_x32(tbase + buf * BN + lane_off + c, r);
-        if (c + 32 == BN) {
+      for (int g = 0; g < BN / OUT_COLS; ++g, ++grp) {
+        uint32_t r[OUT_COLS];
+        tmem_ld32x32b_x64(tbase + buf * BN + lane_off + g * OUT_COLS, r);
+        if (g == BN / OUT_COLS - 1) {
           // every column of this accumulator is in registers: hand it back
           tc_fence_before();
           mbar_arrive(&acc_empty[buf]);
         }
-        const int n = n0 + c;
-        if (row < M && n < N) {
-          float f[32];
+        uint8_t* so = sOut + (grp & 1) * OUT_TILE + et * 128;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float acc = IS_INT8 ? static_cast<float>(static_cast<int>(r[i])) : __uint_as_float(r[i]);
-            const int ni = n + i < N ? n + i : N - 1;
-            const float sw = per_token ? __ldg(w_scale + ni) : sw_t;
-            const float b = bias ? __bfloat162float(bias[ni]) : 0.f;
-            f[i] = fmaf(acc * sx, sw, b);
+        for (int c = 0; c < OUT_COLS / 8; ++c) {
+          const float* sw = sSW + g * OUT_COLS + c * 8;
+          const uint4 bb = *reinterpret_cast<const uint4*>(sBias + g * OUT_COLS + c * 8);
+          const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
+          uint32_t pk[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t r0 = r[c * 8 + 2 * i], r1 = r[c * 8 + 2 * i + 1];
+            const float2 acc = IS_INT8 ? make_float2(static_cast<float>(static_cast<int>(r0)),
+                                                     static_cast<float>(static_cast<int>(r1)))
+                                       : make_float2(__uint_as_float(r0), __uint_as_float(r1));
+            const float2 b2 = make_float2(__uint_as_float(bw[i] << 16), __uint_as_float(bw[i] & 0xFFFF0000u));
+            const float2 f = ffma2(fmul2(acc, sx2), make_float2(sw[2 * i], sw[2 * i + 1]), b2);
+            pk[i] = pack_bf16x2(f.x, f.y);
           }
-          if (n + 32 <= N) {
-            uint4* d4 = reinterpret_cast<uint4*>(yrow + n);
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              d4[v] = make_uint4(pack_bf16x2(f[8 * v], f[8 * v + 1]), pack_bf16x2(f[8 * v + 2], f[8 * v + 3]),
-                                 pack_bf16x2(f[8 * v + 4], f[8 * v + 5]), pack_bf16x2(f[8 * v + 6], f[8 * v + 7]));
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (n + i < N) yrow[n + i] = __float2bfloat16_rn(f[i]);
-          }
+          // 128-byte swizzle: 16-byte chunk c of row et lives at chunk c ^ (et & 7)
+          *reinterpret_cast<uint4*>(so + ((c ^ (et & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+        fence_proxy_async_smem();
+        if (et == 0) bulk_wait_read_all();
+        named_bar_sync(EPI_BAR, 128);
+        if (et == 0) {
+          tma_store_2d(&tmY, sOut + (grp & 1) * OUT_TILE, n0 + g * OUT_COLS, m0);
+          bulk_commit_group();
         }
       }
     }
+    if (et == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -289,6 +320,14 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* _
   if (lane == 0) x_scale[m] = s;
 }
 
+// bf16 [rows, cols] output with a row stride, boxes of 64 columns x 128 rows.
+static int make_map_out(CUtensorMap* map, const void* p, int rows, int cols, int64_t row_stride) {
+  const uint64_t gdim[2] = {(uint64_t)cols, (uint64_t)rows};
+  const uint64_t gstr[1] = {(uint64_t)row_stride * 2};
+  const uint32_t box[2] = {(uint32_t)OUT_COLS, (uint32_t)BM};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p, gdim, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 static int make_map_2d(CUtensorMap* map, const void* p, int rows, int cols, int box_rows) {
   const uint64_t gdim[2] = {(uint64_t)cols, (uint64_t)rows};
   const uint64_t gstr[1] = {(uint64_t)cols};
@@ -314,10 +353,11 @@ extern "C" int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq
   if (!xq || !wq || !y || !x_scale || !w_scale || !aligned16(xq) || !aligned16(wq) || !aligned16(y) ||
       y_row_stride < N || y_row_stride % 8)
     return fail(WF_ERR_INVALID_ARG, "wf_gemm_w8a8: null/misaligned pointer or bad y stride");
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ty;
   int rc;
   if ((rc = make_map_2d(&ta, xq, M, K, BM)) != WF_OK) return rc;
   if ((rc = make_map_2d(&tb, wq, N, K, BN)) != WF_OK) return rc;
+  if ((rc = make_map_out(&ty, y, M, N, y_row_stride)) != WF_OK) return rc;
   static thread_local int configured_dev = -1;
   int dev = 0;
   WFK_CUDA_TRY(cudaGetDevice(&dev));
@@ -335,15 +375,11 @@ extern "C" int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int per_token = scale_mode == WF_SCALE_TOKEN;
   if (qtype == WF_DTYPE_S8)
-    gemm_w8a8_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, x_scale, w_scale,
-                                                             static_cast<const __nv_bfloat16*>(bias),
-                                                             static_cast<__nv_bfloat16*>(y), M, N, K,
-                                                             (long long)y_row_stride, per_token);
+    gemm_w8a8_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(
+        ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token);
   else
-    gemm_w8a8_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, x_scale, w_scale,
-                                                              static_cast<const __nv_bfloat16*>(bias),
-                                                              static_cast<__nv_bfloat16*>(y), M, N, K,
-                                                              (long long)y_row_stride, per_token);
+    gemm_w8a8_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(
+        ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }
