@@ -38,6 +38,9 @@ extern "C" {
 #define WF_SCALE_TENSOR 1
 #define WF_SCALE_TOKEN 2
 
+#define WF_ACT_NONE 0
+#define WF_ACT_GELU_TANH 1
+
 /* ------------------------------------------------------------ library */
 
 /* Message of the last failed call on this host thread ("" if none). */
@@ -144,6 +147,14 @@ int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, int64_t K, 
  * bias may be NULL.  K must be a multiple of 128 and N of 16. */
 int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq, const float* w_scale, const void* bias,
                  void* y, int M, int N, int K, int64_t y_row_stride, int qtype, int scale_mode, void* stream);
+
+/* wf_gemm_w8a8 with an activation applied to the bf16-rounded output in the
+ * epilogue.  WF_ACT_GELU_TANH is the FFN's GELU(approximate="tanh") after
+ * fc_in (the Wan block FFN, causal_model.py:309-420): fc_in and the GELU of the
+ * reference become one call.  WF_ACT_NONE is wf_gemm_w8a8. */
+int wf_gemm_w8a8_act(const void* xq, const float* x_scale, const void* wq, const float* w_scale, const void* bias,
+                     void* y, int M, int N, int K, int64_t y_row_stride, int qtype, int scale_mode, int activation,
+                     void* stream);
 
 /* ---------------------------------------------------------------- RoPE */
 

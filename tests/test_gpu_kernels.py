@@ -265,14 +265,22 @@ def test_kv_quant_publish_matches_oracle(n_dst):
 
 # ----------------------------------------------------------------------- W8A8
 @pytest.mark.parametrize("qtype", ["e4m3", "s8"])
-def test_quantisers_bit_exact(qtype):
+@pytest.mark.parametrize("Kd", [256, 1536, 5120, 8960])
+def test_quantisers_bit_exact(qtype, Kd):
+    """Weight and activation quantisers against the oracle; K covers the
+    register-resident rows (1536, 5120) and the two-pass rows (256, 8960);
+    activations include wide magnitudes, zero rows and -0."""
     K = _kernels()
     from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
 
     qt = WF_DTYPE_E4M3 if qtype == "e4m3" else WF_DTYPE_S8
-    rng = np.random.default_rng(2)
-    w = o_codec.bf16_round((rng.standard_normal((96, 256)) * 0.02).astype(np.float32))
-    x = o_codec.bf16_round((rng.standard_normal((70, 256)) * 2).astype(np.float32))
+    rng = np.random.default_rng(2 + Kd)
+    w = o_codec.bf16_round((rng.standard_normal((96, Kd)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((70, Kd)) * 2 * np.exp(rng.standard_normal((70, Kd)) * 2)
+    x[3] = 0.0
+    x[4] = -0.0
+    x[5, ::3] = -0.0
+    x = o_codec.bf16_round(x.astype(np.float32))
     wq, ws = K.weight_quant(_bf16_gpu(w), qt)
     xq, xs = K.act_quant(_bf16_gpu(x), qt)
     rwq, rws = o_w8a8.quant_weight(w, qtype, per_channel=True)
@@ -301,6 +309,29 @@ def test_gemm_w8a8_matches_oracle(qtype, M, N, K_):
     rwq, rws = o_w8a8.quant_weight(w, qtype)
     rxq, rxs = o_w8a8.quant_act(x, qtype)
     ref = o_w8a8.gemm(rxq, rxs, rwq, rws, b, qtype)
+    assert _rel(_f32(y), ref) <= 1e-2
+
+
+@pytest.mark.parametrize("qtype", ["e4m3", "s8"])
+def test_gemm_w8a8_gelu_epilogue(qtype):
+    """fc_in + GELU(tanh) in one kernel against the oracle linear followed by
+    torch's tanh GELU on the bf16-rounded output."""
+    K = _kernels()
+    from waveforcing_b200._lib import WF_ACT_GELU_TANH, WF_DTYPE_E4M3, WF_DTYPE_S8
+
+    qt = WF_DTYPE_E4M3 if qtype == "e4m3" else WF_DTYPE_S8
+    rng = np.random.default_rng(31)
+    M, N, K_ = 600, 8960, 1536
+    w = o_codec.bf16_round((rng.standard_normal((N, K_)) * 0.02).astype(np.float32))
+    x = o_codec.bf16_round((rng.standard_normal((M, K_)) * 2).astype(np.float32))
+    b = o_codec.bf16_round((rng.standard_normal(N) * 0.1).astype(np.float32))
+    wq, ws = K.weight_quant(_bf16_gpu(w), qt)
+    xq, xs = K.act_quant(_bf16_gpu(x), qt)
+    y = K.gemm_w8a8(xq, xs, wq, ws, _bf16_gpu(b), qt, activation=WF_ACT_GELU_TANH)
+    rwq, rws = o_w8a8.quant_weight(w, qtype)
+    rxq, rxs = o_w8a8.quant_act(x, qtype)
+    lin = o_codec.bf16_round(o_w8a8.gemm(rxq, rxs, rwq, rws, b, qtype).astype(np.float32))
+    ref = torch.nn.functional.gelu(torch.from_numpy(lin).double(), approximate="tanh").numpy()
     assert _rel(_f32(y), ref) <= 1e-2
 
 

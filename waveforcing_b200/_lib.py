@@ -21,6 +21,7 @@ HEADER_PATH = os.path.join(os.path.dirname(_PKG), "include", "wfk.h")
 WF_OK = 0
 WF_DTYPE_BF16, WF_DTYPE_E4M3, WF_DTYPE_S8 = 0, 1, 2
 WF_SCALE_NONE, WF_SCALE_TENSOR, WF_SCALE_TOKEN = 0, 1, 2
+WF_ACT_NONE, WF_ACT_GELU_TANH = 0, 1
 
 _vp = C.c_void_p
 _i64 = C.c_int64
@@ -46,6 +47,7 @@ _SIGS = {
     "wf_weight_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp]),
     "wf_act_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "wf_gemm_w8a8": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
+    "wf_gemm_w8a8_act": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _vp]),
     "wf_rope_apply": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i64, _vp]),
     "wf_ln_modulate": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _f32, _vp]),
     "wf_gate_residual": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),

@@ -12,7 +12,10 @@
 // activation quantisation (the per-row forms of fp8.py:32-36 and :47-48).
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "host_util.h"
+#include "quant_rows.cuh"
 #include "sm100.cuh"
 
 namespace wfk {
@@ -43,6 +46,19 @@ __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, uint6
   return true;
 }
 
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// GELU with the tanh approximation (torch GELU(approximate="tanh")):
+// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), tanh(u) = 1 - 2 / (1 + e^(2u)).
+// e^(2u) saturates to inf / 0 for large |u|, giving tanh = +-1.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  const float e = ex2_approx(u * 2.8853900817779268f);  // e^(2u)
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
+  return 0.5f * x * (2.f - 2.f * r);
+}
+
 // Persistent: CTA c processes output tiles c, c + gridDim.x, ... (tile t ->
 // m-tile t % m_tiles, n-tile t / m_tiles, so CTAs running together share the
 // same weight tile in L2).  The TMEM accumulator is double buffered: the MMA
@@ -52,7 +68,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const float* __restrict__ x_scale, const float* __restrict__ w_scale,
                      const __nv_bfloat16* __restrict__ bias, const __grid_constant__ CUtensorMap tmY, int M, int N,
-                     int K, int per_token) {
+                     int K, int per_token, int act) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sA = smem;
@@ -211,7 +227,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                        : make_float2(__uint_as_float(r0), __uint_as_float(r1));
             const float2 b2 = make_float2(__uint_as_float(bw[i] << 16), __uint_as_float(bw[i] & 0xFFFF0000u));
             const float2 f = ffma2(fmul2(acc, sx2), make_float2(sw[2 * i], sw[2 * i + 1]), b2);
-            pk[i] = pack_bf16x2(f.x, f.y);
+            pk[i] = act == WF_ACT_GELU_TANH ? pack_bf16x2(gelu_tanh(bf16_round(f.x)), gelu_tanh(bf16_round(f.y)))
+                                            : pack_bf16x2(f.x, f.y);
           }
           // 128-byte swizzle: 16-byte chunk c of row et lives at chunk c ^ (et & 7)
           *reinterpret_cast<uint4*>(so + ((c ^ (et & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -273,54 +290,64 @@ __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, uint8_t
   if (lane == 0) w_scale[n] = s;
 }
 
-// Per-token activation quantisation with bf16 scale math (fp8.py:47-48 per row).
-__global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ xq,
-                                 float* __restrict__ x_scale, int64_t M, int64_t K, int64_t xs, int is_int8) {
+// Per-token activation quantisation with bf16 scale math (fp8.py:47-48 per
+// row): s = max(bf16(amax|x| / qmax), bf16(1e-8)), code = e4m3(bf16(x / s)) or
+// clamp(rint(bf16(x / s)), -127, 127).  A warp per row; the row stays in
+// registers for NCH8 > 0 (K = NCH8 * 256), otherwise it is read twice.  The
+// division is one multiply by RN(1/s) (exact for bf16 x and s; see
+// quant_rows.cuh); rows with a non-finite scale take the IEEE division.
+template <bool I8, int NCH8>
+__global__ void __launch_bounds__(256)
+    act_quant_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ xq, float* __restrict__ x_scale,
+                     int64_t M, int64_t K, int64_t xs) {
+  using namespace wfk::quant;
   const int lane = threadIdx.x & 31;
-  const int64_t m = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (m >= M) return;
-  const __nv_bfloat16* row = x + m * xs;
-  const uint4* r4 = reinterpret_cast<const uint4*>(row);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t nch = K / 8;
-  float amax = 0.f;
-  for (int64_t c = lane; c < nch; c += 32) {
-    const uint4 v = __ldg(r4 + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  for (int64_t m = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += nwarps) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(x + m * xs);
+    uint2* out = reinterpret_cast<uint2*>(xq + m * K);
+    uint32_t m2 = 0;
+    uint4 buf[NCH8 > 0 ? NCH8 : 1];
+    if constexpr (NCH8 > 0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(w[i] << 16)), fabsf(__uint_as_float(w[i] & 0xFFFF0000u))));
-  }
-  amax = warp_max(amax);
-  const float qmax = is_int8 ? 127.f : 448.f;
-  float s = bf16r(__fdiv_rn(amax, qmax));
-  const float smin = bf16r(1e-8f);
-  s = s < smin ? smin : s;
-  for (int64_t c = lane; c < nch; c += 32) {
-    const uint4 v = __ldg(r4 + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t out[2] = {0, 0};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float q0 = bf16r(__fdiv_rn(__uint_as_float(w[i] << 16), s));
-      const float q1 = bf16r(__fdiv_rn(__uint_as_float(w[i] & 0xFFFF0000u), s));
-      uint32_t pair;
-      if (is_int8) {
-        const int a = static_cast<int>(fminf(fmaxf(rintf(q0), -127.f), 127.f));
-        const int b = static_cast<int>(fminf(fmaxf(rintf(q1), -127.f), 127.f));
-        pair = (static_cast<uint32_t>(a) & 0xFF) | ((static_cast<uint32_t>(b) & 0xFF) << 8);
-      } else {
-        uint16_t p;
-        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(p) : "f"(fabsf(q1)), "f"(fabsf(q0)));
-        pair = p | ((__float_as_uint(q0) >> 24) & 0x80u) | ((__float_as_uint(q1) >> 16) & 0x8000u);
+      for (int i = 0; i < NCH8; ++i) {
+        buf[i] = __ldg(r4 + lane + 32 * i);
+        m2 = amax8_bits(buf[i], m2);
       }
-      out[i >> 1] |= pair << ((i & 1) * 16);
+    } else {
+      for (int64_t c = lane; c < nch; c += 32) m2 = amax8_bits(__ldg(r4 + c), m2);
     }
-    reinterpret_cast<uint2*>(xq + m * K)[c] = make_uint2(out[0], out[1]);
+    const RowQuant q = make_rowq(warp_amax_bits(m2), I8 ? 127.f : 448.f);
+    auto quant8v = [&](const uint4& v) -> uint2 {
+      if (q.finite) {
+        if constexpr (I8)
+          return make_uint2(i8x2_fast(v.x, q.r) | (i8x2_fast(v.y, q.r) << 16),
+                            i8x2_fast(v.z, q.r) | (i8x2_fast(v.w, q.r) << 16));
+        else
+          return make_uint2(quant4_fast(v.x, v.y, q.r), quant4_fast(v.z, v.w, q.r));
+      }
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[2] = {0, 0};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float b0 = bf16_round_f(__fdiv_rn(__uint_as_float(w[i] << 16), q.s));
+        const float b1 = bf16_round_f(__fdiv_rn(__uint_as_float(w[i] & 0xFFFF0000u), q.s));
+        const uint32_t c = I8 ? (i8_slow(b0) | (i8_slow(b1) << 8)) : (e4m3_encode_sw(b0) | (e4m3_encode_sw(b1) << 8));
+        o[i >> 1] |= c << ((i & 1) * 16);
+      }
+      return make_uint2(o[0], o[1]);
+    };
+    if constexpr (NCH8 > 0) {
+#pragma unroll
+      for (int i = 0; i < NCH8; ++i) out[lane + 32 * i] = quant8v(buf[i]);
+    } else {
+      for (int64_t c = lane; c < nch; c += 32) out[c] = quant8v(__ldg(r4 + c));
+    }
+    if (lane == 0) x_scale[m] = q.s;
   }
-  if (lane == 0) x_scale[m] = s;
 }
 
-// bf16 [rows, cols] output with a row stride, boxes of 64 columns x 128 rows.
 static int make_map_out(CUtensorMap* map, const void* p, int rows, int cols, int64_t row_stride) {
   const uint64_t gdim[2] = {(uint64_t)cols, (uint64_t)rows};
   const uint64_t gstr[1] = {(uint64_t)row_stride * 2};
@@ -341,9 +368,11 @@ static int make_map_2d(CUtensorMap* map, const void* p, int rows, int cols, int 
 using namespace wfk;
 using namespace wfk::gemm;
 
-extern "C" int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq, const float* w_scale,
-                            const void* bias, void* y, int M, int N, int K, int64_t y_row_stride, int qtype,
-                            int scale_mode, void* stream) {
+extern "C" int wf_gemm_w8a8_act(const void* xq, const float* x_scale, const void* wq, const float* w_scale,
+                                const void* bias, void* y, int M, int N, int K, int64_t y_row_stride, int qtype,
+                                int scale_mode, int activation, void* stream) {
+  if (activation != WF_ACT_NONE && activation != WF_ACT_GELU_TANH)
+    return fail(WF_ERR_INVALID_ARG, "wf_gemm_w8a8_act: activation must be WF_ACT_NONE or WF_ACT_GELU_TANH");
   if (qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8)
     return fail(WF_ERR_UNSUPPORTED, "wf_gemm_w8a8: qtype must be WF_DTYPE_E4M3 or WF_DTYPE_S8");
   if (scale_mode != WF_SCALE_TENSOR && scale_mode != WF_SCALE_TOKEN)
@@ -376,12 +405,19 @@ extern "C" int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq
   const int per_token = scale_mode == WF_SCALE_TOKEN;
   if (qtype == WF_DTYPE_S8)
     gemm_w8a8_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(
-        ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token);
+        ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token, activation);
   else
     gemm_w8a8_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(
-        ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token);
+        ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token, activation);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
+}
+
+extern "C" int wf_gemm_w8a8(const void* xq, const float* x_scale, const void* wq, const float* w_scale,
+                            const void* bias, void* y, int M, int N, int K, int64_t y_row_stride, int qtype,
+                            int scale_mode, void* stream) {
+  return wf_gemm_w8a8_act(xq, x_scale, wq, w_scale, bias, y, M, N, K, y_row_stride, qtype, scale_mode, WF_ACT_NONE,
+                          stream);
 }
 
 extern "C" int wf_weight_quant(const void* w, void* wq, float* w_scale, int64_t N, int64_t K, int qtype,
@@ -402,10 +438,33 @@ extern "C" int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, 
     return fail(WF_ERR_INVALID_ARG, "wf_act_quant: bad arguments");
   if (qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8) return fail(WF_ERR_UNSUPPORTED, "wf_act_quant: qtype");
   if (M == 0) return WF_OK;
-  const unsigned blocks = static_cast<unsigned>((M + 7) / 8);
-  act_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<uint8_t*>(xq), x_scale, M, K, x_row_stride,
-      qtype == WF_DTYPE_S8);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (M + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(sms) * 8;
+  const unsigned blocks = static_cast<unsigned>(want < cap ? want : cap);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto xb = static_cast<const __nv_bfloat16*>(x);
+  auto qb = static_cast<uint8_t*>(xq);
+  auto go = [&](auto i8, auto nch) {
+    act_quant_kernel<decltype(i8)::value, decltype(nch)::value><<<blocks, 256, 0, s>>>(xb, qb, x_scale, M, K,
+                                                                                      x_row_stride);
+  };
+  auto by_k = [&](auto i8) {
+    if (K == 1536)
+      go(i8, std::integral_constant<int, 6>());
+    else if (K == 3072)
+      go(i8, std::integral_constant<int, 12>());
+    else if (K == 5120)
+      go(i8, std::integral_constant<int, 20>());
+    else
+      go(i8, std::integral_constant<int, 0>());
+  };
+  if (qtype == WF_DTYPE_S8)
+    by_k(std::true_type());
+  else
+    by_k(std::false_type());
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

@@ -74,7 +74,7 @@ extern "C" unsigned int wfk_status_take_exchange(void);
 
 extern "C" const char* wf_last_error(void) { return wfk::g_last_error.c_str(); }
 
-extern "C" int wf_version(void) { return 1; }
+extern "C" int wf_version(void) { return 2; }
 
 extern "C" unsigned int wf_status_take(void) {
   cudaDeviceSynchronize();

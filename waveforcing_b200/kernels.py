@@ -149,15 +149,18 @@ def act_quant(x: torch.Tensor, qtype: int = L.WF_DTYPE_E4M3, xq: torch.Tensor | 
 
 
 def gemm_w8a8(xq, xs, wq, ws, bias=None, qtype: int = L.WF_DTYPE_E4M3, scale_mode: int = L.WF_SCALE_TOKEN,
-              out: torch.Tensor | None = None) -> torch.Tensor:
+              out: torch.Tensor | None = None, activation: int = L.WF_ACT_NONE) -> torch.Tensor:
+    """y = (xq wq^T) * xs * ws + bias in bf16; activation WF_ACT_GELU_TANH applies
+    GELU(tanh) to the bf16-rounded result in the same kernel."""
     _need_cuda(xq, wq)
     M, K = xq.shape
     N = wq.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
     bp = bias.data_ptr() if bias is not None else 0
-    L.check(L.lib().wf_gemm_w8a8(xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(), bp, out.data_ptr(),
-                                 M, N, K, out.stride(0), qtype, scale_mode, _stream()), "wf_gemm_w8a8")
+    L.check(L.lib().wf_gemm_w8a8_act(xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(), bp, out.data_ptr(),
+                                     M, N, K, out.stride(0), qtype, scale_mode, activation, _stream()),
+            "wf_gemm_w8a8_act")
     return out
 
 

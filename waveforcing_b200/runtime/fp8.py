@@ -53,7 +53,7 @@ class WfW8A8Linear(nn.Module):
         self.register_buffer("bias", bias.detach().to(torch.bfloat16) if bias is not None else None)
         self._ws = None
 
-    def _raw(self, x2: torch.Tensor) -> torch.Tensor:
+    def _raw(self, x2: torch.Tensor, activation: int = L.WF_ACT_NONE) -> torch.Tensor:
         x2 = x2.to(torch.bfloat16)
         if x2.stride(-1) != 1 or x2.stride(0) % 8:
             x2 = x2.contiguous()
@@ -65,12 +65,19 @@ class WfW8A8Linear(nn.Module):
                 self._ws = torch.empty(1, dtype=torch.int32, device=x2.device)
             xq, xs = kernels.kv_quant(x2, L.WF_SCALE_TENSOR, workspace=self._ws)
             mode = L.WF_SCALE_TENSOR
-        return kernels.gemm_w8a8(xq, xs, self.w_q, self.w_scale, self.bias, self.qtype, mode)
+        return kernels.gemm_w8a8(xq, xs, self.w_q, self.w_scale, self.bias, self.qtype, mode, activation=activation)
 
     def forward(self, x: torch.Tensor):
         shape = x.shape
         y = self._raw(x.reshape(-1, shape[-1]))
         return y.reshape(*shape[:-1], self.out_features), None
+
+    def forward_gelu(self, x: torch.Tensor) -> torch.Tensor:
+        """GELU(approximate="tanh") of this linear's bf16 output, fused into the
+        GEMM epilogue (the FFN's fc_in + activation)."""
+        shape = x.shape
+        y = self._raw(x.reshape(-1, shape[-1]), L.WF_ACT_GELU_TANH)
+        return y.reshape(*shape[:-1], self.out_features)
 
 
 def concat_w8a8(mods: list["WfW8A8Linear"]) -> "WfW8A8Linear":

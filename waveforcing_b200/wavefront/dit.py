@@ -355,6 +355,8 @@ class WanDiT(nn.Module):
             fi = b.ffn.fc_in
             if fused and type(fi) is nn.Linear:
                 a = torch._addmm_activation(fi.bias, h, fi.weight.t(), use_gelu=True)  # cuBLASLt bias+GELU(tanh)
+            elif fused and hasattr(fi, "forward_gelu"):
+                a = fi.forward_gelu(h)  # W8A8 GEMM with GELU(tanh) in its epilogue
             else:
                 a = F.gelu(_lin(fi, h), approximate="tanh")
             y = _lin(b.ffn.fc_out, a)
