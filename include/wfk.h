@@ -156,6 +156,33 @@ int wf_gemm_w8a8_act(const void* xq, const float* x_scale, const void* wq, const
                      void* y, int M, int N, int K, int64_t y_row_stride, int qtype, int scale_mode, int activation,
                      void* stream);
 
+/* ------------------------------------------------------ context assembly */
+
+#define WF_SEG_COPY 0    /* bf16 rows copied */
+#define WF_SEG_ROPE 1    /* bf16 rows rotated by per-row f32 cos/sin [rows, head_dim/2] (interleaved pairs) */
+#define WF_SEG_DEQUANT 2 /* e4m3 codes with per-row f32 scales -> bf16(e4m3(code) * scale) */
+
+/* One source of rows of a K or V context buffer. */
+typedef struct wf_kv_segment {
+  int32_t kind;           /* WF_SEG_* */
+  int32_t reserved;       /* 0 */
+  const void* src;        /* bf16 rows (COPY, ROPE) or u8 codes (DEQUANT); 16-byte aligned (8 for codes) */
+  const float* aux0;      /* ROPE: cos table [rows, head_dim/2]; DEQUANT: scales [rows]; COPY: NULL */
+  const float* aux1;      /* ROPE: sin table [rows, head_dim/2]; else NULL */
+  void* dst;              /* bf16 rows, 16-byte aligned */
+  int64_t rows;
+  int64_t src_row_stride; /* elements of the source type (bf16 or bytes), >= cols, multiple of 8 */
+  int64_t dst_row_stride; /* bf16 elements, >= cols, multiple of 8 */
+} wf_kv_segment;
+
+/* Assembles the paged exchange's K/V context of one layer in one launch:
+ * up to 24 segments, each row copied, re-RoPEd or dequantised into place.
+ * Replaces the per-layer anchor/working/self copies of
+ * wave_rt/denoiser/exchange/paged.py:226-237, the anchor re-RoPE of
+ * exchange/common.py:84-87 (rotated straight into the buffer) and the
+ * receive-side dequantisation of FP8 pages.  cols = H * head_dim. */
+int wf_kv_assemble(const wf_kv_segment* segs, int n_segs, int64_t cols, int head_dim, void* stream);
+
 /* ---------------------------------------------------------------- RoPE */
 
 /* Interleaved (non-neox) rotary embedding, y = x * (cos + i sin) on complex

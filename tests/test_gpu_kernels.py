@@ -355,6 +355,41 @@ def test_gemm_per_tensor_matches_reference_golden(golden):
         assert _rel(_f32(y), bits_to_f32(g[f"c{i}_y"])) <= 1e-2, i
 
 
+# ----------------------------------------------------------- context assembly
+def test_kv_assemble_segments_match_separate_kernels():
+    """Copy, RoPE and dequant segments of one launch against torch copies,
+    wf_rope_apply and wf_kv_dequant, into a strided destination."""
+    K = _kernels()
+    from waveforcing_b200 import _lib as L
+
+    torch.manual_seed(3)
+    T, H, D = 300, 3, 128
+    HD = H * D
+    ku = torch.randn(T, H, D, device=DEV).to(torch.bfloat16)
+    kr = torch.randn(2 * T, H, D, device=DEV).to(torch.bfloat16)[::2]  # strided rows
+    cos = torch.rand(T, D // 2, device=DEV) * 2 - 1
+    sin = torch.rand(T, D // 2, device=DEV) * 2 - 1
+    x = torch.randn(T + 17, HD, device=DEV).to(torch.bfloat16)
+    codes, scales = K.kv_quant(x, L.WF_SCALE_TOKEN)
+    dst = torch.zeros(4 * T, HD + 64, device=DEV, dtype=torch.bfloat16)
+    dst_ptr, dst_st = dst.data_ptr(), dst.stride(0)
+    segs = [(L.WF_SEG_ROPE, ku.data_ptr(), cos.data_ptr(), sin.data_ptr(), dst_ptr, T, HD, dst_st),
+            (L.WF_SEG_COPY, kr.data_ptr(), 0, 0, dst_ptr + T * dst_st * 2, T, kr.stride(0), dst_st),
+            (L.WF_SEG_COPY, kr.data_ptr(), 0, 0, dst_ptr + 2 * T * dst_st * 2, 0, kr.stride(0), dst_st),
+            (L.WF_SEG_DEQUANT, codes.data_ptr(), scales.data_ptr(), 0, dst_ptr + 2 * T * dst_st * 2, T + 17, HD,
+             dst_st)]
+    K.kv_assemble(segs, HD, D)
+    torch.cuda.synchronize()
+    assert torch.equal(dst[:T, :HD], K.rope_apply(ku, cos, sin).reshape(T, HD))
+    assert torch.equal(dst[T:2 * T, :HD], kr.reshape(T, HD))
+    assert torch.equal(dst[2 * T:3 * T + 17, :HD], K.kv_dequant(codes, scales, L.WF_SCALE_TOKEN))
+    assert torch.count_nonzero(dst[:, HD:]) == 0 and torch.count_nonzero(dst[3 * T + 17:]) == 0
+    with pytest.raises(RuntimeError):
+        K.kv_assemble([(7, ku.data_ptr(), 0, 0, dst_ptr, T, HD, dst_st)], HD, D)
+    with pytest.raises(RuntimeError):
+        K.kv_assemble([(L.WF_SEG_ROPE, ku.data_ptr(), 0, 0, dst_ptr, T, HD, dst_st)], HD, D)
+
+
 # ----------------------------------------------------------------------- RoPE
 def test_rope_matches_oracle(golden):
     K = _kernels()

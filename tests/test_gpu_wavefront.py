@@ -14,7 +14,7 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
 
 
-def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2):
+def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2, fused_assembly=True):
     from waveforcing_b200.runtime import backend
     from waveforcing_b200.wavefront.dit import DiTConfig, WanDiT
     from waveforcing_b200.wavefront.engine import EngineConfig, WavefrontEngine
@@ -26,6 +26,7 @@ def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2
     g = torch.Generator(device="cpu").manual_seed(1)
     model.set_text(torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(dev))
     eng = WavefrontEngine(model, EngineConfig(steps=steps, num_frames=num_frames, fp8_kv=fp8), device=dev)
+    eng.xport.fused_assembly = fused_assembly
     for t in range(eng.num_ticks):
         eng.tick(t)
     torch.cuda.synchronize()
@@ -74,3 +75,12 @@ def test_fused_rows_match_torch_ops_pipeline():
         dit.WanDiT.forward_stages = orig
     a = _run("wf_b200", False)
     assert _cos(a, b) >= 0.999
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_fused_context_assembly_is_bit_identical(fp8):
+    """One wf_kv_assemble launch per layer (anchor re-RoPE, copies, FP8
+    dequant) builds exactly the context the per-page copies built."""
+    a = _run("wf_b200", fp8, fused_assembly=True)
+    b = _run("wf_b200", fp8, fused_assembly=False)
+    assert torch.equal(a, b)

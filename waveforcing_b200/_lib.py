@@ -22,6 +22,7 @@ WF_OK = 0
 WF_DTYPE_BF16, WF_DTYPE_E4M3, WF_DTYPE_S8 = 0, 1, 2
 WF_SCALE_NONE, WF_SCALE_TENSOR, WF_SCALE_TOKEN = 0, 1, 2
 WF_ACT_NONE, WF_ACT_GELU_TANH = 0, 1
+WF_SEG_COPY, WF_SEG_ROPE, WF_SEG_DEQUANT = 0, 1, 2
 
 _vp = C.c_void_p
 _i64 = C.c_int64
@@ -30,6 +31,16 @@ _u32 = C.c_uint32
 _u64 = C.c_uint64
 _f32 = C.c_float
 _pi64 = C.POINTER(C.c_int64)
+
+
+
+class KvSegment(C.Structure):
+    """wf_kv_segment (include/wfk.h)."""
+
+    _fields_ = [("kind", C.c_int32), ("reserved", C.c_int32), ("src", C.c_void_p), ("aux0", C.c_void_p),
+                ("aux1", C.c_void_p), ("dst", C.c_void_p), ("rows", C.c_int64), ("src_row_stride", C.c_int64),
+                ("dst_row_stride", C.c_int64)]
+
 
 # name -> (restype, argtypes)
 _SIGS = {
@@ -49,6 +60,7 @@ _SIGS = {
     "wf_gemm_w8a8": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
     "wf_gemm_w8a8_act": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _vp]),
     "wf_rope_apply": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i64, _vp]),
+    "wf_kv_assemble": (_i32, [C.POINTER(KvSegment), _i32, _i64, _i32, _vp]),
     "wf_ln_modulate": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _f32, _vp]),
     "wf_gate_residual": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
     "wf_qk_norm_rope": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),

@@ -163,5 +163,25 @@ __device__ __forceinline__ uint32_t i8_slow(float ratio) {
   return static_cast<uint32_t>(static_cast<int>(fminf(fmaxf(rintf(ratio), -127.f), 127.f))) & 0xFFu;
 }
 
+// 8 codes (uint2) -> 8 bf16 (uint4) of e4m3(code) * s: the e4m3 value is
+// exact in f16 and f32, the f32 product rounds once to bf16.
+__device__ __forceinline__ uint4 dequant8(const uint2& c, float s) {
+  const uint32_t w[2] = {c.x, c.y};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t f2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(f2) : "h"(static_cast<uint16_t>(h ? w[j] >> 16 : w[j] & 0xFFFF)));
+      const float2 p = fmul2(make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(f2 & 0xFFFF))),
+                                         __half2float(__ushort_as_half(static_cast<unsigned short>(f2 >> 16)))),
+                             make_float2(s, s));
+      o[2 * j + h] = pack_bf16x2(p.x, p.y);
+    }
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 }  // namespace quant
 }  // namespace wfk

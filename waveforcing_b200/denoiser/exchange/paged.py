@@ -77,6 +77,9 @@ class PagedTransport:
         self.max_attn_frames, self.GT, self.fp8, self.dtype = max_attn_frames, GT, fp8, dtype
         self.timeout_s = timeout_s
         self.group = group
+        # assemble each layer's context with one wf_kv_assemble launch (when the
+        # caller passes RoPE tables); False keeps the per-page copies
+        self.fused_assembly = True
         self.naw_max, self.Wmax = slab_geometry(max_attn_frames, rf_step, npb)
         self.local = [s for s in range(rf_step + 1) if self.stage_rank[s] == rank]
         # a CPU device is accepted only to exercise the host-side bookkeeping in tests
@@ -267,20 +270,73 @@ class PagedTransport:
             raise TimeoutError("paged exchange: a producer flag did not arrive within the timeout")
 
     # ---------------------------------------------------------------- context
-    def anchor_working(self, clean_L, csf, qf, rope_fn):
-        """common.py:70-91 -> (list of K pages, list of V pages) as [T, H, D]."""
+    def anchor_working_parts(self, clean_L, csf, qf):
+        """common.py:70-91 before the RoPE: (anchor page, working pages,
+        anchor rope start frame), or None when the clean list is empty."""
         if not clean_L:
-            return [], []
+            return None
         npb = self.npb
         wmax_chunks = max(0, (self.max_attn_frames - qf - npb) // npb)
         anchor, rest = clean_L[0], clean_L[1:]
         working = rest[-wmax_chunks:] if wmax_chunks > 0 else []
-        rope_start = csf - len(working) * npb - npb
+        return anchor, working, csf - len(working) * npb - npb
+
+    def anchor_working(self, clean_L, csf, qf, rope_fn):
+        """common.py:70-91 -> (list of K pages, list of V pages) as [T, H, D]."""
+        parts = self.anchor_working_parts(clean_L, csf, qf)
+        if parts is None:
+            return [], []
+        anchor, working, rope_start = parts
         ak = rope_fn(anchor["ku"], rope_start)
         return [ak] + [w["kr"] for w in working], [anchor["v"]] + [w["v"] for w in working]
 
+    @staticmethod
+    def _rows(t: torch.Tensor) -> tuple[int, int]:
+        """(data pointer, token-row stride in elements) of a [.., T, H, D] page
+        whose (H, D) rows are contiguous."""
+        if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
+            raise ValueError("context page rows must be contiguous over (H, D)")
+        return t.data_ptr(), t.stride(-3)
+
+    def assemble(self, Kb, Vb, parts, rope_tab_fn, self_kv, self_off, deq=()):
+        """The stage's K/V context of one layer in one launch (wf_kv_assemble):
+        the anchor re-RoPEd straight into slot 0, working pages and the own
+        chunk copied, received FP8 rows dequantised.  ``deq`` lists (rows
+        slice of the context, K codes, K scales, V codes, V scales)."""
+        T, HD = self.T, self.H * self.D
+        kp, kst = self._rows(Kb)
+        vp, vst = self._rows(Vb)
+        esz = Kb.element_size()
+        segs = []
+        off = 0
+        if parts is not None:
+            anchor, working, rs = parts
+            cos, sin = rope_tab_fn(rs)
+            src, ss = self._rows(anchor["ku"])
+            segs.append((L.WF_SEG_ROPE, src, cos.data_ptr(), sin.data_ptr(), kp, T, ss, kst))
+            src, ss = self._rows(anchor["v"])
+            segs.append((L.WF_SEG_COPY, src, 0, 0, vp, T, ss, vst))
+            off = T
+            for w in working:
+                src, ss = self._rows(w["kr"])
+                segs.append((L.WF_SEG_COPY, src, 0, 0, kp + off * kst * esz, T, ss, kst))
+                src, ss = self._rows(w["v"])
+                segs.append((L.WF_SEG_COPY, src, 0, 0, vp + off * vst * esz, T, ss, vst))
+                off += T
+        k, v = self_kv
+        src, ss = self._rows(k)
+        segs.append((L.WF_SEG_COPY, src, 0, 0, kp + self_off * kst * esz, T, ss, kst))
+        src, ss = self._rows(v)
+        segs.append((L.WF_SEG_COPY, src, 0, 0, vp + self_off * vst * esz, T, ss, vst))
+        for rows, kc, ks, vc, vs in deq:
+            n = rows.stop - rows.start
+            segs.append((L.WF_SEG_DEQUANT, kc.data_ptr(), ks.data_ptr(), 0, kp + rows.start * kst * esz, n, HD, kst))
+            segs.append((L.WF_SEG_DEQUANT, vc.data_ptr(), vs.data_ptr(), 0, vp + rows.start * vst * esz, n, HD, vst))
+        kernels.kv_assemble(segs, HD, self.D)
+        return off
+
     def make_denoise_exch(self, m: int, clean, act, tick_csf, tick_qf, store_active, tick, rope_fn,
-                          store_slot_sink: dict | None = None):
+                          store_slot_sink: dict | None = None, rope_tab_fn=None):
         g = tick_geometry(m, tick, act, store_active, self.rf_step, self.max_attn_frames, self.npb)
         if g["active_slots"] > self.Wmax:
             raise RuntimeError(f"[paged stage {m}] active_slots={g['active_slots']} > Wmax={self.Wmax}")
@@ -301,6 +357,23 @@ class PagedTransport:
                 Kb, Vb = sl["kb"], sl["vb"]
             else:
                 Kb, Vb = sl["k"][gen, Lh], sl["v"][gen, Lh]
+            if rope_tab_fn is not None and self.fused_assembly:
+                parts = self.anchor_working_parts(clean[Lh], tick_csf, tick_qf)
+                if (0 if parts is None else 1 + len(parts[1])) != naw:
+                    raise RuntimeError(f"[paged stage {m}] anchor+working != naw={naw} (t={tick})")
+                for src in recv:
+                    self.wait(m, src, Lh, gen, tick)
+                deq = []
+                if self.fp8:
+                    for a, b in ((naw, base_infl), (base_infl + 1, act_slots)):
+                        if b > a:
+                            rows = slice(a * T, b * T)
+                            deq.append((rows, sl["kc"][gen, Lh, rows], sl["ks"][gen, Lh, rows],
+                                        sl["vc"][gen, Lh, rows], sl["vs"][gen, Lh, rows]))
+                self.assemble(Kb, Vb, parts, rope_tab_fn, (k, v), self_off, deq)
+                if store_active and store_slot_sink is not None:
+                    store_slot_sink[Lh] = (Kb[live_off:live_off + T].clone(), Vb[live_off:live_off + T].clone())
+                return Kb[:active_len].unsqueeze(0), Vb[:active_len].unsqueeze(0)
             aK, aV = self.anchor_working(clean[Lh], tick_csf, tick_qf, rope_fn)
             if len(aK) != naw:
                 raise RuntimeError(f"[paged stage {m}] anchor+working={len(aK)} != naw={naw} (t={tick})")
@@ -329,7 +402,7 @@ class PagedTransport:
 
         return exch
 
-    def make_store_exch(self, clean, store_kv: list, chunk: int, act, tick, rope_fn):
+    def make_store_exch(self, clean, store_kv: list, chunk: int, act, tick, rope_fn, rope_tab_fn=None):
         clean_len = min(8, max(0, tick - self.store))
         wmax_chunks = max(0, (self.max_attn_frames - len(act) * self.npb - self.npb) // self.npb)
         naw = 0 if clean_len == 0 else 1 + min(wmax_chunks, clean_len - 1)
@@ -343,6 +416,12 @@ class PagedTransport:
             k = roped_key[0]
             v = value[0]
             self.publish(self.store, k, v, send, layer_idx, gen, tick)
+            if rope_tab_fn is not None and self.fused_assembly:
+                parts = self.anchor_working_parts(clean[layer_idx], chunk * self.npb, self.npb)
+                n_aw = 0 if parts is None else 1 + len(parts[1])
+                self.assemble(Kbuf, Vbuf, parts, rope_tab_fn, (k, v), n_aw * T)
+                store_kv[layer_idx] = (k.clone(), unroped_key[0].clone(), v.clone())
+                return Kbuf[:(n_aw + 1) * T].unsqueeze(0), Vbuf[:(n_aw + 1) * T].unsqueeze(0)
             aK, aV = self.anchor_working(clean[layer_idx], chunk * self.npb, self.npb, rope_fn)
             off = 0
             for ak, av in zip(aK, aV):

@@ -164,6 +164,18 @@ def gemm_w8a8(xq, xs, wq, ws, bias=None, qtype: int = L.WF_DTYPE_E4M3, scale_mod
     return out
 
 
+def kv_assemble(segments, cols: int, head_dim: int) -> None:
+    """One launch that fills K/V context rows from a list of segments
+    (kind, src, aux0, aux1, dst, rows, src_row_stride, dst_row_stride), with
+    kind WF_SEG_COPY / WF_SEG_ROPE / WF_SEG_DEQUANT, pointers as ints (aux as 0
+    when unused) and strides in elements of the source / bf16 destination."""
+    n = len(segments)
+    arr = (L.KvSegment * max(1, n))()
+    for i, (kind, src, a0, a1, dst, rows, ss, ds) in enumerate(segments):
+        arr[i] = L.KvSegment(kind, 0, src, a0 or None, a1 or None, dst, rows, ss, ds)
+    L.check(L.lib().wf_kv_assemble(arr, n, cols, head_dim, _stream()), "wf_kv_assemble")
+
+
 def rope_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor | None = None):
     """Interleaved RoPE on bf16 [L, H, D] with f32 cos/sin [L, D/2]."""
     _need_cuda(x, cos, sin)

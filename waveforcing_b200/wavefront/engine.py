@@ -134,11 +134,15 @@ class WavefrontEngine:
     def act_store(self, t):
         return 0 <= t - self.store < self.cfg.num_blocks
 
-    def _rope(self, ku: torch.Tensor, start_frame: int) -> torch.Tensor:
+    def _rope_tables(self, start_frame: int) -> tuple[torch.Tensor, torch.Tensor]:
         tab = self._rope_cache.get(start_frame)
         if tab is None:
             tab = rope_tables(self.m.cfg, self.cfg.npb, start_frame, self.device)
             self._rope_cache[start_frame] = tab
+        return tab
+
+    def _rope(self, ku: torch.Tensor, start_frame: int) -> torch.Tensor:
+        tab = self._rope_tables(start_frame)
         return kernels.rope_apply(ku, tab[0], tab[1])
 
     def _append_clean(self, page: dict) -> None:
@@ -171,11 +175,13 @@ class WavefrontEngine:
             if s < S and self.act_denoise(s, t):
                 c = t - s
                 exch = self.xport.make_denoise_exch(s, self.clean, act, tick_csf, tick_qf, store_active, t,
-                                                    self._rope, store_slot if not store_slot else None)
+                                                    self._rope, store_slot if not store_slot else None,
+                                                    rope_tab_fn=self._rope_tables)
                 tasks.append(StageTask(self.inputs[s], self.fm.timestep(cfg.steps[s]), c * cfg.npb, s, exch))
             elif s == self.store and store_active:
                 c = t - self.store
-                exch = self.xport.make_store_exch(self.clean, store_kv, c, act, t, self._rope)
+                exch = self.xport.make_store_exch(self.clean, store_kv, c, act, t, self._rope,
+                                                  rope_tab_fn=self._rope_tables)
                 tasks.append(StageTask(self.inputs[s], cfg.context_noise, c * cfg.npb, s, exch))
         flows = self.m.forward_stages(tasks) if tasks else []
         self.xport.drain()
