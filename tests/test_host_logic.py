@@ -116,3 +116,54 @@ def test_two_rank_handle_exchange_and_close_order():
     closes = [p for op, p in res[1][2] if op == "close"]
     assert opens and closes == list(reversed(opens))
     assert len(set(opens)) == len(opens)  # every handle opened once
+
+
+def test_context_assembly_segments(monkeypatch):
+    """PagedTransport.assemble's segment list (host logic of wf_kv_assemble):
+    the anchor re-RoPE into slot 0, working pages after it, the own chunk at
+    self_off and received FP8 ranges, with byte offsets and row strides taken
+    from the tensors (one page has strided rows)."""
+    from waveforcing_b200 import _lib as L
+
+    T, H, D = 4, 2, 8
+    HD = H * D
+    xp = paged.PagedTransport(device="cpu", rank=0, world=1, stage_rank=[0, 0, 0, 0], rf_step=3, Ln=2,
+                              T=T, H=H, D=D, fp8=False)
+    page = lambda: {"ku": torch.randn(T, H, D).bfloat16(), "kr": torch.randn(T, H, D).bfloat16(),  # noqa: E731
+                    "v": torch.randn(T, H, D).bfloat16()}
+    clean = [page() for _ in range(4)]
+    clean[2]["kr"] = torch.randn(2 * T, H, D).bfloat16()[::2]  # strided token rows
+    parts = xp.anchor_working_parts(clean, csf=30, qf=3)
+    anchor, working, rs = parts
+    tabs = {}
+
+    def rope_tab(start):
+        tabs[start] = (torch.zeros(T, D // 2), torch.zeros(T, D // 2))
+        return tabs[start]
+
+    Kb = torch.empty(8 * T, H, D).bfloat16()
+    Vb = torch.empty(8 * T, H, D).bfloat16()
+    k, v = torch.randn(T, H, D).bfloat16(), torch.randn(T, H, D).bfloat16()
+    kc, vc = torch.zeros(2 * T, HD, dtype=torch.uint8), torch.zeros(2 * T, HD, dtype=torch.uint8)
+    ks, vs = torch.ones(2 * T), torch.ones(2 * T)
+    got = []
+    monkeypatch.setattr(paged.kernels, "kv_assemble", lambda segs, cols, hd: got.append((segs, cols, hd)))
+    self_off = (1 + len(working)) * T
+    n_aw = xp.assemble(Kb, Vb, parts, rope_tab, (k, v), self_off, [(slice(5 * T, 7 * T), kc, ks, vc, vs)])
+    assert n_aw == (1 + len(working)) * T
+    (segs, cols, hd), = got
+    assert (cols, hd) == (HD, D)
+    row = HD * 2  # bytes per bf16 context row
+    cos, sin = tabs[rs]
+    exp = [(L.WF_SEG_ROPE, anchor["ku"].data_ptr(), cos.data_ptr(), sin.data_ptr(), Kb.data_ptr(), T, HD, HD),
+           (L.WF_SEG_COPY, anchor["v"].data_ptr(), 0, 0, Vb.data_ptr(), T, HD, HD)]
+    for i, w in enumerate(working):
+        exp.append((L.WF_SEG_COPY, w["kr"].data_ptr(), 0, 0, Kb.data_ptr() + (1 + i) * T * row, T,
+                    w["kr"].stride(0), HD))
+        exp.append((L.WF_SEG_COPY, w["v"].data_ptr(), 0, 0, Vb.data_ptr() + (1 + i) * T * row, T, HD, HD))
+    exp += [(L.WF_SEG_COPY, k.data_ptr(), 0, 0, Kb.data_ptr() + self_off * row, T, HD, HD),
+            (L.WF_SEG_COPY, v.data_ptr(), 0, 0, Vb.data_ptr() + self_off * row, T, HD, HD),
+            (L.WF_SEG_DEQUANT, kc.data_ptr(), ks.data_ptr(), 0, Kb.data_ptr() + 5 * T * row, 2 * T, HD, HD),
+            (L.WF_SEG_DEQUANT, vc.data_ptr(), vs.data_ptr(), 0, Vb.data_ptr() + 5 * T * row, 2 * T, HD, HD)]
+    assert segs == exp
+    assert any(w["kr"].stride(0) == 2 * HD for w in working)  # the strided page is among the working set
