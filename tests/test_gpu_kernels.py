@@ -48,6 +48,7 @@ def _f32(t):
 ATTN_CASES = [
     (128, 128, 1), (130, 300, 2), (5, 517, 3), (257, 1000, 2), (64, 64, 2), (1, 1, 1),
     (300, 129, 4), (4680, 4680, 1), (200, 700, 40), (256, 256, 1), (100, 384, 2),
+    (1024, 600, 40), (28080, 512, 2), (2048, 100, 20),  # more items than SMs: several per CTA
 ]
 
 

@@ -1,11 +1,13 @@
 // tcgen05/TMEM flash attention forward (bf16, head_dim 128) for the chunk
 // self-attention of WaveRT's wavefront step (wave_rt/runtime/backend.py:141-148).
 //
-// One CTA computes a 128-query tile of one head against all Lk keys, in
-// 256-key tiles:
-//   warp 0       TMA producer: Q once; K in 256-key tiles (2-stage ring, the
-//                K ring runs one tile ahead of V); V in 128-key halves
-//                (one slot per half); 128-byte swizzle, 64-column boxes
+// Work item = 128 queries of one head (of one batch entry) against all Lk keys,
+// in 256-key tiles.  The grid is persistent: CTA c processes items c,
+// c + gridDim.x, ...; the next item's Q and K/V loads and its first QK^T run
+// while the previous item's epilogue drains O.
+//   warp 0       TMA producer: Q per item; K in 256-key tiles (2-stage ring,
+//                one tile ahead of V); V in 128-key halves (one slot per
+//                half); 128-byte swizzle, 64-column boxes
 //   warp 1       allocates 512 TMEM columns; lane 0 issues the MMAs:
 //                S_j  = Q K_j^T  as one M=128, N=256 MMA per 16-wide k step
 //                O   += P_j V_j  as M=128, N=128 MMAs (A = P from TMEM,
@@ -22,8 +24,10 @@
 // S is released as soon as both warpgroups have read it into registers, so
 // QK^T of tile j+1 runs on the tensor pipe while P_j is being computed; P is
 // written only after PV_{j-1} has completed.
-// Every wait is bounded (sm100.cuh mbar_wait); a timed-out wait raises the
-// status word and the CTA drains its in-flight work and exits.
+// Barrier phases run on per-CTA counters that continue across items (tiles
+// for the S/P/PV/K/V barriers, items for Q/last/o_free).  Every wait is
+// bounded (sm100.cuh mbar_wait); a timed-out wait raises the status word and
+// the CTA drains its in-flight work and exits.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -34,7 +38,7 @@
 namespace wfk {
 namespace attn {
 
-constexpr int BM = 128;          // queries per CTA
+constexpr int BM = 128;          // queries per item
 constexpr int BN = 256;          // keys per tile
 constexpr int KH = 128;          // keys per softmax warpgroup / per V slot
 constexpr int HD = 128;
@@ -46,7 +50,7 @@ constexpr int VSLOT = KH * HD * 2;   // 32 KB: [d 0-63: 128 rows x 128 B][d 64-1
 constexpr int VHALF = VSLOT / 2;     // 16 KB
 constexpr int QHALF = QTILE / 2;     // 16 KB
 constexpr int BIG = QTILE + NSK * KTILE + 2 * VSLOT;  // 224 KB
-constexpr int NBARS = 1 + 2 * NSK + 4 + 7;
+constexpr int NBARS = 1 + 2 * NSK + 4 + 9;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + BIG + NBARS * 8 + 2 * BM * 4 /*row exchange*/ + 16;
 constexpr int THREADS = 384;
 
@@ -63,17 +67,42 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   return true;
 }
 
+__device__ __forceinline__ void tmem_st_x1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t tmem_ld_x1(uint32_t taddr) {
+  uint32_t v;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\ttcgen05.wait::ld.sync.aligned;"
+               : "=r"(v)
+               : "r"(taddr)
+               : "memory");
+  return v;
+}
+
+struct Item {
+  int q0, h, bz;
+};
+__device__ __forceinline__ Item item_of(int it, int n_qt, int H) {
+  Item r;
+  r.q0 = (it % n_qt) * BM;
+  const int rest = it / n_qt;
+  r.h = rest % H;
+  r.bz = rest / H;
+  return r;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,
-                         long long o_head, long long o_batch, int Lq, int Lk, float scale_log2) {
+                         long long o_head, long long o_batch, int Lq, int Lk, int H, int n_items,
+                         float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + QTILE;
   uint8_t* sV = sK + NSK * KTILE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * VSLOT);
-  uint64_t* bar_q = bars;
+  uint64_t* bar_q = bars;             // Q of the current item landed
   uint64_t* full_k = bars + 1;
   uint64_t* empty_k = full_k + NSK;
   uint64_t* full_v = empty_k + NSK;   // [2], one per 128-key half
@@ -83,18 +112,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bar_p = bar_sfree + 1;    // P_j written
   uint64_t* bar_pv = bar_p + 1;       // PV_j complete
   uint64_t* bar_xch = bar_pv + 1;     // row exchange between the warpgroups
-  uint64_t* bar_last = bar_xch + 1;   // one phase: every PV of the CTA has completed
-  uint64_t* bar_fin = bar_last + 1;
+  uint64_t* bar_last = bar_xch + 1;   // every PV of the current item has completed
+  uint64_t* q_empty = bar_last + 1;   // the current item's last QK^T has completed (Q may be reloaded)
+  uint64_t* o_free = q_empty + 1;     // the epilogue has read O (the next item's first PV may overwrite it)
+  uint64_t* bar_fin = o_free + 1;
   float* xch = reinterpret_cast<float*>(bar_fin + 1);  // [2][BM]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xch + 2 * BM);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * BM;
-  const int h = blockIdx.y;
-  const int bz = blockIdx.z;
   const int nk = (Lk + BN - 1) / BN;
+  const int n_qt = (Lq + BM - 1) / BM;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
@@ -112,6 +141,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(bar_pv, 1);
     mbar_init(bar_xch, 256);
     mbar_init(bar_last, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_free, 256);
     mbar_init(bar_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -143,102 +174,132 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 72;\n" ::: "memory");
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ producer
-      // Issue order: K_0, then per tile j: K_{j+1}, V_j (both halves).  K runs
-      // a tile ahead because QK^T_{j+1} is queued on the tensor pipe before
-      // PV_j, and V_j's slots only free up when PV_{j-1} completes.
+      // Per item: Q (once the previous item's last QK^T has completed), then
+      // K_0, and per tile j: K_{j+1}, V_j (both halves).  K runs a tile ahead
+      // because QK^T_{j+1} is queued on the tensor pipe before PV_j, and
+      // V_j's slots only free up when PV_{j-1} completes.  The counters kt
+      // (K tiles) and vt (V tiles) run across items.
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(bar_q, QTILE);
-      tma_load_4d(sQ, &tmQ, bar_q, 0, h, q0, bz);
-      tma_load_4d(sQ + QHALF, &tmQ, bar_q, 64, h, q0, bz);
-      int k_issued = 0, v_issued = 0;
+      int kt = 0, vt = 0, n_it = 0;
+      int q_loads = 0, v_loads[2] = {0, 0};  // loads issued per barrier, for the drain on abort
       bool run = true;
-      auto load_k = [&](int j) -> bool {
-        const int s = j % NSK;
-        if (j >= NSK && !mbar_wait(&empty_k[s], ((j / NSK) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) return false;
+      auto load_k = [&](const Item& w, int j) -> bool {
+        const int s = kt % NSK;
+        if (kt >= NSK && !mbar_wait(&empty_k[s], ((kt / NSK) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) return false;
         uint8_t* dst = sK + s * KTILE;
         mbar_arrive_expect_tx(&full_k[s], KTILE);
-        tma_load_4d(dst, &tmK, &full_k[s], 0, h, j * BN, bz);
-        tma_load_4d(dst + KH * 128, &tmK, &full_k[s], 0, h, j * BN + KH, bz);
-        tma_load_4d(dst + KHALF, &tmK, &full_k[s], 64, h, j * BN, bz);
-        tma_load_4d(dst + KHALF + KH * 128, &tmK, &full_k[s], 64, h, j * BN + KH, bz);
-        k_issued = j + 1;
+        tma_load_4d(dst, &tmK, &full_k[s], 0, w.h, j * BN, w.bz);
+        tma_load_4d(dst + KH * 128, &tmK, &full_k[s], 0, w.h, j * BN + KH, w.bz);
+        tma_load_4d(dst + KHALF, &tmK, &full_k[s], 64, w.h, j * BN, w.bz);
+        tma_load_4d(dst + KHALF + KH * 128, &tmK, &full_k[s], 64, w.h, j * BN + KH, w.bz);
+        ++kt;
         return true;
       };
-      run = load_k(0);
-      for (int j = 0; run && j < nk; ++j) {
-        if (j + 1 < nk && !(run = load_k(j + 1))) break;
-        for (int half = 0; half < 2; ++half) {
-          if (j >= 1 && !mbar_wait(&empty_v[half], (j - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) {
-            run = false;
-            break;
+      for (int it = blockIdx.x; run && it < n_items; it += gridDim.x, ++n_it) {
+        const Item w = item_of(it, n_qt, H);
+        if (n_it > 0 && !mbar_wait(q_empty, (n_it - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) break;
+        mbar_arrive_expect_tx(bar_q, QTILE);
+        tma_load_4d(sQ, &tmQ, bar_q, 0, w.h, w.q0, w.bz);
+        tma_load_4d(sQ + QHALF, &tmQ, bar_q, 64, w.h, w.q0, w.bz);
+        ++q_loads;
+        if (!(run = load_k(w, 0))) break;
+        for (int j = 0; run && j < nk; ++j) {
+          if (j + 1 < nk && !(run = load_k(w, j + 1))) break;
+          for (int half = 0; half < 2; ++half) {
+            if (vt >= 1 && !mbar_wait(&empty_v[half], (vt - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) {
+              run = false;
+              break;
+            }
+            uint8_t* dst = sV + half * VSLOT;
+            mbar_arrive_expect_tx(&full_v[half], VSLOT);
+            tma_load_4d(dst, &tmV, &full_v[half], 0, w.h, j * BN + half * KH, w.bz);
+            tma_load_4d(dst + VHALF, &tmV, &full_v[half], 64, w.h, j * BN + half * KH, w.bz);
+            ++v_loads[half];
           }
-          uint8_t* dst = sV + half * VSLOT;
-          mbar_arrive_expect_tx(&full_v[half], VSLOT);
-          tma_load_4d(dst, &tmV, &full_v[half], 0, h, j * BN + half * KH, bz);
-          tma_load_4d(dst + VHALF, &tmV, &full_v[half], 64, h, j * BN + half * KH, bz);
-          v_issued = 2 * j + half + 1;
+          if (run) ++vt;
         }
       }
       if (*abort_flag) {
-        // Let the copies this thread issued land before the CTA exits.
-        mbar_wait_drain(bar_q, 0, 200000000ull);
-        for (int j = (k_issued > NSK ? k_issued - NSK : 0); j < k_issued; ++j)
-          mbar_wait_drain(&full_k[j % NSK], (j / NSK) & 1, 200000000ull);
-        for (int v = (v_issued > 2 ? v_issued - 2 : 0); v < v_issued; ++v)
-          mbar_wait_drain(&full_v[v & 1], (v >> 1) & 1, 200000000ull);
+        // Let the copies this thread issued land before the CTA exits: the
+        // last Q, the last NSK K tiles and the last load of each V half
+        // (the phase of load n on a barrier is n & 1).
+        if (q_loads > 0) mbar_wait_drain(bar_q, (q_loads - 1) & 1, 200000000ull);
+        for (int t = (kt > NSK ? kt - NSK : 0); t < kt; ++t)
+          mbar_wait_drain(&full_k[t % NSK], (t / NSK) & 1, 200000000ull);
+        for (int half = 0; half < 2; ++half)
+          if (v_loads[half] > 0) mbar_wait_drain(&full_v[half], (v_loads[half] - 1) & 1, 200000000ull);
       }
     } else if (warp == 1 && lane == 0) {
       // ----------------------------------------------------------------- MMA
       constexpr uint32_t idesc_qk = make_idesc(1, FMT_BF16, FMT_BF16, 0, BM, BN);
       constexpr uint32_t idesc_pv = make_idesc(1, FMT_BF16, FMT_BF16, 1, BM, HD);
       const uint32_t aQ = smem_u32(sQ);
-      bool ok = mbar_wait(bar_q, 0, abort_flag, ST_ATTN_MMA);
-      for (int j = 0; ok && j <= nk; ++j) {
-        if (j < nk) {
-          const int s = j % NSK;
-          if (!mbar_wait(&full_k[s], (j / NSK) & 1, abort_flag, ST_ATTN_MMA)) break;
-          // S is single-buffered: both warpgroups must have read S_{j-1}.
-          if (j >= 1 && !mbar_wait(bar_sfree, (j - 1) & 1, abort_flag, ST_ATTN_MMA)) break;
-          tc_fence_after();
-          const uint32_t aK = smem_u32(sK + s * KTILE);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t qoff = (kk >> 2) * QHALF + (kk & 3) * 32;
-            const uint32_t koff = (kk >> 2) * KHALF + (kk & 3) * 32;
-            umma_f16_ss(tbase + COL_S, desc_sw128(aQ + qoff, 16, 1024), desc_sw128(aK + koff, 16, 1024), idesc_qk,
-                        kk > 0);
-          }
-          umma_commit(&empty_k[s]);
-          umma_commit(bar_s);
-        }
-        if (j >= 1) {
-          const int jj = j - 1;
-          if (!mbar_wait(bar_p, jj & 1, abort_flag, ST_ATTN_MMA)) break;
-          bool vok = true;
-          for (int half = 0; half < 2; ++half) {
-            if (!mbar_wait(&full_v[half], jj & 1, abort_flag, ST_ATTN_MMA)) {
-              vok = false;
+      int kt = 0, st = 0, n_it = 0;  // K tiles, S tiles (= PV tiles) issued, items
+      bool ok = true;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++n_it) {
+        if (!mbar_wait(bar_q, n_it & 1, abort_flag, ST_ATTN_MMA)) break;
+        for (int j = 0; ok && j <= nk; ++j) {
+          if (j < nk) {
+            const int s = kt % NSK;
+            if (!mbar_wait(&full_k[s], (kt / NSK) & 1, abort_flag, ST_ATTN_MMA)) {
+              ok = false;
+              break;
+            }
+            // S is single-buffered: both warpgroups must have read the previous S tile.
+            if (st + j >= 1 && !mbar_wait(bar_sfree, (st + j - 1) & 1, abort_flag, ST_ATTN_MMA)) {
+              ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t aV = smem_u32(sV + half * VSLOT);
-            const uint32_t tP = tbase + COL_P + half * (KH / 2);
+            const uint32_t aK = smem_u32(sK + s * KTILE);
 #pragma unroll
-            for (int kk = 0; kk < KH / 16; ++kk) {
-              umma_f16_ts(tbase + COL_O, tP + kk * 8, desc_sw128(aV + kk * 2048, VHALF, 1024), idesc_pv,
-                          (jj > 0 || half > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint32_t qoff = (kk >> 2) * QHALF + (kk & 3) * 32;
+              const uint32_t koff = (kk >> 2) * KHALF + (kk & 3) * 32;
+              umma_f16_ss(tbase + COL_S, desc_sw128(aQ + qoff, 16, 1024), desc_sw128(aK + koff, 16, 1024),
+                          idesc_qk, kk > 0);
             }
-            umma_commit(&empty_v[half]);
+            umma_commit(&empty_k[s]);
+            umma_commit(bar_s);
+            if (j == nk - 1) umma_commit(q_empty);
+            ++kt;
           }
-          if (!vok) break;
-          umma_commit(bar_pv);
+          if (j >= 1) {
+            const int g = st + j - 1;  // global index of the PV tile
+            if (!mbar_wait(bar_p, g & 1, abort_flag, ST_ATTN_MMA)) {
+              ok = false;
+              break;
+            }
+            // The item's first PV overwrites O: the previous item's epilogue must have read it.
+            if (j == 1 && n_it > 0 && !mbar_wait(o_free, (n_it - 1) & 1, abort_flag, ST_ATTN_MMA)) {
+              ok = false;
+              break;
+            }
+            for (int half = 0; half < 2; ++half) {
+              if (!mbar_wait(&full_v[half], g & 1, abort_flag, ST_ATTN_MMA)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t aV = smem_u32(sV + half * VSLOT);
+              const uint32_t tP = tbase + COL_P + half * (KH / 2);
+#pragma unroll
+              for (int kk = 0; kk < KH / 16; ++kk) {
+                umma_f16_ts(tbase + COL_O, tP + kk * 8, desc_sw128(aV + kk * 2048, VHALF, 1024), idesc_pv,
+                            (j > 1 || half > 0 || kk > 0) ? 1u : 0u);
+              }
+              umma_commit(&empty_v[half]);
+            }
+            if (!ok) break;
+            umma_commit(bar_pv);
+          }
         }
+        if (!ok) break;
+        st += nk;
+        umma_commit(bar_last);
       }
-      // The epilogue waits on its own one-phase barrier: a parity wait on
-      // bar_pv could be two phases behind there.
-      umma_commit(bar_last);
       // Nothing of ours may still be running when TMEM is released.
       umma_commit(bar_fin);
       mbar_wait_drain(bar_fin, 0, 200000000ull);
@@ -254,112 +315,125 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     float* my_x = xch + wg * BM + row;
     const float* other_x = xch + (wg ^ 1) * BM + row;
-    float m_run = -INFINITY;
-    float l_run = 0.f;
+    int st = 0, xc = 0, n_it = 0;  // S tiles consumed, row exchanges, items
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_s, j & 1, abort_flag, ST_ATTN_SOFTMAX));
-      if (!ok) break;
-      tc_fence_after();
-      float s[KH];
-      {
-        uint32_t r[64];
-        tmem_ld32x32b_x64(tbase + lane_off + COL_S + wg * KH, r);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
-        tmem_ld32x32b_x64(tbase + lane_off + COL_S + wg * KH + 64, r);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(r[i]);
-      }
-      const int kvalid = Lk - j * BN - wg * KH;
-      if (kvalid < KH) {
-#pragma unroll
-        for (int i = 0; i < KH; ++i)
-          if (i >= kvalid) s[i] = -INFINITY;
-      }
-      float mx = s[0];
-#pragma unroll
-      for (int i = 1; i < KH; ++i) mx = fmaxf(mx, s[i]);
-      // Row max across the two halves.  The exchange slot is reused every
-      // tile: QK^T_{j+1} (and with it this thread's next write) waits on
-      // bar_sfree, which every thread passes only after its read below.
-      *my_x = mx;
-      mbar_arrive(bar_xch);
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_xch, j & 1, abort_flag, ST_ATTN_SOFTMAX));
-      if (!ok) break;
-      mx = fmaxf(mx, *other_x);
-      tc_fence_before();
-      mbar_arrive(bar_sfree);
-      const float mx2 = mx * scale_log2;
-      float m_new = m_run;
-      bool grow = false;
-      if (j == 0) {
-        m_new = mx2;
-      } else if (mx2 > m_run + 8.f) {
-        m_new = mx2;
-        grow = true;
-      }
-      // P = 2^(s * scale_log2 - m): pairs through packed f32x2 FMAs; 3 of
-      // every 8 pairs take the FMA-pipe polynomial, the rest MUFU ex2, so the
-      // two pipes finish together.
-      const float2 sc2 = make_float2(scale_log2, scale_log2);
-      const float2 nm2 = make_float2(-m_new, -m_new);
-      float2 sum2 = make_float2(0.f, 0.f);
-      uint32_t pk[KH / 2];
-#pragma unroll
-      for (int i = 0; i < KH / 2; ++i) {
-        const float2 x = ffma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
-        float2 pr;
-        if ((i & 7) < 3) {
-          pr = exp2_poly2(x);
-        } else {
-          pr.x = ex2_approx(x.x);
-          pr.y = ex2_approx(x.y);
-        }
-        sum2 = fadd2(sum2, pr);
-        pk[i] = pack_bf16x2(pr.x, pr.y);
-      }
-      const float sum = sum2.x + sum2.y;
-      const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
-      // P and O may only be written once PV_{j-1} has completed.  This parity
-      // wait is unambiguous: S_j's commit (one issuing thread, in order)
-      // already covered PV_{j-2}, and PV_j needs this thread's arrival.
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_pv, (j - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++n_it) {
+      const Item w = item_of(it, n_qt, H);
+      float m_run = -INFINITY;
+      float l_run = 0.f;
+      for (int j = 0; j < nk; ++j, ++st, ++xc) {
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_s, st & 1, abort_flag, ST_ATTN_SOFTMAX));
         if (!ok) break;
         tc_fence_after();
-      }
-      if (__any_sync(0xffffffffu, grow)) {
+        float s[KH];
+        {
+          uint32_t r[64];
+          tmem_ld32x32b_x64(tbase + lane_off + COL_S + wg * KH, r);
 #pragma unroll
-        for (int c = 0; c < HD / 2; c += 32) {
-          uint32_t r[32];
-          tmem_ld32x32b_x32(tbase + lane_off + COL_O + wg * (HD / 2) + c, r);
+          for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
+          tmem_ld32x32b_x64(tbase + lane_off + COL_S + wg * KH + 64, r);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32x32b_x32(tbase + lane_off + COL_O + wg * (HD / 2) + c, r);
+          for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(r[i]);
         }
+        const int kvalid = Lk - j * BN - wg * KH;
+        if (kvalid < KH) {
+#pragma unroll
+          for (int i = 0; i < KH; ++i)
+            if (i >= kvalid) s[i] = -INFINITY;
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int i = 1; i < KH; ++i) mx = fmaxf(mx, s[i]);
+        // Row max across the two halves.  The exchange slot is reused every
+        // tile: the next S tile (and with it this thread's next write) waits on
+        // bar_sfree, which every thread passes only after its read below.
+        *my_x = mx;
+        mbar_arrive(bar_xch);
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_xch, xc & 1, abort_flag, ST_ATTN_SOFTMAX));
+        if (!ok) break;
+        mx = fmaxf(mx, *other_x);
+        tc_fence_before();
+        mbar_arrive(bar_sfree);
+        const float mx2 = mx * scale_log2;
+        float m_new = m_run;
+        bool grow = false;
+        if (j == 0) {
+          m_new = mx2;
+        } else if (mx2 > m_run + 8.f) {
+          m_new = mx2;
+          grow = true;
+        }
+        // P = 2^(s * scale_log2 - m): pairs through packed f32x2 FMAs; 3 of
+        // every 8 pairs take the FMA-pipe polynomial, the rest MUFU ex2, so
+        // the two pipes finish together.
+        const float2 sc2 = make_float2(scale_log2, scale_log2);
+        const float2 nm2 = make_float2(-m_new, -m_new);
+        float2 sum2 = make_float2(0.f, 0.f);
+        uint32_t pk[KH / 2];
+#pragma unroll
+        for (int i = 0; i < KH / 2; ++i) {
+          const float2 x = ffma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
+          float2 pr;
+          if ((i & 7) < 3) {
+            pr = exp2_poly2(x);
+          } else {
+            pr.x = ex2_approx(x.x);
+            pr.y = ex2_approx(x.y);
+          }
+          sum2 = fadd2(sum2, pr);
+          pk[i] = pack_bf16x2(pr.x, pr.y);
+        }
+        const float sum = sum2.x + sum2.y;
+        const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
+        // P and O may only be written once PV_{j-1} has completed.  This
+        // parity wait is unambiguous: S_j's commit (one issuing thread, in
+        // order) already covered PV_{j-2}, and PV_j needs this thread's
+        // arrival.  For j == 0 the previous item's epilogue already waited on
+        // bar_last, which covers its last PV.
+        if (j > 0) {
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_pv, (st - 1) & 1, abort_flag, ST_ATTN_SOFTMAX));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int c = 0; c < HD / 2; c += 32) {
+            uint32_t r[32];
+            tmem_ld32x32b_x32(tbase + lane_off + COL_O + wg * (HD / 2) + c, r);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32x32b_x32(tbase + lane_off + COL_O + wg * (HD / 2) + c, r);
+          }
+        }
+        l_run = l_run * alpha + sum;
+        m_run = m_new;
+        tmem_st32x32b_x64(tbase + lane_off + COL_P + wg * (KH / 2), pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar_p);
       }
-      l_run = l_run * alpha + sum;
-      m_run = m_new;
-      tmem_st32x32b_x64(tbase + lane_off + COL_P + wg * (KH / 2), pk);
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_last, n_it & 1, abort_flag, ST_ATTN_SOFTMAX));
+      if (!ok) break;
+      tc_fence_after();
+      // Row sum across the two halves, through TMEM: each warpgroup writes its
+      // partial sum into the first column of its own P half (P is free: every
+      // PV of this item has completed) and reads the other's after the
+      // exchange barrier.  The next item's P writes come after the next row
+      // max exchange, which the partner reaches only after this read.
+      tmem_st_x1(tbase + lane_off + COL_P + wg * (KH / 2), __float_as_uint(l_run));
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar_p);
-    }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_last, 0, abort_flag, ST_ATTN_SOFTMAX));
-    if (ok) {
-      // Row sum across the two halves (same slot: every thread read the last
-      // max before arriving on bar_p, and bar_last follows every PV).
-      *my_x = l_run;
       mbar_arrive(bar_xch);
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_xch, nk & 1, abort_flag, ST_ATTN_SOFTMAX));
-    }
-    if (ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_xch, xc & 1, abort_flag, ST_ATTN_SOFTMAX));
+      ++xc;
+      if (!ok) break;
       tc_fence_after();
-      const float inv_l = 1.f / (l_run + *other_x);
-      const int qrow = q0 + row;
+      const float l_other = __uint_as_float(tmem_ld_x1(tbase + lane_off + COL_P + (wg ^ 1) * (KH / 2)));
+      const float inv_l = 1.f / (l_run + l_other);
+      const int qrow = w.q0 + row;
       __nv_bfloat16* dst =
-          out + (long long)bz * o_batch + (long long)qrow * o_tok + (long long)h * o_head + wg * (HD / 2);
+          out + (long long)w.bz * o_batch + (long long)qrow * o_tok + (long long)w.h * o_head + wg * (HD / 2);
 #pragma unroll
       for (int c = 0; c < HD / 2; c += 32) {
         uint32_t r[32];
@@ -368,15 +442,19 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-            w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-            w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-            w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-            d4[v] = w;
+            uint4 wv;
+            wv.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+            wv.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+            wv.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+            wv.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+            d4[v] = wv;
           }
         }
       }
+      // O is in registers (tcgen05.ld waits for completion): the next item's
+      // first PV may overwrite it.
+      tc_fence_before();
+      mbar_arrive(o_free);
     }
     teardown();
   }
@@ -436,11 +514,26 @@ extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o,
     WFK_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     configured_dev = dev;
   }
-  const dim3 grid((Lq + BM - 1) / BM, H, batch);
+  const long long items = (long long)((Lq + BM - 1) / BM) * H * batch;
+  if (items > (1LL << 30)) return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: too many query tiles (%lld)", items);
+  static thread_local int sms = 0, sms_dev = -1;
+  if (sms_dev != dev) {
+    WFK_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    sms_dev = dev;
+  }
+  // Persistent grid: at most one CTA per SM; with more items than SMs each
+  // CTA walks items blockIdx.x, blockIdx.x + gridDim.x, ...  When items do
+  // not fill whole waves, the grid is the smallest count that keeps every
+  // CTA's item count within one of the others'.
+  long long grid = items < sms ? items : sms;
+  if (items > sms) {
+    const long long per = (items + sms - 1) / sms;
+    grid = (items + per - 1) / per;
+  }
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
-  attn_fwd_bf16_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+  attn_fwd_bf16_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
       tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
-      (long long)o_stride[0], Lq, Lk, scale_log2);
+      (long long)o_stride[0], Lq, Lk, H, (int)items, scale_log2);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }
