@@ -139,6 +139,14 @@ int wf_weight_quant(const void* w, void* wq, float* w_scale, int64_t N, int64_t 
 int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, int64_t K, int64_t x_row_stride, int qtype,
                  void* stream);
 
+/* wf_act_quant of bf16(activation(x)): WF_ACT_GELU_TANH maps each element
+ * through the FFN's GELU(approximate="tanh") first, so fc_out's input
+ * quantisation reads fc_in's bf16 output once and the activation's bf16
+ * tensor is never written (the Wan FFN, causal_model.py:309-420).
+ * WF_ACT_NONE is wf_act_quant. */
+int wf_act_quant_act(const void* x, void* xq, float* x_scale, int64_t M, int64_t K, int64_t x_row_stride, int qtype,
+                     int activation, void* stream);
+
 /* y[M, N] (bf16, row stride y_row_stride) = (xq[M, K] . wq[N, K]^T) * x_scale[m] * w_scale[n] + bias[n]
  * on tcgen05 (kind::f8f6f4 for e4m3, kind::i8 for s8), replacing the
  * torch._scaled_mm call of wave_rt/runtime/fp8.py:49-56.  scale_mode

@@ -336,6 +336,34 @@ def test_gemm_w8a8_gelu_epilogue(qtype):
     assert _rel(_f32(y), ref) <= 1e-2
 
 
+@pytest.mark.parametrize("qtype", ["e4m3", "s8"])
+@pytest.mark.parametrize("Kd", [1536, 8960, 13824])
+def test_act_quant_with_gelu_input(qtype, Kd):
+    """Per-token quantisation of bf16(GELU_tanh(x)) against the oracle applied
+    to the exactly computed GELU.  The kernel's tanh is the MUFU approximation
+    (relative error 2^-11), so a code may differ where the bf16 rounding of the
+    activation flips: at most 1 in 1000 codes, each by one step."""
+    K = _kernels()
+    from waveforcing_b200._lib import WF_ACT_GELU_TANH, WF_DTYPE_E4M3, WF_DTYPE_S8
+
+    qt = WF_DTYPE_E4M3 if qtype == "e4m3" else WF_DTYPE_S8
+    rng = np.random.default_rng(Kd)
+    x = o_codec.bf16_round((rng.standard_normal((64, Kd)) * 3).astype(np.float32))
+    g = o_codec.bf16_round(torch.nn.functional.gelu(torch.from_numpy(x).double(), approximate="tanh").float().numpy())
+    rq, rs = o_w8a8.quant_act(g, qtype)
+    xq, xs = K.act_quant(_bf16_gpu(x), qt, activation=WF_ACT_GELU_TANH)
+    xs = xs.cpu().numpy()
+    assert np.all(np.abs(xs - rs) <= rs * 2.0**-7)
+    got = xq.cpu().numpy().view(rq.dtype)
+    mism = got != rq
+    assert mism.mean() <= 1e-3
+    if qtype == "e4m3":
+        dg, dr = o_codec.e4m3_decode(got[mism]), o_codec.e4m3_decode(rq[mism])
+        assert np.all(np.abs(dg - dr) <= np.maximum(np.abs(dr) * 0.126, 2.0**-9 * 1.001))  # one e4m3 step
+    else:
+        assert np.all(np.abs(got[mism].astype(np.int32) - rq[mism].astype(np.int32)) <= 1)
+
+
 def test_gemm_per_tensor_matches_reference_golden(golden):
     """The reference's per-tensor WaveFp8Linear outputs, through our GEMM."""
     K = _kernels()

@@ -14,7 +14,8 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
 
 
-def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2, fused_assembly=True):
+def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2, fused_assembly=True,
+         w8a8=None):
     from waveforcing_b200.runtime import backend
     from waveforcing_b200.wavefront.dit import DiTConfig, WanDiT
     from waveforcing_b200.wavefront.engine import EngineConfig, WavefrontEngine
@@ -23,6 +24,10 @@ def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2
     dev = torch.device("cuda", 0)
     cfg = DiTConfig(dim=256, heads=2, layers=layers, ffn=512, text_len=16, text_dim=64, lat_h=16, lat_w=24)
     model = WanDiT.random(cfg, dev, seed=0)
+    if w8a8 is not None:
+        from waveforcing_b200.runtime.fp8 import quantize_transformer_w8a8
+
+        quantize_transformer_w8a8(model, scope="all", qtype=w8a8, granularity="channel")
     g = torch.Generator(device="cpu").manual_seed(1)
     model.set_text(torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(dev))
     eng = WavefrontEngine(model, EngineConfig(steps=steps, num_frames=num_frames, fp8_kv=fp8), device=dev)
@@ -84,3 +89,22 @@ def test_fused_context_assembly_is_bit_identical(fp8):
     a = _run("wf_b200", fp8, fused_assembly=True)
     b = _run("wf_b200", fp8, fused_assembly=False)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("qtype", ["e4m3", "int8"])
+def test_w8a8_ffn_fusion_matches_unfused(qtype):
+    """W8A8 linears (per-channel weights, per-token activations): the fused
+    FFN (plain fc_in GEMM, GELU(tanh) inside fc_out's input quantiser) against
+    the unfused block (torch GELU between two W8A8 linears)."""
+    from waveforcing_b200.wavefront import dit
+
+    orig = dit.WanDiT.forward_stages
+    try:
+        dit.WanDiT.forward_stages = lambda self, tasks, layer_hook=None, fused=True: orig(self, tasks, layer_hook,
+                                                                                          fused=False)
+        b = _run("wf_b200", True, w8a8=qtype)
+    finally:
+        dit.WanDiT.forward_stages = orig
+    a = _run("wf_b200", True, w8a8=qtype)
+    assert torch.isfinite(a).all()
+    assert _cos(a, b) >= 0.999

@@ -57,6 +57,7 @@ _SIGS = {
                                    C.POINTER(_vp), C.POINTER(_vp), _i32, _vp]),
     "wf_weight_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp]),
     "wf_act_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
+    "wf_act_quant_act": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "wf_gemm_w8a8": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
     "wf_gemm_w8a8_act": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _vp]),
     "wf_rope_apply": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i64, _vp]),

@@ -49,14 +49,22 @@ __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, uint6
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // GELU with the tanh approximation (torch GELU(approximate="tanh")):
-// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), tanh(u) = 1 - 2 / (1 + e^(2u)).
-// e^(2u) saturates to inf / 0 for large |u|, giving tanh = +-1.
+// 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715 x^3), evaluated as
+// x * sigmoid(2u) = x / (1 + e^(-2u)).  That form has no cancellation for
+// negative x (where 1 + tanh(u) is small): e^(-2u) from ex2.approx and the
+// reciprocal from rcp.approx keep the relative error near 2^-22; e^(-2u)
+// saturates to +inf / 0 for large |u|, giving 0 / x.
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
-  const float e = ex2_approx(u * 2.8853900817779268f);  // e^(2u)
+  const float e = ex2_approx(u * -2.8853900817779268f);  // e^(-2u)
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
-  return 0.5f * x * (2.f - 2.f * r);
+  return x * r;
+}
+
+// bf16 GELU(tanh) of two bf16 values in one word (f32 math, RNE back to bf16).
+__device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t w) {
+  return pack_bf16x2(gelu_tanh(__uint_as_float(w << 16)), gelu_tanh(__uint_as_float(w & 0xFFFF0000u)));
 }
 
 // Persistent: CTA c processes output tiles c, c + gridDim.x, ... (tile t ->
@@ -296,7 +304,9 @@ __global__ void weight_quant_kernel(const __nv_bfloat16* __restrict__ w, uint8_t
 // registers for NCH8 > 0 (K = NCH8 * 256), otherwise it is read twice.  The
 // division is one multiply by RN(1/s) (exact for bf16 x and s; see
 // quant_rows.cuh); rows with a non-finite scale take the IEEE division.
-template <bool I8, int NCH8>
+// GELU: the row is first mapped through bf16(GELU_tanh(x)) -- the FFN's
+// activation, quantised for fc_out without its bf16 output ever being stored.
+template <bool I8, bool GELU, int NCH8>
 __global__ void __launch_bounds__(256)
     act_quant_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ xq, float* __restrict__ x_scale,
                      int64_t M, int64_t K, int64_t xs) {
@@ -304,6 +314,11 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t nch = K / 8;
+  auto load = [&](const uint4* p) -> uint4 {
+    uint4 v = __ldcs(p);
+    if constexpr (GELU) v = make_uint4(gelu_bf16x2(v.x), gelu_bf16x2(v.y), gelu_bf16x2(v.z), gelu_bf16x2(v.w));
+    return v;
+  };
   for (int64_t m = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += nwarps) {
     const uint4* r4 = reinterpret_cast<const uint4*>(x + m * xs);
     uint2* out = reinterpret_cast<uint2*>(xq + m * K);
@@ -312,11 +327,11 @@ __global__ void __launch_bounds__(256)
     if constexpr (NCH8 > 0) {
 #pragma unroll
       for (int i = 0; i < NCH8; ++i) {
-        buf[i] = __ldg(r4 + lane + 32 * i);
+        buf[i] = load(r4 + lane + 32 * i);
         m2 = amax8_bits(buf[i], m2);
       }
     } else {
-      for (int64_t c = lane; c < nch; c += 32) m2 = amax8_bits(__ldg(r4 + c), m2);
+      for (int64_t c = lane; c < nch; c += 32) m2 = amax8_bits(load(r4 + c), m2);
     }
     const RowQuant q = make_rowq(warp_amax_bits(m2), I8 ? 127.f : 448.f);
     auto quant8v = [&](const uint4& v) -> uint2 {
@@ -342,7 +357,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
       for (int i = 0; i < NCH8; ++i) out[lane + 32 * i] = quant8v(buf[i]);
     } else {
-      for (int64_t c = lane; c < nch; c += 32) out[c] = quant8v(__ldg(r4 + c));
+      for (int64_t c = lane; c < nch; c += 32) out[c] = quant8v(load(r4 + c));
     }
     if (lane == 0) x_scale[m] = q.s;
   }
@@ -431,12 +446,14 @@ extern "C" int wf_weight_quant(const void* w, void* wq, float* w_scale, int64_t 
   return WF_OK;
 }
 
-extern "C" int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, int64_t K, int64_t x_row_stride,
-                            int qtype, void* stream) {
+extern "C" int wf_act_quant_act(const void* x, void* xq, float* x_scale, int64_t M, int64_t K,
+                                int64_t x_row_stride, int qtype, int activation, void* stream) {
   if (!x || !xq || !x_scale || M < 0 || K < 8 || K % 8 || x_row_stride < K || x_row_stride % 8 || !aligned16(x) ||
       (reinterpret_cast<uintptr_t>(xq) & 7))
     return fail(WF_ERR_INVALID_ARG, "wf_act_quant: bad arguments");
   if (qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8) return fail(WF_ERR_UNSUPPORTED, "wf_act_quant: qtype");
+  if (activation != WF_ACT_NONE && activation != WF_ACT_GELU_TANH)
+    return fail(WF_ERR_INVALID_ARG, "wf_act_quant_act: activation must be WF_ACT_NONE or WF_ACT_GELU_TANH");
   if (M == 0) return WF_OK;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -447,26 +464,34 @@ extern "C" int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto xb = static_cast<const __nv_bfloat16*>(x);
   auto qb = static_cast<uint8_t*>(xq);
-  auto go = [&](auto i8, auto nch) {
-    act_quant_kernel<decltype(i8)::value, decltype(nch)::value><<<blocks, 256, 0, s>>>(xb, qb, x_scale, M, K,
-                                                                                      x_row_stride);
+  auto go = [&](auto i8, auto gelu, auto nch) {
+    act_quant_kernel<decltype(i8)::value, decltype(gelu)::value, decltype(nch)::value>
+        <<<blocks, 256, 0, s>>>(xb, qb, x_scale, M, K, x_row_stride);
   };
-  auto by_k = [&](auto i8) {
+  auto by_k = [&](auto i8, auto gelu) {
     if (K == 1536)
-      go(i8, std::integral_constant<int, 6>());
+      go(i8, gelu, std::integral_constant<int, 6>());
     else if (K == 3072)
-      go(i8, std::integral_constant<int, 12>());
+      go(i8, gelu, std::integral_constant<int, 12>());
     else if (K == 5120)
-      go(i8, std::integral_constant<int, 20>());
+      go(i8, gelu, std::integral_constant<int, 20>());
+    else if (K == 8960)
+      go(i8, gelu, std::integral_constant<int, 35>());
     else
-      go(i8, std::integral_constant<int, 0>());
+      go(i8, gelu, std::integral_constant<int, 0>());
   };
+  const bool gelu = activation == WF_ACT_GELU_TANH;
   if (qtype == WF_DTYPE_S8)
-    by_k(std::true_type());
+    gelu ? by_k(std::true_type(), std::true_type()) : by_k(std::true_type(), std::false_type());
   else
-    by_k(std::false_type());
+    gelu ? by_k(std::false_type(), std::true_type()) : by_k(std::false_type(), std::false_type());
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
+}
+
+extern "C" int wf_act_quant(const void* x, void* xq, float* x_scale, int64_t M, int64_t K, int64_t x_row_stride,
+                            int qtype, void* stream) {
+  return wf_act_quant_act(x, xq, x_scale, M, K, x_row_stride, qtype, WF_ACT_NONE, stream);
 }
 
 extern "C" unsigned int wfk_status_take_gemm(void) { return wfk::status_take_local(); }

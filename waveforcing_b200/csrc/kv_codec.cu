@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 }
 
-// Publish v2: NDST destinations known at compile time (pointer table stays in
+// Fused publish: NDST destinations known at compile time (pointer table stays in
 // parameter space), each lane owns 16 consecutive elements per chunk so every
 // destination receives 16-byte code stores, and warps loop over rows.
 // NCH16 = cols / 512.

@@ -136,15 +136,17 @@ def weight_quant(w: torch.Tensor, qtype: int = L.WF_DTYPE_E4M3):
 
 
 def act_quant(x: torch.Tensor, qtype: int = L.WF_DTYPE_E4M3, xq: torch.Tensor | None = None,
-              xs: torch.Tensor | None = None):
+              xs: torch.Tensor | None = None, activation: int = L.WF_ACT_NONE):
+    """Per-token activation quantisation of x [M, K] bf16; activation
+    WF_ACT_GELU_TANH quantises bf16(GELU_tanh(x)) instead."""
     _need_cuda(x)
     M, K = x.shape
     if xq is None:
         xq = torch.empty((M, K), dtype=torch.uint8, device=x.device)
     if xs is None:
         xs = torch.empty((M,), dtype=torch.float32, device=x.device)
-    L.check(L.lib().wf_act_quant(x.data_ptr(), xq.data_ptr(), xs.data_ptr(), M, K, x.stride(0), qtype, _stream()),
-            "wf_act_quant")
+    L.check(L.lib().wf_act_quant_act(x.data_ptr(), xq.data_ptr(), xs.data_ptr(), M, K, x.stride(0), qtype,
+                                     activation, _stream()), "wf_act_quant_act")
     return xq, xs
 
 

@@ -53,14 +53,17 @@ class WfW8A8Linear(nn.Module):
         self.register_buffer("bias", bias.detach().to(torch.bfloat16) if bias is not None else None)
         self._ws = None
 
-    def _raw(self, x2: torch.Tensor, activation: int = L.WF_ACT_NONE) -> torch.Tensor:
+    def _raw(self, x2: torch.Tensor, activation: int = L.WF_ACT_NONE,
+             input_activation: int = L.WF_ACT_NONE) -> torch.Tensor:
         x2 = x2.to(torch.bfloat16)
         if x2.stride(-1) != 1 or x2.stride(0) % 8:
             x2 = x2.contiguous()
         if self.granularity == "channel":
-            xq, xs = kernels.act_quant(x2, self.qtype)
+            xq, xs = kernels.act_quant(x2, self.qtype, activation=input_activation)
             mode = L.WF_SCALE_TOKEN
         else:
+            if input_activation != L.WF_ACT_NONE:
+                raise ValueError("an input activation is only fused into the per-token quantiser")
             if self._ws is None or self._ws.device != x2.device:
                 self._ws = torch.empty(1, dtype=torch.int32, device=x2.device)
             xq, xs = kernels.kv_quant(x2, L.WF_SCALE_TENSOR, workspace=self._ws)
@@ -71,6 +74,14 @@ class WfW8A8Linear(nn.Module):
         shape = x.shape
         y = self._raw(x.reshape(-1, shape[-1]))
         return y.reshape(*shape[:-1], self.out_features), None
+
+    def forward_gelu_input(self, x: torch.Tensor) -> torch.Tensor:
+        """This linear applied to GELU(approximate="tanh")(x): the activation is
+        computed inside the per-token input quantiser, so the bf16 activation
+        tensor is never written (the FFN's fc_out after a plain fc_in)."""
+        shape = x.shape
+        y = self._raw(x.reshape(-1, shape[-1]), input_activation=L.WF_ACT_GELU_TANH)
+        return y.reshape(*shape[:-1], self.out_features)
 
     def forward_gelu(self, x: torch.Tensor) -> torch.Tensor:
         """GELU(approximate="tanh") of this linear's bf16 output, fused into the

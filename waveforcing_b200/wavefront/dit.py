@@ -352,14 +352,17 @@ class WanDiT(nn.Module):
             oc = dispatch_attention(qc, kc, vc)
             xs = gate_add(xs, _lin(b.cross_attn.o, oc.view(S * T, dim)), None, 0)
             h = ln_mod(xs, e_all, 3)
-            fi = b.ffn.fc_in
+            fi, fo = b.ffn.fc_in, b.ffn.fc_out
             if fused and type(fi) is nn.Linear:
                 a = torch._addmm_activation(fi.bias, h, fi.weight.t(), use_gelu=True)  # cuBLASLt bias+GELU(tanh)
+                y = _lin(fo, a)
+            elif fused and getattr(fo, "granularity", None) == "channel" and hasattr(fo, "forward_gelu_input"):
+                # W8A8, per-token: plain fc_in GEMM, GELU(tanh) inside fc_out's input quantiser
+                y = fo.forward_gelu_input(_lin(fi, h))
             elif fused and hasattr(fi, "forward_gelu"):
-                a = fi.forward_gelu(h)  # W8A8 GEMM with GELU(tanh) in its epilogue
+                y = _lin(fo, fi.forward_gelu(h))  # W8A8 GEMM with GELU(tanh) in its epilogue
             else:
-                a = F.gelu(_lin(fi, h), approximate="tanh")
-            y = _lin(b.ffn.fc_out, a)
+                y = _lin(fo, F.gelu(_lin(fi, h), approximate="tanh"))
             xs = gate_add(xs, y, e_all, 5)
             if layer_hook is not None:
                 layer_hook(li)
