@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec", "dequant", "publish"],
                     help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
+    ap.add_argument("--forward", action="store_true",
+                    help="BASELINE config 2: one full DiT forward of a 3-frame chunk at t=600 with a 6-chunk context")
     return ap.parse_args()
 
 
@@ -592,9 +594,66 @@ def run_publish_bench(args):
     dist.destroy_process_group()
 
 
+def run_forward_bench(args):
+    """BASELINE config 2 on one GPU: the full 30-layer (1.3B) DiT forward of one
+    3-frame chunk-stage task at timestep 600 whose self-attention sees a
+    6-chunk K/V context (5 earlier chunks, random bf16 per layer, plus its own
+    chunk), with the text cross-attention.  CUDA-event timed per forward."""
+    from waveforcing_b200.runtime import backend
+    from waveforcing_b200.runtime.fp8 import quantize_transformer_w8a8
+    from waveforcing_b200.wavefront.dit import DiTConfig, StageTask, WanDiT
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.set_grad_enabled(False)
+    backend.select_backend("wf_b200")
+    cfg = DiTConfig.preset(args.preset)
+    model = WanDiT.random(cfg, dev, seed=0)
+    if args.w8a8 != "none":
+        quantize_transformer_w8a8(model, scope="all", qtype=args.w8a8, granularity="channel")
+    g = torch.Generator(device="cpu").manual_seed(0)
+    model.set_text(torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(dev))
+    T, H, D = cfg.tokens_per_chunk, cfg.heads, cfg.head_dim
+    ctx = 6
+    gd = torch.Generator(device=dev).manual_seed(1)
+    kctx = [torch.randn(1, ctx * T, H, D, device=dev, generator=gd).bfloat16() for _ in range(cfg.layers)]
+    vctx = [torch.randn(1, ctx * T, H, D, device=dev, generator=gd).bfloat16() for _ in range(cfg.layers)]
+
+    def exch(*, layer_idx, roped_query, roped_key, unroped_key, value, **_):
+        kctx[layer_idx][0, (ctx - 1) * T:].copy_(roped_key[0])
+        vctx[layer_idx][0, (ctx - 1) * T:].copy_(value[0])
+        return kctx[layer_idx], vctx[layer_idx]
+
+    lat = torch.randn(cfg.in_ch, cfg.frames_per_block, cfg.lat_h, cfg.lat_w, device=dev, generator=gd)
+    task = StageTask(lat, 600.0, (ctx - 1) * cfg.frames_per_block, 0, exch)
+    for _ in range(max(3, args.warmup)):
+        model.forward_stages([task])
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    evs[0].record()
+    for i in range(args.steps):
+        model.forward_stages([task])
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    ms = statistics.median([evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)])
+    dim, ffn = cfg.dim, cfg.ffn
+    lin = 2 * T * (6 * dim * dim + 2 * dim * ffn)  # q,k,v,o, cross q,o, FFN in+out (cross K/V are cached)
+    flops = cfg.layers * (4 * T * ctx * T * H * D + lin + 4 * T * cfg.text_len * H * D)
+    peaks, src = _peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({"workload": f"config 2: {args.preset} DiT forward, one 3-frame chunk (T={T}) at t=600, "
+                                  f"{ctx}-chunk self-attention context, 512-token text",
+                      "ms_per_forward_p50": ms, "steps": args.steps, "tflop_per_forward": flops / 1e12,
+                      "achieved_tflops": tf, "frac_of_sustained_bf16": tf / peaks["bf16_tflops_sustained"],
+                      "peak_source": src, "w8a8": args.w8a8, "data": "synthetic (random-init weights and context)"}),
+          flush=True)
+
+
 def main():
     args = parse()
-    if args.kernel == "publish":
+    if args.forward:
+        run_forward_bench(args)
+    elif args.kernel == "publish":
         run_publish_bench(args)
     elif args.kernel:
         run_kernel_bench(args)
