@@ -296,8 +296,11 @@ def run_gpu_arm(args):
     # exposed exchange: device time this rank's compute stream spent in remote flag waits
     wait_ms_rank = sum(e0.elapsed_time(e1) for e0, e1 in wait_sink) / args.steps
     wait_ms = max_over_ranks([wait_ms_rank])[0]
-    # the critical rank hosts stage 0 (the longest K/V context): its waits are the exposed exchange
-    crit = max_over_ranks([wait_ms_rank if 0 in eng.local else 0.0])[0]
+    # Every rank's tick has the same length, so the critical (busiest) rank is
+    # the active rank that waits least; its waits are the exchange time exposed
+    # on the critical path.  Ranks without stages (N = 8: two) are left out.
+    crit = -max_over_ranks([-wait_ms_rank if eng.local else float("-inf")])[0]
+    stage0_wait = max_over_ranks([wait_ms_rank if 0 in eng.local else 0.0])[0]
     host_p50 = max_over_ranks([statistics.median(host_ms)])[0]
     eng.close()
     del eng
@@ -379,8 +382,10 @@ def run_gpu_arm(args):
             "exchange": {"critical_rank_wait_ms_per_tick": crit,
                          "critical_frac_of_tick": crit / p50 if p50 else None,
                          "max_rank_wait_ms_per_tick": wait_ms,
+                         "stage0_rank_wait_ms_per_tick": stage0_wait,
                          "note": "device time consumer streams spent in bounded flag waits for remote K/V; "
-                                 "the critical rank hosts stage 0, lighter ranks wait for slower producers"},
+                                 "the critical rank is the active rank that waits least (the busiest: its "
+                                 "waits are on the critical path); lighter ranks wait for slower producers"},
             "host_issue_ms_per_tick_p50": host_p50,
             "gpu_launches": launches,
             "clocks": clocks,
