@@ -58,6 +58,10 @@ def parse():
     ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec", "dequant", "publish"],
                     help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
+    ap.add_argument("--kv-len", type=int, default=0,
+                    help="--kernel attn: K/V length in tokens (overrides --ctx-chunks; 512 = cross-attention)")
+    ap.add_argument("--library", action="store_true",
+                    help="--kernel attn: also time torch SDPA, the reference's attention call, on the same buffers")
     ap.add_argument("--forward", action="store_true",
                     help="BASELINE config 2: one full DiT forward of a 3-frame chunk at t=600 with a 6-chunk context")
     return ap.parse_args()
@@ -424,15 +428,25 @@ def run_kernel_bench(args):
         return max(2, int(math.ceil(1.5 * l2 / set_bytes)))
 
     fns = []
+    lib_fns = []  # torch SDPA on the same buffers (--library)
+    lib_diff = None
     if args.kernel == "attn":
-        Lk = args.ctx_chunks * T
+        Lk = args.kv_len if args.kv_len > 0 else args.ctx_chunks * T
         set_bytes = 2 * (2 * T + 2 * Lk) * H * D
-        for _ in range(n_sets(set_bytes)):
+        for i in range(n_sets(set_bytes)):
             q = torch.randn(1, T, H, D, device=dev, generator=g).bfloat16()
             k = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
             v = torch.randn(1, Lk, H, D, device=dev, generator=g).bfloat16()
             o = torch.empty_like(q)
             fns.append(lambda q=q, k=k, v=v, o=o: kernels.attention(q, k, v, out=o))
+            if args.library:
+                # torch SDPA wants [batch, heads, tokens, dim]; the transposed views share storage.
+                qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+                lib_fns.append(lambda qt=qt, kt=kt, vt=vt: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt))
+                if i == 0:
+                    ref = lib_fns[0]().transpose(1, 2)
+                    lib_diff = float((kernels.attention(q, k, v).float() - ref.float()).abs().max())
+                    del ref
         work, unit, bound = 4.0 * T * Lk * H * D / 1e12, "TFLOP/s", "tensor"
         name = f"attn_fwd q{T} kv{Lk} h{H}"
     elif args.kernel == "gemm":
@@ -477,23 +491,35 @@ def run_kernel_bench(args):
         work = (2 * T * HD * 2 + n * 2 * (T * HD + 4 * T)) / 1e9
         unit, bound = "GB/s", "hbm"
         name = f"kv_quant_publish {T}x{HD} to {n} slots"
-    for i in range(max(3, args.warmup)):
-        fns[i % len(fns)]()
-    torch.cuda.synchronize()
     launches = max(args.steps, len(fns))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for i in range(launches):
-            fns[i % len(fns)]()
-    graph.replay()  # warm the graph itself
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / launches
-    del graph
+
+    def graph_ms(fs):
+        for i in range(max(3, args.warmup)):
+            fs[i % len(fs)]()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(launches):
+                fs[i % len(fs)]()
+        graph.replay()  # warm the graph itself
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / launches
+        del graph
+        return t
+
+    ms = graph_ms(fns)
+    library = None
+    if lib_fns:
+        lms = graph_ms(lib_fns)
+        library = {"name": "torch SDPA, default dispatch (cuDNN on B200)", "ms": lms,
+                   "achieved": work / (lms * 1e-3), "max_abs_diff_vs_wf": lib_diff,
+                   # the product kernel once more after the library leg, to expose clock drift
+                   "wf_ms_after": graph_ms(fns)}
     peaks, src = _peaks()
     peak = peaks["bf16_tflops"] if bound == "tensor" else peaks["hbm_gbs"]
     if args.kernel == "gemm":
@@ -501,7 +527,8 @@ def run_kernel_bench(args):
     ach = work / (ms * 1e-3)
     print(json.dumps({"kernel": name, "ms": ms, "achieved": ach, "unit": unit, "peak": peak,
                       "frac": ach / peak, "peak_source": src + (" bf16 burst x2" if args.kernel == "gemm" else ""),
-                      "launches": launches, "buffer_sets": len(fns), "status": L.status_take()}), flush=True)
+                      "launches": launches, "buffer_sets": len(fns), "status": L.status_take(),
+                      **({"library": library} if library else {})}), flush=True)
 
 
 def run_publish_bench(args):
