@@ -6,7 +6,6 @@ reference tests its close ordering the same way, tests/test_ipc_lifecycle.py).""
 import os
 import socket
 
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp

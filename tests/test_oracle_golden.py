@@ -1,7 +1,6 @@
 """Pin the CPU oracle to golden vectors produced by the reference's own code."""
 
 import numpy as np
-import pytest
 import torch
 
 from oracle import attention, codec, geometry, rope, w8a8

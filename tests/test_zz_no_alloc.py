@@ -14,7 +14,6 @@ This file is collected last so a failure here cannot hide other results.
 
 import ctypes as C
 
-import numpy as np
 import pytest
 import torch
 
