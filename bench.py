@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--w8a8", default="none", choices=["none", "e4m3", "int8"])
     ap.add_argument("--denoise-steps", default="1000,800,600,400,200")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec", "dequant", "publish"],
+    ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec", "dequant", "assemble", "publish"],
                     help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
     ap.add_argument("--kv-len", type=int, default=0,
@@ -410,6 +410,9 @@ def run_kernel_bench(args):
       codec per-token FP8 quantise-and-publish of one layer's K and V to 4 slots
       dequant per-token FP8 dequantise of one layer's 5 received K and V slots
               into the bf16 context buffer (one launch for K, one for V)
+      assemble one layer's r0 K/V context in one wf_kv_assemble launch: anchor
+              key re-RoPEd into slot 0, anchor value, one working page and
+              the own chunk copied, 5 received FP8 slots dequantised
     The launches rotate over independent buffer sets whose total footprint
     exceeds L2 (126 MB), so each launch reads its inputs from HBM, and `steps`
     launches are captured in one CUDA graph so that host-side argument
@@ -460,6 +463,38 @@ def run_kernel_bench(args):
             fns.append(lambda xq=xq, xs=xs, wq=wq, ws=ws, out=out: kernels.gemm_w8a8(xq, xs, wq, ws, None, out=out))
         work, unit, bound = 2.0 * T * cfg.dim * cfg.ffn / 1e12, "TFLOP/s", "tensor"
         name = f"gemm_w8a8 e4m3 {T}x{cfg.ffn}x{cfg.dim}"
+    elif args.kernel == "assemble":
+        HD = H * D
+        n_deq = 5
+        ctx = (3 + n_deq) * T  # anchor, working, own chunk, received slots
+        set_bytes = 6 * T * HD * 2 + 2 * n_deq * T * (HD + 4) + 2 * ctx * HD * 2 + 2 * T * (D // 2) * 4
+        for _ in range(n_sets(set_bytes)):
+            pages = [torch.randn(T, HD, device=dev, generator=g).bfloat16() for _ in range(6)]
+            codes = [torch.randint(0, 256, (n_deq * T, HD), device=dev, dtype=torch.uint8, generator=g)
+                     for _ in range(2)]
+            for c in codes:
+                c[(c & 0x7F) == 0x7F] = 0  # no NaN codes
+            scales = [torch.rand(n_deq * T, device=dev, generator=g) + 0.5 for _ in range(2)]
+            ang = torch.rand(T, D // 2, device=dev, generator=g) * 6.2831853
+            cos, sin = torch.cos(ang), torch.sin(ang)
+            kb = torch.empty(ctx, HD, device=dev, dtype=torch.bfloat16)
+            vb = torch.empty_like(kb)
+            kp, vp, rb = kb.data_ptr(), vb.data_ptr(), HD * 2
+            segs = [(L.WF_SEG_ROPE, pages[0].data_ptr(), cos.data_ptr(), sin.data_ptr(), kp, T, HD, HD),
+                    (L.WF_SEG_COPY, pages[1].data_ptr(), 0, 0, vp, T, HD, HD)]
+            for i, base in ((2, T), (4, 2 * T)):  # working page, own chunk
+                segs.append((L.WF_SEG_COPY, pages[i].data_ptr(), 0, 0, kp + base * rb, T, HD, HD))
+                segs.append((L.WF_SEG_COPY, pages[i + 1].data_ptr(), 0, 0, vp + base * rb, T, HD, HD))
+            segs.append((L.WF_SEG_DEQUANT, codes[0].data_ptr(), scales[0].data_ptr(), 0, kp + 3 * T * rb,
+                         n_deq * T, HD, HD))
+            segs.append((L.WF_SEG_DEQUANT, codes[1].data_ptr(), scales[1].data_ptr(), 0, vp + 3 * T * rb,
+                         n_deq * T, HD, HD))
+            keep = (pages, codes, scales, cos, sin, kb, vb)
+            fns.append(lambda segs=segs, keep=keep: kernels.kv_assemble(segs, HD, D))
+        # ROPE: 2+2 B/elem + 512 B of cos/sin per row; COPY: 2+2 B/elem; DEQUANT: 1+2 B/elem + 4 B/row
+        work = (T * (4 * HD + 2 * (D // 2) * 4) + 5 * T * HD * 4 + 2 * n_deq * T * (3 * HD + 4)) / 1e9
+        unit, bound = "GB/s", "hbm"
+        name = f"kv_assemble r0 context {ctx}x{HD} K+V (RoPE anchor, 5 copied pages, {2 * n_deq} FP8 slots)"
     elif args.kernel == "dequant":
         HD = H * D
         R = 5 * T
