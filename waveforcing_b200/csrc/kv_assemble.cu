@@ -10,6 +10,9 @@
 // straight into the context buffer, and all segments of K and V of one layer
 // share a launch.  A warp per row; lane l handles 16-byte output chunks l,
 // l + 32, ... so loads and stores of a row are contiguous across the warp.
+// Each lane issues UNR loads before their stores: without that the compiler,
+// which cannot rule out that dst aliases src, keeps one load per lane in
+// flight.
 #include <cuda_runtime.h>
 
 #include "host_util.h"
@@ -21,6 +24,7 @@ namespace assemble {
 
 constexpr int MAX_SEGS = 24;
 constexpr int WARPS = 8;
+constexpr int UNR = 6;  // chunks per lane in flight (a 1536-column row is 6 per lane)
 
 struct Params {
   wf_kv_segment seg[MAX_SEGS];
@@ -59,20 +63,45 @@ __global__ void __launch_bounds__(WARPS * 32) assemble_kernel(const __grid_const
     if (sg.kind == WF_SEG_DEQUANT) {
       const uint2* src = reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(sg.src) + row * sg.src_row_stride);
       const float s = __ldg(sg.aux0 + row);
-      for (int64_t c = lane; c < nch; c += 32) dst[c] = quant::dequant8(__ldcs(src + c), s);
+      for (int64_t c0 = lane; c0 < nch; c0 += 32 * UNR) {
+        uint2 v[UNR];
+#pragma unroll
+        for (int u = 0; u < UNR; ++u)
+          if (c0 + u * 32 < nch) v[u] = __ldcs(src + c0 + u * 32);
+#pragma unroll
+        for (int u = 0; u < UNR; ++u)
+          if (c0 + u * 32 < nch) dst[c0 + u * 32] = quant::dequant8(v[u], s);
+      }
     } else {
       const uint4* src =
           reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(sg.src) + row * sg.src_row_stride);
       if (sg.kind == WF_SEG_ROPE) {
         const float* ct = sg.aux0 + row * half_d;
         const float* st = sg.aux1 + row * half_d;
-        for (int64_t c = lane; c < nch; c += 32) {
-          const int d2 = static_cast<int>((c * 8) % p.head_dim) / 2;
-          dst[c] = rope8(__ldg(src + c), *reinterpret_cast<const float4*>(ct + d2),
-                         *reinterpret_cast<const float4*>(st + d2));
+        for (int64_t c0 = lane; c0 < nch; c0 += 32 * UNR) {
+          uint4 v[UNR];
+#pragma unroll
+          for (int u = 0; u < UNR; ++u)
+            if (c0 + u * 32 < nch) v[u] = __ldg(src + c0 + u * 32);
+#pragma unroll
+          for (int u = 0; u < UNR; ++u) {
+            const int64_t c = c0 + u * 32;
+            if (c < nch) {
+              const int d2 = static_cast<int>((c * 8) % p.head_dim) / 2;
+              dst[c] = rope8(v[u], *reinterpret_cast<const float4*>(ct + d2), *reinterpret_cast<const float4*>(st + d2));
+            }
+          }
         }
       } else {
-        for (int64_t c = lane; c < nch; c += 32) dst[c] = __ldg(src + c);
+        for (int64_t c0 = lane; c0 < nch; c0 += 32 * UNR) {
+          uint4 v[UNR];
+#pragma unroll
+          for (int u = 0; u < UNR; ++u)
+            if (c0 + u * 32 < nch) v[u] = __ldg(src + c0 + u * 32);
+#pragma unroll
+          for (int u = 0; u < UNR; ++u)
+            if (c0 + u * 32 < nch) dst[c0 + u * 32] = v[u];
+        }
       }
     }
   }
