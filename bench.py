@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
     ap.add_argument("--kv-len", type=int, default=0,
                     help="--kernel attn: K/V length in tokens (overrides --ctx-chunks; 512 = cross-attention)")
+    ap.add_argument("--q-len", type=int, default=0,
+                    help="--kernel attn: query length in tokens (default one chunk; 28080 = the tick's "
+                         "batched cross-attention of six stages)")
     ap.add_argument("--library", action="store_true",
                     help="--kernel attn: also time torch SDPA, the reference's attention call, on the same buffers")
     ap.add_argument("--forward", action="store_true",
@@ -376,7 +379,9 @@ def run_gpu_arm(args):
                        "kv_transport": args.kv, "w8a8": args.w8a8, "world": world,
                        "l2": "inputs larger than L2 (K/V slabs and weights, GBs per tick)",
                        "parallelism": f"wavefront stages over {min(world, S + 1)} GPU(s)"},
-            "roofline": {"bound": "tensor", "kernel": "attn_fwd_bf16_kernel (self + cross attention)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "attn_fwd_bf16_kernel (wavefront self-attention; the text cross-attention "
+                                   "runs on torch SDPA, as in the reference)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None, "traffic": traffic,
                          "launches": n_attn, "peak_source": f"{src} bf16_tflops_sustained"},
@@ -435,6 +440,8 @@ def run_kernel_bench(args):
     lib_diff = None
     if args.kernel == "attn":
         Lk = args.kv_len if args.kv_len > 0 else args.ctx_chunks * T
+        if args.q_len > 0:
+            T = args.q_len
         set_bytes = 2 * (2 * T + 2 * Lk) * H * D
         for i in range(n_sets(set_bytes)):
             q = torch.randn(1, T, H, D, device=dev, generator=g).bfloat16()

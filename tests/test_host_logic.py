@@ -166,3 +166,47 @@ def test_context_assembly_segments(monkeypatch):
             (L.WF_SEG_DEQUANT, vc.data_ptr(), vs.data_ptr(), 0, Vb.data_ptr() + 5 * T * row, 2 * T, HD, HD)]
     assert segs == exp
     assert any(w["kr"].stride(0) == 2 * HD for w in working)  # the strided page is among the working set
+
+
+def test_dit_routes_only_self_attention_through_the_backend(monkeypatch):
+    """The reference sends only the patched self-attention through a custom
+    kernel and leaves SGLang's other attention on torch SDPA
+    (wave_rt/runtime/backend.py:215-219).  A tiny DiT forward on CPU (plain
+    torch ops, RoPE restated in torch) must call the backend dispatch once per
+    stage and layer and the SDPA path once per layer for the text
+    cross-attention."""
+    from waveforcing_b200 import kernels
+    from waveforcing_b200.runtime import backend
+    from waveforcing_b200.wavefront import dit as D
+
+    def rope_torch(x, cos, sin, out=None):
+        xf = x.float().reshape(*x.shape[:-1], -1, 2)
+        re, im = xf[..., 0], xf[..., 1]
+        c, s = cos[:, None, :], sin[:, None, :]
+        return torch.stack([re * c - im * s, re * s + im * c], -1).flatten(-2).to(x.dtype)
+
+    calls = {"self": 0, "cross": 0}
+    orig_self, orig_cross = D.dispatch_attention, D.sdpa_elsewhere
+
+    def count_self(*a):
+        calls["self"] += 1
+        return orig_self(*a)
+
+    def count_cross(*a):
+        calls["cross"] += 1
+        return orig_cross(*a)
+
+    monkeypatch.setattr(kernels, "rope_apply", rope_torch)
+    monkeypatch.setitem(backend._WAVE_STATE, "attn", "torch_sdpa")
+    monkeypatch.setattr(D, "dispatch_attention", count_self)
+    monkeypatch.setattr(D, "sdpa_elsewhere", count_cross)
+    cfg = D.DiTConfig(dim=256, heads=2, layers=2, ffn=512, text_len=16, text_dim=64, lat_h=4, lat_w=4)
+    torch.manual_seed(0)
+    m = D.WanDiT.random(cfg, torch.device("cpu"), seed=0)
+    m.set_text(torch.randn(cfg.text_len, cfg.text_dim))
+    tasks = [D.StageTask(torch.randn(cfg.in_ch, cfg.frames_per_block, cfg.lat_h, cfg.lat_w), 600.0, 3 * s, s)
+             for s in (1, 0)]
+    out = m.forward_stages(tasks, fused=False)
+    assert [tuple(o.shape) for o in out] == [(cfg.in_ch, cfg.frames_per_block, cfg.lat_h, cfg.lat_w)] * 2
+    assert all(torch.isfinite(o).all() for o in out)
+    assert calls == {"self": cfg.layers * len(tasks), "cross": cfg.layers}

@@ -69,6 +69,14 @@ def _torch_sdpa(q, k, v):
     return out.transpose(1, 2)
 
 
+def sdpa_elsewhere(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Attention outside the wavefront path (the text cross-attention).  The
+    reference runs only the patched self-attention through its custom kernels
+    and leaves SGLang's other attention on torch SDPA for every custom backend
+    (wave_rt/runtime/backend.py:215-219); this does the same.  NHD in and out."""
+    return _torch_sdpa(q, k, v)
+
+
 def set_attention_timer(sink: list | None) -> None:
     """When ``sink`` is a list, every dispatched attention appends
     (flops, start_event, end_event, algorithmic_bytes) recorded on the current stream."""

@@ -9,7 +9,8 @@ its vendored statement is the naive Rolling-Forcing model, restated here:
                        RoPE q/k, call the exchange closure, attention on
                        (roped_query, ctx_k, ctx_v)
   * cross-attention -- naive_rt/rolling_forcing/wan/modules/model.py:158-196
-                       (text K/V computed once and cached)
+                       (text K/V computed once and cached), on torch SDPA as
+                       the reference leaves it (wave_rt/runtime/backend.py:215-219)
   * embeddings/head -- causal_model.py:524-533 and :421-433
   * x0 from flow    -- naive_rt/rolling_forcing/utils/wan_wrapper.py:169-193
   * presets/init    -- wave_rt/runtime/dummy_model.py:25-59 (N(0, 0.02))
@@ -30,7 +31,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from waveforcing_b200 import kernels
-from waveforcing_b200.runtime.backend import dispatch_attention
+from waveforcing_b200.runtime.backend import dispatch_attention, sdpa_elsewhere
 
 PRESETS = {
     "1.3b": dict(dim=1536, heads=12, layers=30, ffn=8960),
@@ -360,7 +361,7 @@ class WanDiT(nn.Module):
             qc = (kernels.rms_norm(qc, b.cross_attn.norm_q.weight, eps) if fused
                   else b.cross_attn.norm_q(qc)).view(1, S * T, H, D)
             kc, vc = self._cross_kv[li]
-            oc = dispatch_attention(qc, kc, vc)
+            oc = sdpa_elsewhere(qc, kc, vc)
             xs = gate_add(xs, _lin(b.cross_attn.o, oc.view(S * T, dim)), None, 0)
             h = ln_mod(xs, e_all, 3)
             fi, fo = b.ffn.fc_in, b.ffn.fc_out
