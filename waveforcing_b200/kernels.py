@@ -23,6 +23,14 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+def _check(cond: bool, msg: str) -> None:
+    """Shape/dtype validation the C ABI cannot do: it sees pointers, not sizes,
+    so a mis-shaped output or side tensor would be read or written out of
+    bounds.  Runs before the device check."""
+    if not cond:
+        raise ValueError(msg)
+
+
 def _need_cuda(*ts: torch.Tensor) -> None:
     for t in ts:
         if not t.is_cuda:
@@ -43,7 +51,6 @@ def _strides_bthd(t: torch.Tensor):
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """softmax(q k^T * scale) v on the tcgen05 kernel; NHD bf16, head_dim 128."""
-    _need_cuda(q, k, v)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
         raise TypeError("attention: q, k, v must be bfloat16")
     for t in (q, k, v):
@@ -56,6 +63,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: 
         raise ValueError(f"attention: shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    _check(out.shape == q.shape and out.dtype == torch.bfloat16 and out.device == q.device and out.stride(-1) == 1,
+           "attention: out must be bf16 with q's shape and device and a contiguous last dim")
+    _need_cuda(q, k, v, out)
     _, _, _, _, os_ = _strides_bthd(out)
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     L.check(
@@ -99,10 +109,17 @@ def kv_quant(x: torch.Tensor, mode: int = L.WF_SCALE_TOKEN, codes: torch.Tensor 
 
 def kv_dequant(codes: torch.Tensor, scales: torch.Tensor | None, mode: int = L.WF_SCALE_TOKEN,
                out: torch.Tensor | None = None) -> torch.Tensor:
-    _need_cuda(codes)
     if codes.dtype != torch.uint8 or codes.dim() != 2 or not codes.is_contiguous():
         raise ValueError("kv_dequant: codes must be a contiguous 2-D uint8 matrix")
     rows, cols = codes.shape
+    if mode != L.WF_SCALE_NONE:
+        _check(scales is not None and scales.dtype == torch.float32
+               and scales.numel() >= (rows if mode == L.WF_SCALE_TOKEN else 1),
+               "kv_dequant: f32 scales needed, one per row (token) or one (tensor)")
+    if out is not None:
+        _check(out.dim() == 2 and tuple(out.shape) == (rows, cols) and out.dtype == torch.bfloat16
+               and out.stride(-1) == 1, "kv_dequant: out must be bf16 [rows, cols] with contiguous rows")
+    _need_cuda(codes)
     if out is None:
         out = torch.empty((rows, cols), dtype=torch.bfloat16, device=codes.device)
     sp = scales.data_ptr() if scales is not None else 0
@@ -114,9 +131,13 @@ def kv_dequant(codes: torch.Tensor, scales: torch.Tensor | None, mode: int = L.W
 def kv_quant_publish(k: torch.Tensor, v: torch.Tensor, dst_codes_k, dst_codes_v, dst_scales_k, dst_scales_v) -> None:
     """Per-token quantise K and V [rows, cols] and write codes/scales to every
     destination (device pointers as ints, local or peer)."""
+    _check(k.dim() == 2 and v.shape == k.shape and k.dtype == v.dtype == torch.bfloat16,
+           "kv_quant_publish: k and v must be bf16 matrices of one shape")
+    n = len(dst_codes_k)
+    _check(n >= 1 and len(dst_codes_v) == len(dst_scales_k) == len(dst_scales_v) == n,
+           "kv_quant_publish: one code and one scale destination per K and V, same count")
     _need_cuda(k, v)
     rows, cols = k.shape
-    n = len(dst_codes_k)
     L.check(L.lib().wf_kv_quant_publish(k.data_ptr(), v.data_ptr(), rows, cols, k.stride(0), v.stride(0),
                                         L.ptr_array(dst_codes_k), L.ptr_array(dst_codes_v),
                                         L.ptr_array(dst_scales_k), L.ptr_array(dst_scales_v), n, _stream()),
@@ -125,6 +146,7 @@ def kv_quant_publish(k: torch.Tensor, v: torch.Tensor, dst_codes_k, dst_codes_v,
 
 def weight_quant(w: torch.Tensor, qtype: int = L.WF_DTYPE_E4M3):
     """bf16 [N, K] -> (codes [N, K] uint8/int8 storage, f32 scales [N])."""
+    _check(w.dim() == 2 and w.dtype == torch.bfloat16, "weight_quant: w must be a bf16 [N, K] matrix")
     _need_cuda(w)
     w = w.contiguous()
     N, K = w.shape
@@ -139,8 +161,12 @@ def act_quant(x: torch.Tensor, qtype: int = L.WF_DTYPE_E4M3, xq: torch.Tensor | 
               xs: torch.Tensor | None = None, activation: int = L.WF_ACT_NONE):
     """Per-token activation quantisation of x [M, K] bf16; activation
     WF_ACT_GELU_TANH quantises bf16(GELU_tanh(x)) instead."""
-    _need_cuda(x)
+    _check(x.dim() == 2 and x.dtype == torch.bfloat16 and x.stride(-1) == 1,
+           "act_quant: x must be a bf16 [M, K] matrix with contiguous rows")
     M, K = x.shape
+    _check(xq is None or tuple(xq.shape) == (M, K), "act_quant: xq must be [M, K]")
+    _check(xs is None or (xs.dtype == torch.float32 and xs.numel() >= M), "act_quant: xs must hold M f32 scales")
+    _need_cuda(x)
     if xq is None:
         xq = torch.empty((M, K), dtype=torch.uint8, device=x.device)
     if xs is None:
@@ -154,9 +180,18 @@ def gemm_w8a8(xq, xs, wq, ws, bias=None, qtype: int = L.WF_DTYPE_E4M3, scale_mod
               out: torch.Tensor | None = None, activation: int = L.WF_ACT_NONE) -> torch.Tensor:
     """y = (xq wq^T) * xs * ws + bias in bf16; activation WF_ACT_GELU_TANH applies
     GELU(tanh) to the bf16-rounded result in the same kernel."""
-    _need_cuda(xq, wq)
+    _check(xq.dim() == 2 and wq.dim() == 2 and xq.shape[1] == wq.shape[1],
+           "gemm_w8a8: xq [M, K] and wq [N, K] must share K")
     M, K = xq.shape
     N = wq.shape[0]
+    per_token = scale_mode == L.WF_SCALE_TOKEN
+    _check(xs.dtype == ws.dtype == torch.float32 and xs.numel() >= (M if per_token else 1)
+           and ws.numel() >= (N if per_token else 1),
+           "gemm_w8a8: f32 scales needed, x_scale per row and w_scale per channel (one each per tensor)")
+    _check(bias is None or bias.numel() == N, "gemm_w8a8: bias must have N elements")
+    _check(out is None or (tuple(out.shape) == (M, N) and out.dtype == torch.bfloat16 and out.stride(-1) == 1),
+           "gemm_w8a8: out must be bf16 [M, N] with contiguous rows")
+    _need_cuda(xq, wq)
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
     bp = bias.data_ptr() if bias is not None else 0
@@ -180,10 +215,14 @@ def kv_assemble(segments, cols: int, head_dim: int) -> None:
 
 def rope_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor | None = None):
     """Interleaved RoPE on bf16 [L, H, D] with f32 cos/sin [L, D/2]."""
-    _need_cuda(x, cos, sin)
     if x.dim() == 4:
         x = x[0]
     Lt, H, D = x.shape
+    for tab in (cos, sin):
+        _check(tab.dtype == torch.float32 and tab.dim() == 2 and tab.shape[0] >= Lt and tab.shape[1] == D // 2
+               and tab.is_contiguous(), "rope_apply: cos/sin must be contiguous f32 [>= L, D/2]")
+    _check(out is None or (out.shape == x.shape and out.dtype == x.dtype), "rope_apply: out must match x")
+    _need_cuda(x, cos, sin)
     if out is None:
         out = torch.empty_like(x)
     L.check(L.lib().wf_rope_apply(x.data_ptr(), out.data_ptr(), cos.data_ptr(), sin.data_ptr(), Lt, H, D,
@@ -195,8 +234,14 @@ def rope_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch
 def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_per_stage: int, eps: float,
                 out: torch.Tensor | None = None) -> torch.Tensor:
     """out = LN(x) * (1 + scale[s]) + shift[s]; x bf16 [rows, dim], shift/scale f32 [S, dim] row-strided."""
-    _need_cuda(x)
+    _check(x.dim() == 2 and x.dtype == torch.bfloat16, "ln_modulate: x must be a bf16 [rows, dim] matrix")
     rows, dim = x.shape
+    for t in (shift, scale):
+        _check(t.dtype == torch.float32 and t.dim() == 2 and t.shape[1] == dim and t.stride(1) == 1
+               and t.shape[0] * rows_per_stage >= rows, "ln_modulate: shift/scale must be f32 [stages, dim]")
+    _check(shift.stride(0) == scale.stride(0), "ln_modulate: shift and scale must share their row stride")
+    _check(out is None or (out.shape == x.shape and out.dtype == torch.bfloat16), "ln_modulate: out must match x")
+    _need_cuda(x)
     if out is None:
         out = torch.empty_like(x, memory_format=torch.contiguous_format)
     L.check(L.lib().wf_ln_modulate(x.data_ptr(), x.stride(0), shift.data_ptr(), scale.data_ptr(), shift.stride(0),
@@ -207,8 +252,13 @@ def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_
 
 def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, rows_per_stage: int) -> torch.Tensor:
     """x += y * gate[s] in place (f32 math, bf16 storage)."""
-    _need_cuda(x, y)
+    _check(x.dim() == 2 and y.shape == x.shape and x.dtype == y.dtype == torch.bfloat16,
+           "gate_residual: x and y must be bf16 matrices of one shape")
     rows, dim = x.shape
+    _check(gate.dtype == torch.float32 and gate.shape[-1] == dim and gate.stride(-1) == 1
+           and (gate.dim() == 1 or (gate.dim() == 2 and gate.shape[0] * rows_per_stage >= rows)),
+           "gate_residual: gate must be f32 [dim] or [stages, dim]")
+    _need_cuda(x, y)
     gs = gate.stride(0) if gate.dim() == 2 else 0
     L.check(L.lib().wf_gate_residual(x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), gate.data_ptr(), gs,
                                      rows, dim, rows_per_stage, _stream()), "wf_gate_residual")
@@ -219,8 +269,15 @@ def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor
                  sin: torch.Tensor, head_dim: int, rows_per_stage: int, eps: float, want_unroped: bool = True):
     """Fused RMSNorm(q), RMSNorm(k) + RoPE from the fused QKV GEMM output.
     Returns (roped q, roped k, normalised un-roped k or None), each [rows, dim]."""
-    _need_cuda(qkv)
+    _check(qkv.dim() == 2 and qkv.dtype == torch.bfloat16 and qkv.shape[1] >= 3 * dim,
+           "qk_norm_rope: qkv must be a bf16 [rows, >= 3*dim] matrix")
     rows = qkv.shape[0]
+    _check(wq.numel() == dim and wk.numel() == dim, "qk_norm_rope: norm weights must have dim elements")
+    for tab in (cos, sin):
+        _check(tab.dtype == torch.float32 and tab.dim() == 2 and tab.shape[0] >= rows
+               and tab.shape[1] == head_dim // 2 and tab.is_contiguous(),
+               "qk_norm_rope: cos/sin must be contiguous f32 [>= rows, head_dim/2]")
+    _need_cuda(qkv)
     q = torch.empty((rows, dim), device=qkv.device, dtype=torch.bfloat16)
     k = torch.empty_like(q)
     ku = torch.empty_like(q) if want_unroped else None
@@ -232,6 +289,8 @@ def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    _check(x.dim() == 2 and x.dtype == torch.bfloat16 and w.numel() == x.shape[1],
+           "rms_norm: x must be bf16 [rows, dim] and w must have dim elements")
     _need_cuda(x)
     rows, dim = x.shape
     out = torch.empty((rows, dim), device=x.device, dtype=torch.bfloat16)
