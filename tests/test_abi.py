@@ -37,3 +37,35 @@ def test_errors_are_reported_without_a_gpu():
     assert rc == 1
     with pytest.raises(RuntimeError):
         L.check(rc, "wf_gemm_w8a8")
+
+
+def test_more_argument_errors_without_a_gpu():
+    """Each entry point rejects malformed arguments on the host, before any
+    launch: unknown segment kinds, misaligned rows, too many destinations,
+    sizes that do not tile."""
+    lib = L.lib()
+    seg = (L.KvSegment * 1)()
+    seg[0] = L.KvSegment(7, 0, 16, None, None, 16, 1, 1536, 1536)  # unknown kind
+    assert lib.wf_kv_assemble(seg, 1, 1536, 128, None) == L.WF_ERR_INVALID_ARG
+    assert "unknown kind" in L.last_error()
+    assert lib.wf_kv_assemble(seg, 99, 1536, 128, None) == L.WF_ERR_INVALID_ARG  # more than 24 segments
+    seg[0] = L.KvSegment(L.WF_SEG_COPY, 0, 16, None, None, 16, 1, 1536, 1536)
+    assert lib.wf_kv_assemble(seg, 1, 1536, 100, None) == L.WF_ERR_INVALID_ARG  # cols not a multiple of head_dim
+    seg[0] = L.KvSegment(L.WF_SEG_ROPE, 0, 16, None, None, 16, 1, 1536, 1536)
+    assert lib.wf_kv_assemble(seg, 1, 1536, 128, None) == L.WF_ERR_INVALID_ARG  # RoPE without tables
+    assert "cos/sin" in L.last_error()
+    seg[0] = L.KvSegment(L.WF_SEG_COPY, 0, 16, None, None, 24, 1, 1536, 1536)
+    assert lib.wf_kv_assemble(seg, 1, 1536, 128, None) == L.WF_ERR_INVALID_ARG  # destination not 16-byte aligned
+    assert lib.wf_kv_assemble(seg, 0, 1536, 128, None) == L.WF_OK  # nothing to do, nothing launched
+
+
+def test_constants_match_the_header():
+    """Every #define WF_* of include/wfk.h has the same value in the ctypes module."""
+    import os
+    import re
+
+    hdr = open(os.path.join(os.path.dirname(__file__), "..", "include", "wfk.h")).read()
+    defs = dict(re.findall(r"^#define (WF_[A-Z0-9_]+) (-?\d+)", hdr, re.M))
+    assert len(defs) >= 16
+    for name, value in defs.items():
+        assert getattr(L, name) == int(value), name

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(_PKG, "libwfk.so")
 HEADER_PATH = os.path.join(os.path.dirname(_PKG), "include", "wfk.h")
 
 WF_OK = 0
+WF_ERR_INVALID_ARG, WF_ERR_UNSUPPORTED, WF_ERR_CUDA, WF_ERR_TIMEOUT = 1, 2, 3, 4
 WF_DTYPE_BF16, WF_DTYPE_E4M3, WF_DTYPE_S8 = 0, 1, 2
 WF_SCALE_NONE, WF_SCALE_TENSOR, WF_SCALE_TOKEN = 0, 1, 2
 WF_ACT_NONE, WF_ACT_GELU_TANH = 0, 1
