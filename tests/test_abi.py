@@ -69,3 +69,30 @@ def test_constants_match_the_header():
     assert len(defs) >= 16
     for name, value in defs.items():
         assert getattr(L, name) == int(value), name
+
+
+@pytest.mark.parametrize("name,args,code", [
+    ("wf_kv_quant", (None, None, None, 4, 16, 16, 2, None, None), 1),
+    ("wf_kv_quant", (16, 16, 16, 4, 12, 16, 2, None, None), 1),                # cols not a multiple of 8
+    ("wf_kv_dequant", (16, None, 16, 4, 16, 16, 2, None), 1),                 # token mode without scales
+    ("wf_kv_quant_tensor_static", (None, None, None, 4, 16, 16, None), 1),
+    ("wf_weight_quant", (None, None, None, 4, 16, 1, None), 1),
+    ("wf_act_quant_act", (16, 16, 16, 4, 16, 16, 1, 9, None), 1),             # unknown activation
+    ("wf_gemm_w8a8_act", (16, 16, 16, 16, None, 16, 4, 16, 16, 16, 1, 2, 9, None), 1),
+    ("wf_gemm_w8a8", (16, 16, 16, 16, None, 16, 4, 16, 16, 16, 7, 2, None), 2),  # unknown qtype
+    ("wf_gemm_w8a8", (16, 16, 16, 16, None, 16, 4, 10, 16, 16, 1, 2, None), 1),  # N not a multiple of 16
+    ("wf_rope_apply", (None, None, None, None, 4, 2, 128, 256, 256, None), 1),
+    ("wf_ln_modulate", (None, 16, None, None, 16, None, 16, 4, 16, 4, 1e-6, None), 1),
+    ("wf_gate_residual", (None, 16, None, 16, None, 16, 4, 16, 4, None), 1),
+    ("wf_rms_norm", (None, 16, None, None, 16, 4, 16, 1e-6, None), 1),
+    ("wf_ipc_close", (None,), 1),
+    ("wf_stream_write_u32", (None, 18, 1), 1),                                # misaligned flag address
+    ("wf_wait_flag", (16, 1, 0, None, None), 1),                              # zero timeout
+    ("wf_memcpy_async", (None, None, 16, None), 1),
+])
+def test_entry_points_reject_bad_arguments(name, args, code):
+    """Malformed calls return the header's error code with a message, and touch
+    no device (these run without a GPU)."""
+    rc = getattr(L.lib(), name)(*args)
+    assert rc == code, (name, rc, L.last_error())
+    assert L.last_error(), name
