@@ -104,6 +104,8 @@ int wf_kv_quant(const void* x, uint8_t* codes, float* scales, int64_t rows, int6
  * (4096 x 8192); larger inputs are rejected with WF_ERR_INVALID_ARG.  The first
  * call on a device resolves the array's device address (cudaGetSymbolAddress
  * with that device current); make that first call before any stream capture.
+ * The address is cached per device and context: the first call in a new
+ * context (after cudaDeviceReset, for example) resolves it again.
  * All calls on a device share the array: calls whose kernels overlap on the
  * GPU race.  Codes and scale are bit-identical to wf_kv_quant's. */
 int wf_kv_quant_tensor_static(const void* x, uint8_t* codes, float* scale, int64_t rows, int64_t cols,

@@ -96,3 +96,27 @@ def test_entry_points_reject_bad_arguments(name, args, code):
     rc = getattr(L.lib(), name)(*args)
     assert rc == code, (name, rc, L.last_error())
     assert L.last_error(), name
+
+
+def test_static_quant_size_limit_is_checked_without_overflow():
+    """wf_kv_quant_tensor_static compares its size limit by division, so sizes
+    whose product wraps a 64-bit integer are still rejected."""
+    lib = L.lib()
+    for rows, cols in [(1 << 61, 8), ((1 << 62) + 8, 1 << 10), (33_554_440 // 8, 8)]:
+        rc = lib.wf_kv_quant_tensor_static(16, 16, 16, rows, cols, cols, None)
+        assert rc == L.WF_ERR_INVALID_ARG, (rows, cols)
+        assert "static scratch limit" in L.last_error()
+
+
+def test_static_quant_accepts_exactly_its_limit():
+    """33,554,432 elements pass the size check.  Without a GPU the call then
+    stops at the device lookup, before any launch; with a GPU present the fake
+    pointers would be launched on, so the case runs on GPU-less hosts only."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("fake device pointers must not reach a launch on a GPU host")
+    lib = L.lib()
+    rc = lib.wf_kv_quant_tensor_static(16, 16, 16, 33_554_432 // 1024, 1024, 1024, None)
+    assert rc == L.WF_ERR_CUDA, L.last_error()
+    assert "static scratch limit" not in L.last_error()

@@ -88,3 +88,31 @@ def test_row_kernel_wrappers():
     _passes(K.rope_apply, page[None], tab[:T], tab[:T])
     _rejects(K.rope_apply, page, tab[:T].double(), tab[:T].double())
     _rejects(K.rope_apply, page, tab[:T - 1], tab[:T - 1])
+
+
+def test_codec_quant_side_buffers():
+    rows, cols = 96, 1536
+    x = torch.zeros(rows, cols, dtype=bf)
+    _passes(K.kv_quant, x, L.WF_SCALE_TOKEN)
+    _passes(K.kv_quant, x, L.WF_SCALE_TOKEN, codes=torch.empty(rows, cols, dtype=torch.uint8),
+            scales=torch.empty(rows))
+    _rejects(K.kv_quant, x, L.WF_SCALE_TOKEN, codes=torch.empty(rows, cols - 8, dtype=torch.uint8))
+    _rejects(K.kv_quant, x, L.WF_SCALE_TOKEN, codes=torch.empty(rows, cols, dtype=bf))
+    _rejects(K.kv_quant, x, L.WF_SCALE_TOKEN, scales=torch.empty(rows - 1))
+    _rejects(K.kv_quant, x, L.WF_SCALE_TOKEN, scales=torch.empty(rows, dtype=bf))
+    _rejects(K.kv_quant, x, L.WF_SCALE_TENSOR, workspace=torch.empty(1, dtype=f32))
+
+
+def test_rope_and_norm_weight_dtypes():
+    x = torch.zeros(10, 2, 128, dtype=bf)
+    tab = torch.zeros(10, 64)
+    _passes(K.rope_apply, x, tab, tab)
+    _rejects(K.rope_apply, x.float(), tab, tab)
+    _rejects(K.rope_apply, x.transpose(1, 2).contiguous().transpose(1, 2), tab, tab)  # heads not contiguous
+    dim = 256
+    _passes(K.rms_norm, torch.zeros(4, dim, dtype=bf), torch.ones(dim, dtype=bf), 1e-6)
+    _rejects(K.rms_norm, torch.zeros(4, dim, dtype=bf), torch.ones(dim), 1e-6)  # f32 weight
+    qkv = torch.zeros(4, 3 * dim, dtype=bf)
+    t = torch.zeros(4, 64)
+    _passes(K.qk_norm_rope, qkv, dim, torch.ones(dim, dtype=bf), torch.ones(dim, dtype=bf), t, t, 128, 4, 1e-6)
+    _rejects(K.qk_norm_rope, qkv, dim, torch.ones(dim), torch.ones(dim, dtype=bf), t, t, 128, 4, 1e-6)

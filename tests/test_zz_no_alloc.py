@@ -55,9 +55,12 @@ def test_static_scratch_rejects_sizes_beyond_its_limit():
     from waveforcing_b200 import _lib as L
 
     lib = L.lib()
-    rows, cols = 4096 * 8192 // 1024 + 8, 1024  # one row more than the 33,554,432-element limit allows
     dummy = torch.empty(16, dtype=torch.bfloat16, device="cuda")
-    rc = lib.wf_kv_quant_tensor_static(dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), rows, cols, cols,
-                                       torch.cuda.current_stream().cuda_stream)
-    assert rc == L.WF_OK + 1  # WF_ERR_INVALID_ARG, rejected before any launch
-    assert "static scratch limit" in L.last_error()
+    # 8 rows (8192 elements) over the 33,554,432-element limit, then a size
+    # whose element count wraps 64 bits (2^61 x 8 = 2^64 -> 0)
+    for rows, cols in [(4096 * 8192 // 1024 + 8, 1024), (1 << 61, 8)]:
+        rc = lib.wf_kv_quant_tensor_static(dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), rows, cols, cols,
+                                           torch.cuda.current_stream().cuda_stream)
+        assert rc == L.WF_ERR_INVALID_ARG, (rows, cols)  # rejected before any launch
+        assert "static scratch limit" in L.last_error()
+    assert L.status_take() == 0

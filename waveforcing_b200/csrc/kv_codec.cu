@@ -496,21 +496,36 @@ __global__ void __launch_bounds__(256) quant_from_partials_kernel(const __nv_bfl
 }
 
 // Device address of g_noalloc_partials per device ordinal, resolved on the
-// first call made with that device current.
+// first call made with that device current.  The cache also records the
+// context the address was resolved in: after cudaDeviceReset (or any other
+// teardown of the primary context) the module is loaded again and the array
+// may move, so a call in a new context resolves the address again.
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_ptr[256] = {};
+static CUcontext g_noalloc_ctx[256] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 
 static int noalloc_scratch(float** out) {
   int dev = 0;
   WFK_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 256) return fail(WF_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  auto get_ctx = reinterpret_cast<CtxGetCurrentFn>(driver_fn("cuCtxGetCurrent"));
+  if (!get_ctx) return fail(WF_ERR_CUDA, "cuCtxGetCurrent unavailable from the driver");
+  // Before the first runtime call that needs it, no context may be current
+  // yet (ctx == nullptr); cudaGetSymbolAddress below makes the primary
+  // context current, and the context is read again afterwards.
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return fail(WF_ERR_CUDA, "cuCtxGetCurrent failed on device %d", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (!ctx || !g_noalloc_ptr[dev] || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (e != cudaSuccess || !p)
       return fail(WF_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
+    if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return fail(WF_ERR_CUDA, "no current context on device %d", dev);
     g_noalloc_ptr[dev] = static_cast<float*>(p);
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return WF_OK;
@@ -523,11 +538,12 @@ extern "C" int wf_kv_quant_tensor_static(const void* x, uint8_t* codes, float* s
                                          int64_t x_row_stride, void* stream) {
   if (!rows_ok(x, rows, cols, x_row_stride) || !codes || !scale || (reinterpret_cast<uintptr_t>(codes) & 7))
     return fail(WF_ERR_INVALID_ARG, "wf_kv_quant_tensor_static: bad arguments (cols %% 8, 16-byte x, 8-byte codes)");
-  if (rows * cols > NOALLOC_MAX_ELEMS)
+  // Compared by division so that no product of two unchecked sizes can wrap.
+  if (cols > NOALLOC_MAX_ELEMS || rows > NOALLOC_MAX_ELEMS / cols)
     return fail(WF_ERR_INVALID_ARG,
-                "wf_kv_quant_tensor_static: %lld elements exceed the static scratch limit of %lld "
+                "wf_kv_quant_tensor_static: %lld x %lld elements exceed the static scratch limit of %lld "
                 "(4096 partial maxima of 8192 elements); use wf_kv_quant with a workspace",
-                (long long)(rows * cols), (long long)NOALLOC_MAX_ELEMS);
+                (long long)rows, (long long)cols, (long long)NOALLOC_MAX_ELEMS);
   if (rows == 0) return WF_OK;
   float* partials = nullptr;
   int rc = noalloc_scratch(&partials);
@@ -536,6 +552,7 @@ extern "C" int wf_kv_quant_tensor_static(const void* x, uint8_t* codes, float* s
   const int nparts = static_cast<int>((rows * cols + NOALLOC_SPAN - 1) / NOALLOC_SPAN);
   amax_partials_kernel<<<nparts, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride,
                                               partials);
+  WFK_CUDA_TRY(cudaGetLastError());  // the quantise pass must not run on partials that were never written
   const int g = grid_for(rows * (cols / 8), 256);
   quant_from_partials_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, x_row_stride,
                                                partials, nparts, codes, scale);

@@ -89,14 +89,24 @@ def _as_rows(x: torch.Tensor):
 def kv_quant(x: torch.Tensor, mode: int = L.WF_SCALE_TOKEN, codes: torch.Tensor | None = None,
              scales: torch.Tensor | None = None, workspace: torch.Tensor | None = None):
     """bf16 [rows, cols] -> (u8 codes [rows, cols], f32 scales [rows] or [1])."""
-    _need_cuda(x)
     if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(-1) != 1:
         raise ValueError("kv_quant: x must be a 2-D bf16 matrix with contiguous rows")
     rows, cols = x.shape
+    n_scales = rows if mode == L.WF_SCALE_TOKEN else 1
+    if codes is not None:
+        _check(codes.dtype == torch.uint8 and codes.is_contiguous() and codes.numel() == rows * cols,
+               "kv_quant: codes must be a contiguous uint8 tensor of rows * cols elements")
+    if scales is not None and mode != L.WF_SCALE_NONE:
+        _check(scales.dtype == torch.float32 and scales.is_contiguous() and scales.numel() >= n_scales,
+               "kv_quant: scales must be contiguous f32 with one element per row (token) or one (tensor)")
+    if workspace is not None:
+        _check(workspace.dtype == torch.int32 and workspace.numel() >= 1,
+               "kv_quant: workspace must be an int32 tensor of at least one element")
+    _need_cuda(x)
     if codes is None:
         codes = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
     if scales is None and mode != L.WF_SCALE_NONE:
-        scales = torch.empty((rows if mode == L.WF_SCALE_TOKEN else 1,), dtype=torch.float32, device=x.device)
+        scales = torch.empty((n_scales,), dtype=torch.float32, device=x.device)
     ws = 0
     if mode == L.WF_SCALE_TENSOR:
         if workspace is None:
@@ -218,10 +228,13 @@ def rope_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch
     if x.dim() == 4:
         x = x[0]
     Lt, H, D = x.shape
+    _check(x.dtype == torch.bfloat16 and x.stride(2) == 1 and x.stride(1) == D,
+           "rope_apply: x must be bf16 [L, H, D] with contiguous heads (token stride is free)")
     for tab in (cos, sin):
         _check(tab.dtype == torch.float32 and tab.dim() == 2 and tab.shape[0] >= Lt and tab.shape[1] == D // 2
                and tab.is_contiguous(), "rope_apply: cos/sin must be contiguous f32 [>= L, D/2]")
-    _check(out is None or (out.shape == x.shape and out.dtype == x.dtype), "rope_apply: out must match x")
+    _check(out is None or (out.shape == x.shape and out.dtype == x.dtype and out.stride(2) == 1
+                           and out.stride(1) == D), "rope_apply: out must match x, with contiguous heads")
     _need_cuda(x, cos, sin)
     if out is None:
         out = torch.empty_like(x)
@@ -272,7 +285,8 @@ def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor
     _check(qkv.dim() == 2 and qkv.dtype == torch.bfloat16 and qkv.shape[1] >= 3 * dim,
            "qk_norm_rope: qkv must be a bf16 [rows, >= 3*dim] matrix")
     rows = qkv.shape[0]
-    _check(wq.numel() == dim and wk.numel() == dim, "qk_norm_rope: norm weights must have dim elements")
+    _check(all(w.numel() == dim and w.dtype == torch.bfloat16 and w.is_contiguous() for w in (wq, wk)),
+           "qk_norm_rope: norm weights must be contiguous bf16 with dim elements")
     for tab in (cos, sin):
         _check(tab.dtype == torch.float32 and tab.dim() == 2 and tab.shape[0] >= rows
                and tab.shape[1] == head_dim // 2 and tab.is_contiguous(),
@@ -289,8 +303,8 @@ def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    _check(x.dim() == 2 and x.dtype == torch.bfloat16 and w.numel() == x.shape[1],
-           "rms_norm: x must be bf16 [rows, dim] and w must have dim elements")
+    _check(x.dim() == 2 and x.dtype == torch.bfloat16 and w.numel() == x.shape[1] and w.dtype == torch.bfloat16
+           and w.is_contiguous(), "rms_norm: x must be bf16 [rows, dim] and w contiguous bf16 with dim elements")
     _need_cuda(x)
     rows, dim = x.shape
     out = torch.empty((rows, dim), device=x.device, dtype=torch.bfloat16)
