@@ -19,7 +19,9 @@ Ticks before the timed window fill the pipeline and are untimed.
 ``e2e``    the same ticks driven from pinned HOST noise: each tick copies its
            noise chunk host->device and reads the finished latent chunk back.
 ``--impl reference``  the reference's torch CPU path (oracle port, all host
-           threads) on a bounded sample of one tick, extrapolated by FLOPs.
+           threads): each step is BASELINE config 1 measured in full (FP8
+           round trip, 12-head SDPA, one linear); `value` is the steady FPS
+           the measured rates give for this tick's work.
 """
 
 from __future__ import annotations
@@ -133,77 +135,210 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU side
-def cpu_reference_sample(preset: str, min_s: float = 10.0):
-    """Time the reference's torch CPU path on a bounded sample of one steady tick
-    and extrapolate by FLOPs.  Sample: stage 0's self-attention for one head
-    (q = one 4680-token chunk, K/V = its 8-chunk context), exactly the call of
-    naive_rt/rolling_forcing/wan/modules/attention.py:76-89, plus the
-    per-token FP8 K/V codec round trip of that head's slots and one FFN
-    linear on 512 rows.  Returns (fps, seconds, sample description, threads)."""
-    from oracle import attention as oattn
-    from waveforcing_b200.wavefront.dit import DiTConfig
-    from waveforcing_b200.wavefront.engine import stage_costs
+def steady_tick_work(cfg, rf_step: int, max_attn_frames: int = 21, npb: int = 3) -> dict:
+    """Algorithmic work of one steady-state tick of the rf_step wavefront + store
+    (every stage active, anchor + 7 clean pages).  Stage s < rf_step attends to
+    naw + 1 + (rf_step - s) chunks (anchor/working, live store slot, its own
+    chunk, the higher stages' in-flight chunks; wave_rt/denoiser/exchange/
+    paged.py:160-189); the store attends to anchor + clean pages + its own
+    chunk.  Linears per stage and layer: q, k, v, o, cross q, cross o on T
+    rows (6 dim^2) and the FFN (2 dim ffn); the cross k/v of the 512 text rows
+    are cached once.  FP8 codec: stages 1..rf_step-1 and the store publish
+    (quantise) one K and one V chunk per layer; stage s receives (dequantises)
+    rf_step - s chunks of K and of V per layer."""
+    T, dim, ffn, Ln = cfg.tokens_per_chunk, cfg.dim, cfg.ffn, cfg.layers
+    wmax = max(0, (max_attn_frames - rf_step * npb - npb) // npb)
+    naw = 1 + wmax
+    ctx = [naw + 1 + (rf_step - s) for s in range(rf_step)]
+    ctx.append(1 + max(0, (max_attn_frames - 2 * npb) // npb) + 1)
+    stages = rf_step + 1
+    return {
+        "ctx_chunks": ctx,
+        "attn_flops": Ln * sum(4.0 * T * c * T * dim for c in ctx),
+        "cross_flops": Ln * stages * 4.0 * T * cfg.text_len * dim,
+        "linear_flops": Ln * stages * 2.0 * T * (6 * dim * dim + 2 * dim * ffn),
+        "quant_elems": Ln * rf_step * 2.0 * T * dim,
+        "dequant_elems": Ln * (rf_step * (rf_step + 1) // 2) * 2.0 * T * dim,
+    }
 
-    cfg = DiTConfig.preset(preset)
-    T, D = cfg.tokens_per_chunk, cfg.head_dim
-    threads = torch.get_num_threads()
-    g = torch.Generator().manual_seed(0)
-    q = torch.randn(1, T, 1, D, generator=g) / math.sqrt(D)
-    k = torch.randn(1, 8 * T, 1, D, generator=g) / math.sqrt(D)
-    v = torch.randn(1, 8 * T, 1, D, generator=g) / math.sqrt(D)
-    x = torch.randn(512, cfg.dim, generator=g).to(torch.bfloat16)
-    w = (torch.randn(cfg.ffn, cfg.dim, generator=g) * 0.02).to(torch.bfloat16)
-    k0, v0 = k, v
-    reps = 0
+
+def _config1_inputs(cfg, seed: int = 0):
+    """q one 3-frame chunk, K/V three chunks (two prior +
+    current), fp32 N(0,1)/sqrt(head_dim) from seed 0."""
+    T, H, D = cfg.tokens_per_chunk, cfg.heads, cfg.head_dim
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, T, H, D, generator=g) / math.sqrt(D)
+    k = torch.randn(1, 3 * T, H, D, generator=g) / math.sqrt(D)
+    v = torch.randn(1, 3 * T, H, D, generator=g) / math.sqrt(D)
+    return q, k, v
+
+
+def cpu_config1_sample(cfg, inputs):
+    """One measured sample of the reference's CPU torch path
+    in full (all heads):
+      * the per-tensor FP8 K/V codec of wave_rt/denoiser/exchange/common.py:
+        143-164 on stack(K, V) in the runtime dtype (quantise, then dequantise);
+      * attention: F.scaled_dot_product_attention in fp32 on the transposed
+        [B, H, L, D] views, as naive_rt/rolling_forcing/wan/modules/
+        attention.py:76-89, on the dequantised K/V;
+      * one T-row linear of the layer (the q projection, dim x dim) in fp32.
+    Returns the wall seconds of each part."""
+    from oracle import attention as oattn
+    from oracle import codec as ocodec
+
+    q, k, v = inputs
+    T, H, D = cfg.tokens_per_chunk, cfg.heads, cfg.head_dim
+    L = k.shape[1]
     t0 = time.perf_counter()
-    while True:
-        # codec round trip on the received K/V rows of this head (torch CPU, the reference's ops)
-        kv = torch.cat([k0, v0], 1).to(torch.bfloat16)
-        s = (kv.abs().amax(dim=-1, keepdim=True) / 448.0).clamp(min=1e-8).float()
-        kvq = (kv / s).to(torch.float8_e4m3fn)
-        kv = (kvq.to(torch.bfloat16) * s).float()
-        k, v = kv[:, :8 * T], kv[:, 8 * T:]
-        oattn.sdpa_reference_torch(q, k, v)
-        torch.nn.functional.linear(x.float(), w.float())
-        reps += 1
-        if time.perf_counter() - t0 >= min_s:
-            break
-    dt = (time.perf_counter() - t0) / reps
-    sample_flops = 4.0 * T * 8 * T * D + 2.0 * 512 * cfg.dim * cfg.ffn
-    # whole tick FLOPs: attention over every stage's context, all heads, all layers; all linears
-    ctx_chunks = [c - 2.9 for c in stage_costs(5)]
-    attn = sum(4.0 * T * c * T * cfg.dim for c in ctx_chunks) + 4.0 * T * 6 * cfg.text_len * cfg.dim
-    lin = 6 * 2.0 * T * (8 * cfg.dim * cfg.dim + 2 * cfg.dim * cfg.ffn)
-    tick_flops = cfg.layers * (attn + lin)
-    tick_s = dt * tick_flops / sample_flops
-    desc = (f"stage-0 self-attention of 1 head (q {T}, K/V {8 * T}) via F.scaled_dot_product_attention fp32 + "
-            f"per-token FP8 K/V round trip + one 512-row FFN linear; {dt:.2f}s per sample (mean of {reps}), x"
-            f"{tick_flops / sample_flops:.0f} by FLOPs to one steady tick")
-    return FRAMES_PER_TICK / tick_s, dt, desc, threads
+    kv = torch.stack([k[0], v[0]]).to(torch.bfloat16).reshape(2 * L, H * D)
+    codes, scale = ocodec.quant_per_tensor_torch(kv)
+    t1 = time.perf_counter()
+    deq = ocodec.dequant_torch(codes, scale, per_token=False)
+    t2 = time.perf_counter()
+    oattn.sdpa_reference_torch(q, deq[:L].reshape(1, L, H, D), deq[L:].reshape(1, L, H, D))
+    t3 = time.perf_counter()
+    w = torch.randn(cfg.dim, cfg.dim) * 0.02
+    t4 = time.perf_counter()
+    torch.nn.functional.linear(q.reshape(T, H * D), w)
+    t5 = time.perf_counter()
+    return {"quant_s": t1 - t0, "dequant_s": t2 - t1, "attn_s": t3 - t2, "linear_s": t5 - t4,
+            "codec_elems": float(2 * L * H * D), "attn_flops": 4.0 * T * L * H * D,
+            "linear_flops": 2.0 * T * cfg.dim * cfg.dim}
+
+
+def cpu_tick_model(cfg, rf_step: int, samples: list) -> dict:
+    """Steady tick on the host's cores from the measured config-1 rates: the
+    tick's attention (self + cross) at the measured SDPA FLOP/s, its linears at
+    the measured linear FLOP/s, its FP8 publishes and receives at the measured
+    quantise and dequantise element rates (medians over the samples)."""
+    med = lambda key: statistics.median(x[key] for x in samples)  # noqa: E731
+    s0 = samples[0]
+    attn_rate = s0["attn_flops"] / med("attn_s")
+    lin_rate = s0["linear_flops"] / med("linear_s")
+    q_rate = s0["codec_elems"] / med("quant_s")
+    d_rate = s0["codec_elems"] / med("dequant_s")
+    w = steady_tick_work(cfg, rf_step)
+    parts = {"attention_s": (w["attn_flops"] + w["cross_flops"]) / attn_rate,
+             "linears_s": w["linear_flops"] / lin_rate,
+             "codec_s": w["quant_elems"] / q_rate + w["dequant_elems"] / d_rate}
+    tick_s = sum(parts.values())
+    return {"tick_s": tick_s, "fps": FRAMES_PER_TICK / tick_s, "parts": parts,
+            "rates": {"sdpa_tflops": attn_rate / 1e12, "linear_tflops": lin_rate / 1e12,
+                      "quant_gelem_s": q_rate / 1e9, "dequant_gelem_s": d_rate / 1e9},
+            "config1_layer_s": med("quant_s") + med("dequant_s") + med("attn_s")}
+
+
+def cpu_baseline(cfg, rf_step: int, min_s: float = 10.0, max_samples: int = 64) -> dict:
+    """The cpu_baseline object of the bench line: config-1 samples on all host
+    threads for about `min_s` seconds, converted to steady FPS by cpu_tick_model."""
+    threads = torch.get_num_threads()
+    inputs = _config1_inputs(cfg)
+    samples = []
+    t0 = time.perf_counter()
+    while not samples or (time.perf_counter() - t0 < min_s and len(samples) < max_samples):
+        samples.append(cpu_config1_sample(cfg, inputs))
+    m = cpu_tick_model(cfg, rf_step, samples)
+    L = 3 * cfg.tokens_per_chunk
+    return {"value": m["fps"], "unit": "FPS", "cores": threads, "nproc": os.cpu_count(), "kind": "port",
+            "sample": (f"BASELINE config 1 measured in full on the host: per-tensor FP8 round trip of stack(K,V) "
+                       f"[2x{L}x{cfg.dim}] (common.py:143-164), fp32 SDPA q {cfg.tokens_per_chunk} x K/V {L} x "
+                       f"{cfg.heads} heads (attention.py:76-89), one {cfg.tokens_per_chunk}x{cfg.dim}x{cfg.dim} "
+                       f"linear; {len(samples)} samples; tick = measured rates x the tick's work "
+                       f"(attention + cross FLOPs, linear FLOPs, codec elements)"),
+            "config1_layer_ms": 1e3 * m["config1_layer_s"], "tick_s_model": m["tick_s"],
+            "tick_parts_s": m["parts"], "rates": m["rates"], "samples": len(samples)}
+
+
+def gpu_config1(cfg, dev, reps: int = 10) -> dict:
+    """The GPU time of the same config-1 call as cpu_config1_sample: libwfk's
+    per-tensor FP8 round trip of stack(K, V) (wf_kv_quant + wf_kv_dequant) and
+    wf_attn_fwd, CUDA-event timed over `reps` calls after warm-up."""
+    from waveforcing_b200 import _lib as L
+    from waveforcing_b200 import kernels
+
+    q, k, v = _config1_inputs(cfg)
+    H, D, Lk = cfg.heads, cfg.head_dim, k.shape[1]
+    qd = q.to(dev).bfloat16()
+    kv = torch.stack([k[0], v[0]]).to(dev).bfloat16().reshape(2 * Lk, H * D)
+    codes = torch.empty(2 * Lk, H * D, device=dev, dtype=torch.uint8)
+    scale = torch.empty(1, device=dev)
+    ws = torch.empty(1, device=dev, dtype=torch.int32)
+    deq = torch.empty(2 * Lk, H * D, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(qd)
+
+    def call():
+        kernels.kv_quant(kv, L.WF_SCALE_TENSOR, codes=codes, scales=scale, workspace=ws)
+        kernels.kv_dequant(codes, scale, L.WF_SCALE_TENSOR, out=deq)
+        d = deq.view(2, 1, Lk, H, D)
+        kernels.attention(qd, d[0], d[1], out=out)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"gpu_ms": ms, "what": "BASELINE config 1 layer: per-tensor FP8 round trip of stack(K,V) + attention, "
+                                  "q 4680 x K/V 14040 x 12 heads (bf16 on the GPU, fp32 on the host)"}
+
+
+def bench_config(args, world: int) -> dict:
+    """The `config` object, identical in both arms for the same flags."""
+    from waveforcing_b200.wavefront.dit import DiTConfig
+    from waveforcing_b200.wavefront.engine import place_stages
+
+    cfg = DiTConfig.preset(args.preset)
+    S = len(args.denoise_steps.split(","))
+    return {"workload": f"{args.preset} {S}-step wavefront + store, steady tick, stages merged onto "
+                        f"{min(world, S + 1)} rank(s)",
+            "model": f"Wan2.1-{args.preset}-shape", "tokens_per_chunk": cfg.tokens_per_chunk,
+            "denoise_steps": args.denoise_steps, "kv_transport": args.kv, "w8a8": args.w8a8, "world": world,
+            "l2": "inputs larger than L2 (K/V slabs and weights, GBs per tick)",
+            "parallelism": f"wavefront stages over {min(world, S + 1)} GPU(s)",
+            "stage_rank": place_stages(S, world)}
 
 
 def run_reference_arm(args):
+    """The reference's CPU torch path on the host's cores (rank 0 only): each
+    step is one measured config-1 sample (cpu_config1_sample), its wall time is
+    ms_per_step, and `value` is the steady FPS that the measured rates give for
+    this config's tick (cpu_tick_model)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    from waveforcing_b200.wavefront.dit import DiTConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     torch.set_num_threads(os.cpu_count() or 1)
+    cfg = DiTConfig.preset(args.preset)
+    S = len(args.denoise_steps.split(","))
+    inputs = _config1_inputs(cfg)
     for _ in range(max(0, args.warmup)):
-        cpu_reference_sample(args.preset, min_s=2.0)
-    vals = []
-    t0 = time.perf_counter()
+        cpu_config1_sample(cfg, inputs)
+    samples, walls = [], []
     for _ in range(max(1, args.steps)):
-        fps, dt, desc, threads = cpu_reference_sample(args.preset)
-        vals.append(fps)
-    wall = time.perf_counter() - t0
-    fps = statistics.median(vals)
+        t0 = time.perf_counter()
+        samples.append(cpu_config1_sample(cfg, inputs))
+        walls.append(time.perf_counter() - t0)
+    m = cpu_tick_model(cfg, S, samples)
+    threads = torch.get_num_threads()
+    desc = (f"each step = BASELINE config 1 in full on the host (per-tensor FP8 K/V round trip, fp32 SDPA "
+            f"{cfg.tokens_per_chunk}x{3 * cfg.tokens_per_chunk}x{cfg.heads} heads, one dim x dim linear); value = "
+            f"steady FPS of the tick at the measured rates (tick {m['tick_s']:.1f} s)")
     line = {
-        "impl": "reference", "metric": METRIC, "value": fps, "unit": "FPS", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * FRAMES_PER_TICK / fps,
+        "impl": "reference", "metric": METRIC, "value": m["fps"], "unit": "FPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(walls),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": f"{args.preset} 5-step wavefront steady tick, CPU torch path",
-                                        "sample_wall_s": wall / max(1, args.steps)},
-        "cpu_baseline": {"value": fps, "unit": "FPS", "cores": threads, "kind": "port", "sample": desc},
-        "e2e": {"value": fps, "unit": "FPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "data": "synthetic (config 1 inputs, seed 0)", "config": bench_config(args, world),
+        "cpu_baseline": {"value": m["fps"], "unit": "FPS", "cores": threads, "nproc": os.cpu_count(), "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": m["fps"], "unit": "FPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "tick_s_model": m["tick_s"], "tick_parts_s": m["parts"], "rates": m["rates"],
+        "config1_layer_ms": 1e3 * m["config1_layer_s"],
     }
     print(json.dumps(line), flush=True)
 
@@ -364,28 +499,30 @@ def run_gpu_arm(args):
             with open(tp) as f:
                 traffic = a_bytes * json.load(f)["ratio_traffic_to_algorithmic"]
         cpu = None
+        config1 = None
         if world == 1:
             torch.set_num_threads(os.cpu_count() or 1)
-            fps_cpu, dt, desc, threads = cpu_reference_sample(args.preset)
-            cpu = {"value": fps_cpu, "unit": "FPS", "cores": threads, "kind": "port", "sample": desc}
+            cpu = cpu_baseline(cfg, S)
+            config1 = gpu_config1(cfg, dev)
+            config1["cpu_ms"] = cpu["config1_layer_ms"]
+            config1["cpu_over_gpu"] = cpu["config1_layer_ms"] / config1["gpu_ms"]
         line = {
             "metric": METRIC, "value": fps, "unit": "FPS", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "tick_ms_p50": p50,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init N(0,0.02) weights, N(0,1) text, seed-0 Gaussian noise)",
-            "config": {"workload": f"{args.preset} {S}-step wavefront + store, steady tick, stages merged onto "
-                                   f"{min(world, S + 1)} rank(s)",
-                       "model": f"Wan2.1-{args.preset}-shape", "tokens_per_chunk": cfg.tokens_per_chunk,
-                       "kv_transport": args.kv, "w8a8": args.w8a8, "world": world,
-                       "l2": "inputs larger than L2 (K/V slabs and weights, GBs per tick)",
-                       "parallelism": f"wavefront stages over {min(world, S + 1)} GPU(s)"},
+            "config": bench_config(args, world),
             "roofline": {"bound": "tensor",
                          "kernel": "attn_fwd_bf16_kernel (wavefront self-attention; the text cross-attention "
                                    "runs on torch SDPA, as in the reference)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+                         "traffic_source": ("not measured in this run: the mean launch's algorithmic bytes x "
+                                            "the DRAM/algorithmic ratio of the committed ncu capture "
+                                            "(profiles/attention_traffic.json)") if traffic is not None else None,
                          "launches": n_attn, "peak_source": f"{src} bf16_tflops_sustained"},
             "cpu_baseline": cpu,
+            "config1": config1,
             "e2e": e2e,
             "dit_fps": dit,
             "exchange": {"critical_rank_wait_ms_per_tick": crit,
@@ -399,9 +536,6 @@ def run_gpu_arm(args):
             "gpu_launches": launches,
             "clocks": clocks,
         }
-        from waveforcing_b200.wavefront.engine import place_stages
-
-        line["config"]["stage_rank"] = place_stages(S, world)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

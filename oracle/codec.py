@@ -128,3 +128,38 @@ def dequant(codes: np.ndarray, scales: np.ndarray, per_token: bool) -> np.ndarra
 def cast_scale_free(x: np.ndarray) -> np.ndarray:
     """onesided.py:152 -- kv.to(e4m3fn) with no scale (bf16 input)."""
     return e4m3_encode(bf16_round(x))
+
+
+# ------------------------------------------------------------------ torch CPU
+# The same dtype sequences written with torch CPU ops, i.e. the reference's
+# own lines (common.py:145-150, :162) run on the host.  numpy's integer and
+# log2 ufuncs are slow on some hosts; these forms quantise the full-size K/V
+# of BASELINE config 1 (43 M elements) in well under a second.  They are
+# pinned to the numpy restatement above by tests/test_oracle_golden.py.
+def quant_per_tensor_torch(x):
+    """x: CPU bf16 tensor -> (uint8 codes, f32 0-dim scale) as common.py:145-150."""
+    import torch
+
+    x = x.to(torch.bfloat16)
+    scale = (x.abs().amax() / E4M3_MAX).clamp(min=SCALE_MIN).to(torch.float32)
+    return (x / scale).to(torch.float8_e4m3fn).view(torch.uint8), scale
+
+
+def quant_per_token_torch(x2):
+    """x2: CPU bf16 [rows, cols] -> (uint8 codes, f32 scales [rows]); the row-wise
+    form of common.py:145-150 (bf16 scale math, bf16 quotient)."""
+    import torch
+
+    x2 = x2.to(torch.bfloat16)
+    scales = (x2.abs().amax(dim=1) / E4M3_MAX).clamp(min=SCALE_MIN).to(torch.float32)
+    q = (x2.float() / scales[:, None]).to(torch.bfloat16)
+    return q.to(torch.float8_e4m3fn).view(torch.uint8), scales
+
+
+def dequant_torch(codes, scales, per_token: bool):
+    """common.py:162 on CPU tensors: f32(bf16(e4m3 value) * scale)."""
+    import torch
+
+    v = codes.view(torch.float8_e4m3fn).to(torch.bfloat16)
+    s = scales.reshape(-1, 1) if per_token else scales.reshape(1)
+    return v * s

@@ -116,3 +116,33 @@ def test_sdpa_numpy_matches_reference_torch_call():
     ref = attention.sdpa_reference_torch(torch.from_numpy(q), torch.from_numpy(k), torch.from_numpy(v)).numpy()
     o = attention.sdpa_numpy(q[0], k[0], v[0])
     assert np.abs(o - ref[0]).max() < 1e-5
+
+
+def test_torch_codec_forms_match_the_numpy_restatement(golden):
+    """The torch-CPU codec forms (used on config 1's full size) give the numpy
+    restatement's codes, scales and dequantised values bit for bit, on the
+    golden inputs and on rows with zeros, tiny and large magnitudes."""
+    g = golden("codec_per_tensor.npz")
+    rng = np.random.default_rng(11)
+    mats = []
+    for i in range(int(g["n"])):
+        x = bits_to_f32(g[f"c{i}_x"])
+        mats.append(x.reshape(-1, x.shape[-2] * x.shape[-1]))
+    m = codec.bf16_round((rng.standard_normal((64, 256)) * np.exp(rng.uniform(-20, 8, (64, 1)))).astype(np.float32))
+    m[3] = 0.0
+    m[5, :7] = 1e-30
+    mats.append(m)
+    for x2 in mats:
+        xt = torch.from_numpy(np.ascontiguousarray(x2)).to(torch.bfloat16)
+        c_ref, s_ref = codec.quant_per_tensor(x2)
+        c, s = codec.quant_per_tensor_torch(xt)
+        assert float(s) == float(s_ref) and np.array_equal(c.numpy(), c_ref)
+        d = codec.dequant_torch(c, s, per_token=False).numpy()
+        assert np.array_equal(np.nan_to_num(d, nan=1e30),
+                              np.nan_to_num(codec.dequant(c_ref, s_ref, per_token=False), nan=1e30))
+        c_ref, s_ref = codec.quant_per_token(x2)
+        c, s = codec.quant_per_token_torch(xt)
+        assert np.array_equal(s.numpy(), s_ref) and np.array_equal(c.numpy(), c_ref)
+        d = codec.dequant_torch(c, s, per_token=True).numpy()
+        assert np.array_equal(np.nan_to_num(d, nan=1e30),
+                              np.nan_to_num(codec.dequant(c_ref, s_ref, per_token=True), nan=1e30))
