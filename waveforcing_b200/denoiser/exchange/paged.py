@@ -21,10 +21,11 @@ What is new relative to the reference:
     GPU is a stream-ordered local write, to another GPU an IPC peer write
     plus a release flag;
   * FP8 e4m3 transport (the reference refuses FP8 with paged, paged.py:36-37):
-    slabs hold per-token codes + f32 scales written by one fused
-    quantise-and-publish kernel; the consumer dequantises the received slots
-    into a bf16 assembly buffer before attention.  Local pages (anchor,
-    working, self) stay bf16, so numerics do not depend on stage placement.
+    slabs hold e4m3 codes + per-row f32 scales, written by one fused
+    quantise-and-publish kernel (per-token scales) or by the per-tensor codec;
+    the consumer dequantises the received slots into a bf16 assembly buffer
+    before attention.  Local pages (anchor, working, self) stay bf16, so
+    numerics do not depend on stage placement.
 """
 
 from __future__ import annotations
@@ -68,7 +69,19 @@ class PagedTransport:
 
     def __init__(self, *, device, rank: int, world: int, stage_rank: list[int], rf_step: int, Ln: int, T: int,
                  H: int, D: int, npb: int = 3, max_attn_frames: int = 21, GT: int = 2, fp8: bool = False,
-                 dtype=torch.bfloat16, timeout_s: float = 30.0, group=None) -> None:
+                 fp8_gran: str = "token", dtype=torch.bfloat16, timeout_s: float = 30.0, group=None,
+                 ipc_open=None) -> None:
+        """``ipc_open`` (optional) opens peer handles on behalf of a host that
+        owns their lifetime -- the reference WaveDenoiser's ``_ipc_open``, which
+        records every mapping for its two-barrier close (engine.py:127-212);
+        the transport then leaves closing them to the host.  ``fp8_gran`` is
+        the FP8 scale granularity: "token" (one scale per token row, fused
+        quantise-and-publish) or "tensor" (the reference's per-tensor scale over
+        stack(K, V), common.py:143-150, written into every row's scale)."""
+        if fp8_gran not in ("token", "tensor"):
+            raise ValueError(f"fp8_gran must be 'token' or 'tensor', got {fp8_gran!r}")
+        self.fp8_gran = fp8_gran
+        self._host_ipc_open = ipc_open
         self.device = torch.device(device)
         self.rank, self.world = rank, world
         self.stage_rank = list(stage_rank)  # stage -> rank, stages 0..rf_step (rf_step = store)
@@ -150,11 +163,14 @@ class PagedTransport:
         if self.world > 1:
             dist.barrier(group=self.group)
 
-    def _open(self, h: bytes) -> int:
+    def _open(self, h) -> int:
         if h not in self._opened:
-            base = ipc.ipc_open_handle(h)
+            if self._host_ipc_open is not None:
+                base = self._host_ipc_open(h)  # the host records and closes it
+            else:
+                base = ipc.ipc_open_handle(h)
+                self._ipc_bases.append(base)
             self._opened[h] = base
-            self._ipc_bases.append(base)
         return self._opened[h]
 
     def close(self, coordinated: bool = True) -> None:
@@ -165,6 +181,11 @@ class PagedTransport:
         if getattr(self, "_closed", False):
             return
         self._closed = True
+        if self._host_ipc_open is not None:
+            # the host closes the mappings it opened (between its own barriers)
+            self._opened.clear()
+            self.dst.clear()
+            return
         if self.copy_stream is not None:
             self.copy_stream.synchronize()
             torch.cuda.synchronize(self.device)
@@ -192,7 +213,7 @@ class PagedTransport:
             return
         T, HD = self.T, self.H * self.D
         src_i = {m: self.src_index_of(m, s) for m, _ in send}
-        cur = torch.cuda.current_stream(self.device)
+        cur_h = self._cur_stream_handle()
         if self.fp8:
             ck, cv, sk, sv = [], [], [], []
             for m, slot in send:
@@ -202,12 +223,15 @@ class PagedTransport:
                 cv.append(d["vc"] + tok * HD)
                 sk.append(d["ks"] + tok * 4)
                 sv.append(d["vs"] + tok * 4)
-            kernels.kv_quant_publish(k.view(T, HD), v.view(T, HD), ck, cv, sk, sv)
+            if self.fp8_gran == "token":
+                kernels.kv_quant_publish(k.reshape(T, HD), v.reshape(T, HD), ck, cv, sk, sv)
+            else:
+                self._publish_tensor_scaled(k, v, ck, cv, sk, sv, cur_h)
             for m, _slot in send:
                 d = self.dst[m]
                 if not d["local"]:
                     fl = d["flags"] + ((src_i[m] * self.GT + gen) * self.Ln + layer) * 4
-                    ipc.stream_write_u32(cur.cuda_stream, fl, tick)
+                    ipc.stream_write_u32(cur_h, fl, tick)
             return
         remote = []
         for m, slot in send:
@@ -220,10 +244,13 @@ class PagedTransport:
                 remote.append((m, slot))
         if not remote:
             return
-        ev = torch.cuda.Event()
-        ev.record(cur)
-        self.copy_stream.wait_event(ev)
-        sh = self.copy_stream.cuda_stream
+        if self.copy_stream is not None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self.copy_stream.wait_event(ev)
+            sh = self.copy_stream.cuda_stream
+        else:
+            sh = 0  # host bookkeeping mode (CPU tensors; the IPC layer is the host's)
         nb = k.numel() * k.element_size()
         for m, slot in remote:
             d = self.dst[m]
@@ -232,9 +259,31 @@ class PagedTransport:
             ipc.memcpy_dtod_async(d["v"] + off, v.data_ptr(), nb, sh)
             fl = d["flags"] + ((src_i[m] * self.GT + gen) * self.Ln + layer) * 4
             ipc.stream_write_u32(sh, fl, tick)
-        k.record_stream(self.copy_stream)
-        v.record_stream(self.copy_stream)
+        if self.copy_stream is not None:
+            k.record_stream(self.copy_stream)
+            v.record_stream(self.copy_stream)
         self._pending += [k, v]
+
+    def _cur_stream_handle(self) -> int:
+        if self.device.type != "cuda":
+            return 0
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _publish_tensor_scaled(self, k, v, ck, cv, sk, sv, stream) -> None:
+        """FP8 publish with the reference's per-tensor scale: one scale over
+        stack(K, V) (common.py:143-150), codes copied to every destination and
+        the scale written into each destination's per-row scales, so consumers
+        dequantise every slot the same way."""
+        T, HD = self.T, self.H * self.D
+        kv = torch.stack([k.reshape(T, HD), v.reshape(T, HD)]).view(2 * T, HD)
+        codes, scale = kernels.kv_quant(kv, L.WF_SCALE_TENSOR)
+        rows = scale.expand(T).contiguous()
+        for a, b, c, d in zip(ck, cv, sk, sv):
+            ipc.memcpy_dtod_async(a, codes.data_ptr(), T * HD, stream)
+            ipc.memcpy_dtod_async(b, codes.data_ptr() + T * HD, T * HD, stream)
+            ipc.memcpy_dtod_async(c, rows.data_ptr(), 4 * T, stream)
+            ipc.memcpy_dtod_async(d, rows.data_ptr(), 4 * T, stream)
+        self._pending += [codes, rows]
 
     def src_index_of(self, m: int, s: int) -> int:
         srcs = list(range(m + 1, self.rf_step)) + [self.store]
@@ -246,12 +295,12 @@ class PagedTransport:
             return  # same GPU: the publish precedes this read on the stream
         i = self.src_index[m][src]
         addr = self.flags[m][i, gen, layer].data_ptr()
-        cur = torch.cuda.current_stream(self.device)
-        sink = self.wait_timer
+        sink = self.wait_timer if self.device.type == "cuda" else None
         if sink is not None:
+            cur = torch.cuda.current_stream(self.device)
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record(cur)
-        ipc.wait_flag_bounded(cur.cuda_stream, addr, tick, self.timeout_s, self.timeout_word.data_ptr())
+        ipc.wait_flag_bounded(self._cur_stream_handle(), addr, tick, self.timeout_s, self.timeout_word.data_ptr())
         if sink is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record(cur)
@@ -259,9 +308,10 @@ class PagedTransport:
 
     def drain(self) -> None:
         """onesided.py:181-187: order later work after this tick's publications."""
-        ev = torch.cuda.Event()
-        ev.record(self.copy_stream)
-        torch.cuda.current_stream(self.device).wait_event(ev)
+        if self.copy_stream is not None:
+            ev = torch.cuda.Event()
+            ev.record(self.copy_stream)
+            torch.cuda.current_stream(self.device).wait_event(ev)
         self._pending = []
 
     def check_timeouts(self) -> None:
@@ -335,11 +385,33 @@ class PagedTransport:
         kernels.kv_assemble(segs, HD, self.D)
         return off
 
-    def make_denoise_exch(self, m: int, clean, act, tick_csf, tick_qf, store_active, tick, rope_fn,
-                          store_slot_sink: dict | None = None, rope_tab_fn=None):
+    @staticmethod
+    def _lp_mark(prof):
+        """A CUDA event for the optional per-layer profile of the host
+        (WaveDenoiser._lp_cur, wave_rt/denoiser/exchange/paged.py:206-254)."""
+        if prof is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
+    def make_denoise_exch(self, m: int, clean, act, tick_csf, tick_qf, store_active, tick, rope_fn=None,
+                          store_slot_sink: dict | None = None, rope_tab_fn=None, prof=None):
+        """The denoise closure of stage ``m`` for one tick (paged.py:156-255).
+
+        ``rope_tab_fn(start_frame, pph, ppw, dim, heads) -> (cos, sin)`` gives
+        the anchor's RoPE tables (f32 [T, head_dim/2]); with it every layer's
+        context is one wf_kv_assemble launch.  Without it, ``rope_fn(ku,
+        start_frame)`` rotates the anchor and the pages are copied one by one.
+        ``store_slot_sink[layer]`` receives a [2, T, H, D] copy of the store's
+        live slot (the reference's ``_exch_store_slot``, promoted to a clean
+        page after the tick).  ``prof()`` returns the host's per-layer profile
+        record (or None)."""
         g = tick_geometry(m, tick, act, store_active, self.rf_step, self.max_attn_frames, self.npb)
         if g["active_slots"] > self.Wmax:
             raise RuntimeError(f"[paged stage {m}] active_slots={g['active_slots']} > Wmax={self.Wmax}")
+        if rope_tab_fn is None and rope_fn is None:
+            raise ValueError("make_denoise_exch needs rope_tab_fn or rope_fn for the anchor re-RoPE")
         T = self.T
         gen = tick % self.GT
         naw, base_infl, act_slots = g["naw"], g["base_infl"], g["active_slots"]
@@ -352,7 +424,10 @@ class PagedTransport:
             Lh = layer_idx
             k = roped_key[0]
             v = value[0]
+            lp = prof() if prof is not None else None
+            e_en = self._lp_mark(lp)
             self.publish(m, k, v, send, Lh, gen, tick)
+            e_pub = self._lp_mark(lp)
             if self.fp8:
                 Kb, Vb = sl["kb"], sl["vb"]
             else:
@@ -363,6 +438,7 @@ class PagedTransport:
                     raise RuntimeError(f"[paged stage {m}] anchor+working != naw={naw} (t={tick})")
                 for src in recv:
                     self.wait(m, src, Lh, gen, tick)
+                e_wt = self._lp_mark(lp)
                 deq = []
                 if self.fp8:
                     for a, b in ((naw, base_infl), (base_infl + 1, act_slots)):
@@ -370,39 +446,49 @@ class PagedTransport:
                             rows = slice(a * T, b * T)
                             deq.append((rows, sl["kc"][gen, Lh, rows], sl["ks"][gen, Lh, rows],
                                         sl["vc"][gen, Lh, rows], sl["vs"][gen, Lh, rows]))
-                self.assemble(Kb, Vb, parts, rope_tab_fn, (k, v), self_off, deq)
-                if store_active and store_slot_sink is not None:
-                    store_slot_sink[Lh] = (Kb[live_off:live_off + T].clone(), Vb[live_off:live_off + T].clone())
-                return Kb[:active_len].unsqueeze(0), Vb[:active_len].unsqueeze(0)
-            aK, aV = self.anchor_working(clean[Lh], tick_csf, tick_qf, rope_fn)
-            if len(aK) != naw:
-                raise RuntimeError(f"[paged stage {m}] anchor+working={len(aK)} != naw={naw} (t={tick})")
-            off = 0
-            for ak, av in zip(aK, aV):
-                Kb[off:off + T].copy_(ak)
-                Vb[off:off + T].copy_(av)
-                off += T
-            Kb[self_off:self_off + T].copy_(k)
-            Vb[self_off:self_off + T].copy_(v)
-            for src in recv:
-                self.wait(m, src, Lh, gen, tick)
-            if self.fp8:
-                HD = self.H * self.D
-                for a, b in ((naw, base_infl), (base_infl + 1, act_slots)):
-                    if b <= a:
-                        continue
-                    rows = slice(a * T, b * T)
-                    kernels.kv_dequant(sl["kc"][gen, Lh, rows], sl["ks"][gen, Lh, rows], L.WF_SCALE_TOKEN,
-                                       out=Kb[rows].view(-1, HD))
-                    kernels.kv_dequant(sl["vc"][gen, Lh, rows], sl["vs"][gen, Lh, rows], L.WF_SCALE_TOKEN,
-                                       out=Vb[rows].view(-1, HD))
+                tabs = (lambda start: rope_tab_fn(start, post_patch_height, post_patch_width, dim,
+                                                  rope_num_heads))
+                self.assemble(Kb, Vb, parts, tabs, (k, v), self_off, deq)
+            else:
+                aK, aV = self.anchor_working(clean[Lh], tick_csf, tick_qf, rope_fn)
+                if len(aK) != naw:
+                    raise RuntimeError(f"[paged stage {m}] anchor+working={len(aK)} != naw={naw} (t={tick})")
+                off = 0
+                for ak, av in zip(aK, aV):
+                    Kb[off:off + T].copy_(ak.reshape(T, self.H, self.D))
+                    Vb[off:off + T].copy_(av.reshape(T, self.H, self.D))
+                    off += T
+                Kb[self_off:self_off + T].copy_(k)
+                Vb[self_off:self_off + T].copy_(v)
+                for src in recv:
+                    self.wait(m, src, Lh, gen, tick)
+                e_wt = self._lp_mark(lp)
+                if self.fp8:
+                    HD = self.H * self.D
+                    for a, b in ((naw, base_infl), (base_infl + 1, act_slots)):
+                        if b <= a:
+                            continue
+                        rows = slice(a * T, b * T)
+                        kernels.kv_dequant(sl["kc"][gen, Lh, rows], sl["ks"][gen, Lh, rows], L.WF_SCALE_TOKEN,
+                                           out=Kb[rows].view(-1, HD))
+                        kernels.kv_dequant(sl["vc"][gen, Lh, rows], sl["vs"][gen, Lh, rows], L.WF_SCALE_TOKEN,
+                                           out=Vb[rows].view(-1, HD))
             if store_active and store_slot_sink is not None:
-                store_slot_sink[Lh] = (Kb[live_off:live_off + T].clone(), Vb[live_off:live_off + T].clone())
+                # torch.stack copies: the live slot outlives this layer's buffers
+                store_slot_sink[Lh] = torch.stack([Kb[live_off:live_off + T], Vb[live_off:live_off + T]])
+            if lp is not None:
+                lp["layers"].append(dict(layer=Lh, enter=e_en, pub=e_pub, wait=e_wt, cat=self._lp_mark(lp)))
             return Kb[:active_len].unsqueeze(0), Vb[:active_len].unsqueeze(0)
 
         return exch
 
-    def make_store_exch(self, clean, store_kv: list, chunk: int, act, tick, rope_fn, rope_tab_fn=None):
+    def make_store_exch(self, clean, store_kv: list, chunk: int, act, tick, rope_fn=None, rope_tab_fn=None,
+                        prof=None):
+        """The store closure for one tick (paged.py:257-310).  ``store_kv[layer]``
+        receives (roped_key, unroped_key, value) as passed, [1, T, H, D] each,
+        as the reference keeps them for promotion (engine.py:449-515)."""
+        if rope_tab_fn is None and rope_fn is None:
+            raise ValueError("make_store_exch needs rope_tab_fn or rope_fn for the anchor re-RoPE")
         clean_len = min(8, max(0, tick - self.store))
         wmax_chunks = max(0, (self.max_attn_frames - len(act) * self.npb - self.npb) // self.npb)
         naw = 0 if clean_len == 0 else 1 + min(wmax_chunks, clean_len - 1)
@@ -415,39 +501,111 @@ class PagedTransport:
                  post_patch_height, post_patch_width, dim, rope_num_heads, num_frames_per_block):
             k = roped_key[0]
             v = value[0]
+            lp = prof() if prof is not None else None
+            e_en = self._lp_mark(lp)
             self.publish(self.store, k, v, send, layer_idx, gen, tick)
+            e_pub = self._lp_mark(lp)
             if rope_tab_fn is not None and self.fused_assembly:
                 parts = self.anchor_working_parts(clean[layer_idx], chunk * self.npb, self.npb)
                 n_aw = 0 if parts is None else 1 + len(parts[1])
-                self.assemble(Kbuf, Vbuf, parts, rope_tab_fn, (k, v), n_aw * T)
-                store_kv[layer_idx] = (k.clone(), unroped_key[0].clone(), v.clone())
-                return Kbuf[:(n_aw + 1) * T].unsqueeze(0), Vbuf[:(n_aw + 1) * T].unsqueeze(0)
-            aK, aV = self.anchor_working(clean[layer_idx], chunk * self.npb, self.npb, rope_fn)
-            off = 0
-            for ak, av in zip(aK, aV):
-                Kbuf[off:off + T].copy_(ak)
-                Vbuf[off:off + T].copy_(av)
-                off += T
-            Kbuf[off:off + T].copy_(k)
-            Vbuf[off:off + T].copy_(v)
-            store_kv[layer_idx] = (k.clone(), unroped_key[0].clone(), v.clone())
+                tabs = (lambda start: rope_tab_fn(start, post_patch_height, post_patch_width, dim,
+                                                  rope_num_heads))
+                self.assemble(Kbuf, Vbuf, parts, tabs, (k, v), n_aw * T)
+                off = n_aw * T
+            else:
+                aK, aV = self.anchor_working(clean[layer_idx], chunk * self.npb, self.npb, rope_fn)
+                off = 0
+                for ak, av in zip(aK, aV):
+                    Kbuf[off:off + T].copy_(ak.reshape(T, self.H, self.D))
+                    Vbuf[off:off + T].copy_(av.reshape(T, self.H, self.D))
+                    off += T
+                Kbuf[off:off + T].copy_(k)
+                Vbuf[off:off + T].copy_(v)
+            store_kv[layer_idx] = (roped_key, unroped_key, value)
+            if lp is not None:
+                lp["layers"].append(dict(layer=layer_idx, enter=e_en, pub=e_pub, wait=e_pub,
+                                         cat=self._lp_mark(lp)))
             return Kbuf[:off + T].unsqueeze(0), Vbuf[:off + T].unsqueeze(0)
 
         return exch
 
 
+def _env_flag(name: str) -> bool:
+    import os
+
+    return os.environ.get(name, "").strip().lower() not in ("", "0", "false", "no", "off")
+
+
 class PagedExchangeMixin:
-    """Reference-named entry points (wave_rt/denoiser/exchange/paged.py) over
-    ``PagedTransport`` for a WaveDenoiser whose rank hosts one stage."""
+    """The reference's paged-mode entry points (wave_rt/denoiser/exchange/
+    paged.py) over ``PagedTransport``, for the reference's WaveDenoiser, one
+    stage per rank (wave_rt/config.py:79-83).  Placed ahead of the reference
+    mixins in WaveDenoiser's bases, it needs nothing from its host beyond what
+    the reference's classes already provide:
+
+      * ``_init_paged`` is called by ``_init_transport_state`` (engine.py:
+        147-148) after ``_ipc_handles`` exists.  It sets what the reference's
+        ``_init_onesided`` sets for the paged mode and what ``close()`` reads:
+        ``_p2p`` (the IPC module, whose ``ipc_close_handle`` the close uses),
+        ``_os_scopy`` (the copy stream, synchronised by the close), ``_os_gt``,
+        ``_os_src_index``, ``_os_in_srcs`` and ``_pg_naw`` / ``_pg_wmax`` /
+        ``_pg_dst`` / ``_pg_k`` / ``_pg_v``.  Every peer mapping is opened
+        through the host's ``_ipc_open``, so the host's close (engine.py:
+        156-212) closes them in reverse order between its two barriers.
+      * the anchor re-RoPE tables come from the host's ``_anchor_rope``
+        (common.py:45-68); the rotation runs inside the one-launch context
+        assembly;
+      * FP8 transport is switched by the reference's own flag,
+        ``WAVE_FP8KV_ONESIDED`` (settings.py:21), which the reference's paged
+        mode refuses (paged.py:36-37); ``WAVE_FP8KV_GRAN`` = ``token``
+        (default) or ``tensor`` picks the scale granularity;
+      * the closures store ``store_kv[L] = (roped_key, unroped_key, value)``
+        and ``_exch_store_slot[L]`` as a [2, T, H, D] tensor, the shapes the
+        host's promotion reads (engine.py:449-515), and fill ``_lp_cur``.
+    """
 
     def _init_paged(self) -> None:
+        self._p2p = ipc
+        fp8 = _env_flag("WAVE_FP8KV_ONESIDED")
+        gran = __import__("os").environ.get("WAVE_FP8KV_GRAN", "token").strip() or "token"
+        self._os_fp8 = False  # the reference's onesided FP8 cast is not used by this transport
+        self._paged_fp8 = fp8
         self._pg = PagedTransport(device=self.device, rank=self.rank, world=self.world,
                                   stage_rank=list(range(self.rf_step + 1)), rf_step=self.rf_step, Ln=self.Ln,
                                   T=self.tokens_per_chunk, H=self._kv_shape[2], D=self._kv_shape[3], npb=self.npb,
-                                  max_attn_frames=self.max_attn_frames,
-                                  fp8=bool(getattr(self, "_paged_fp8", False)))
-        self._pg_naw, self._pg_wmax = self._pg.naw_max, self._pg.Wmax
-        self._os_gt = self._pg.GT
+                                  max_attn_frames=self.max_attn_frames, fp8=fp8, fp8_gran=gran, dtype=self.dtype,
+                                  ipc_open=self._ipc_open)
+        pg = self._pg
+        self._pg_naw, self._pg_wmax = pg.naw_max, pg.Wmax
+        self._os_gt = pg.GT
+        self._os_scopy = pg.copy_stream
+        self._os_src_index = dict(pg.src_index.get(self.rank, {}))
+        self._os_in_srcs = sorted(self._os_src_index, key=self._os_src_index.get)
+        self._pg_dst = {m: d for m, d in pg.dst.items() if m != self.rank}
+        sl = pg.slabs.get(self.rank)
+        if sl is not None:
+            self._pg_k = sl.get("k", sl.get("kc"))
+            self._pg_v = sl.get("v", sl.get("vc"))
+
+    def _wf_rope_tables(self, start_frame, pph, ppw, dim, heads):
+        """The host's anchor RoPE tables (common.py:45-68) as f32 [T, head_dim/2]
+        interleaved-pair tables, the form wf_kv_assemble reads.  A table of
+        head_dim columns (each angle repeated for its pair) is reduced to one
+        column per pair."""
+        cos, sin = self._anchor_rope(self.npb, pph, ppw, start_frame, dim, heads, self.device)
+        hd = dim // heads
+        T = self.tokens_per_chunk
+        out = []
+        for t in (cos, sin):
+            t = t.reshape(T, -1)
+            if t.shape[1] == hd:
+                if not torch.equal(t[:, 0::2], t[:, 1::2]):
+                    raise ValueError("anchor RoPE table: head_dim columns that are not pair-repeated")
+                t = t[:, 0::2]
+            if t.shape[1] != hd // 2:
+                raise ValueError(f"anchor RoPE table has {t.shape[1]} columns; expected {hd // 2}")
+            out.append(t.float().contiguous())
+        return out[0], out[1]
 
     def _publish_paged(self, k, v, dst_slots, layer: int, gen: int, tick: int) -> None:
         self._pg.publish(self.rank, k, v, dst_slots, layer, gen, tick)
@@ -457,10 +615,12 @@ class PagedExchangeMixin:
 
     def _make_denoise_exch_paged(self, clean, act_ranks, tick_csf, tick_qf, store_active):
         return self._pg.make_denoise_exch(self.rank, clean, act_ranks, tick_csf, tick_qf, store_active,
-                                          self._cur_tick, self._wf_rope_fn, self._exch_store_slot)
+                                          self._cur_tick, store_slot_sink=self._exch_store_slot,
+                                          rope_tab_fn=self._wf_rope_tables, prof=lambda: self._lp_cur)
 
     def _make_store_exch_paged(self, clean, store_kv, c, act_ranks):
-        return self._pg.make_store_exch(clean, store_kv, c, act_ranks, self._cur_tick, self._wf_rope_fn)
+        return self._pg.make_store_exch(clean, store_kv, c, act_ranks, self._cur_tick,
+                                        rope_tab_fn=self._wf_rope_tables, prof=lambda: self._lp_cur)
 
     def _drain_publish(self) -> None:
         self._pg.drain()

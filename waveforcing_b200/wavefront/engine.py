@@ -88,6 +88,23 @@ def place_stages(rf_step: int, world: int) -> list[int]:
     return out
 
 
+class _StoreKV(list):
+    """``store_kv`` of one tick for merged stages.  The store closure assigns
+    ``(roped_key, unroped_key, value)`` per layer, [1, T, H, D] views that the
+    reference keeps as they are (engine.py:449-515).  Here those views point
+    into per-layer buffers of every merged stage, so each assignment keeps a
+    copy of only the two tensors the promotion reads: the unroped key and the
+    value at the anchor tick (cid 0), the roped key and the value otherwise."""
+
+    def __init__(self, n: int, anchor: bool) -> None:
+        super().__init__([None] * n)
+        self.anchor = anchor
+
+    def __setitem__(self, i, kv) -> None:
+        kr, ku, v = kv
+        super().__setitem__(i, (None if self.anchor else kr.clone(), ku.clone() if self.anchor else None, v.clone()))
+
+
 @dataclass
 class TickStats:
     tick_ms: list = field(default_factory=list)
@@ -141,6 +158,11 @@ class WavefrontEngine:
             self._rope_cache[start_frame] = tab
         return tab
 
+    def _rope_tab(self, start_frame: int, *_geometry) -> tuple[torch.Tensor, torch.Tensor]:
+        """Anchor RoPE tables for the exchange closures (the chunk geometry the
+        closures also pass is fixed by the model config here)."""
+        return self._rope_tables(start_frame)
+
     def _rope(self, ku: torch.Tensor, start_frame: int) -> torch.Tensor:
         tab = self._rope_tables(start_frame)
         return kernels.rope_apply(ku, tab[0], tab[1])
@@ -169,19 +191,19 @@ class WavefrontEngine:
         if 0 in self.local and self.act_denoise(0, t):
             self.inputs[0] = self.noise_chunk(t)
         tasks = []
-        store_kv = [None] * self.Ln
+        store_kv = _StoreKV(self.Ln, anchor=(t - self.store == 0))
         store_slot: dict = {}
         for s in sorted(self.local, reverse=True):
             if s < S and self.act_denoise(s, t):
                 c = t - s
                 exch = self.xport.make_denoise_exch(s, self.clean, act, tick_csf, tick_qf, store_active, t,
                                                     self._rope, store_slot if not store_slot else None,
-                                                    rope_tab_fn=self._rope_tables)
+                                                    rope_tab_fn=self._rope_tab)
                 tasks.append(StageTask(self.inputs[s], self.fm.timestep(cfg.steps[s]), c * cfg.npb, s, exch))
             elif s == self.store and store_active:
                 c = t - self.store
                 exch = self.xport.make_store_exch(self.clean, store_kv, c, act, t, self._rope,
-                                                  rope_tab_fn=self._rope_tables)
+                                                  rope_tab_fn=self._rope_tab)
                 tasks.append(StageTask(self.inputs[s], cfg.context_noise, c * cfg.npb, s, exch))
         flows = self.m.forward_stages(tasks) if tasks else []
         self.xport.drain()
@@ -202,18 +224,20 @@ class WavefrontEngine:
         cid = t - self.store
         Ln = self.Ln
         hosts_store = self.store in self.local
+        # store_kv[L] = (roped_key, unroped_key, value) as [1, T, H, D] (copies,
+        # see _StoreKV); store_slot[L] = [2, T, H, D] copy of the live slot
         if cid == 0:
             # anchor: the store's unroped key and value for every layer (engine.py:449-488)
             if hosts_store:
-                blob = torch.stack([torch.stack([store_kv[L][1] for L in range(Ln)]),
-                                    torch.stack([store_kv[L][2] for L in range(Ln)])]).contiguous()
+                blob = torch.stack([torch.stack([store_kv[L][1][0] for L in range(Ln)]),
+                                    torch.stack([store_kv[L][2][0] for L in range(Ln)])]).contiguous()
             else:
                 blob = torch.empty((2, Ln, self.T, self.H, self.D), device=self.device, dtype=torch.bfloat16)
             if self.world > 1:
                 dist.broadcast(blob, src=self.stage_rank[self.store], group=self.group)
             self._append_clean([dict(ku=blob[0, L], v=blob[1, L], cid=cid) for L in range(Ln)])
         elif hosts_store:
-            self._append_clean([dict(kr=store_kv[L][0], v=store_kv[L][2], cid=cid) for L in range(Ln)])
+            self._append_clean([dict(kr=store_kv[L][0][0], v=store_kv[L][2][0], cid=cid) for L in range(Ln)])
         elif len(store_slot) == Ln:
             self._append_clean([dict(kr=store_slot[L][0], v=store_slot[L][1], cid=cid) for L in range(Ln)])
 
