@@ -190,3 +190,35 @@ def make_config(engine_mod, *, rf_step: int, steps, num_frames: int, exchange_mo
 
     return WaveConfig(rf_step=rf_step, wp_size=rf_step + 1, denoising_step_list=tuple(steps), num_frames=num_frames,
                       exchange_mode=exchange_mode, kv_context="causal")
+
+
+# ------------------------------------------------------------ Wan DiT model
+def wan_forward(model, *, fused: bool):
+    """``model(latent_bcthw, step, start_frame, exch) -> x0_btchw`` over this
+    repository's Wan-shaped DiT (waveforcing_b200/wavefront/dit.py, random
+    weights).  ``step`` is the warped timestep the engine passes (its dsl,
+    backend.py:460-463); x0 = x_t - (step / 1000) * flow, the flow-matching
+    inversion of naive_rt/rolling_forcing/utils/wan_wrapper.py:169-193.
+
+    fused=False is the reference's GPU path restated in plain torch: q, k and
+    v as three linears, the RoPE stand-in above applied as patched_forward
+    does (``apply_rope(q, cos, sin).type_as(v)``, backend.py:119-121), torch
+    ops for norms and modulation, and whatever attention backend is selected
+    (torch SDPA for the reference).  fused=True is this repository's path
+    (libwfk row kernels, fused QKV, the selected backend)."""
+    from waveforcing_b200.wavefront.dit import StageTask
+
+    def torch_rope(x, cos, sin):
+        return apply_rotary_interleaved(x, cos, sin).to(x.dtype)
+
+    def forward(lat_bcthw, step, start_frame, exch):
+        xt = lat_bcthw[0]
+        task = StageTask(xt, float(step), int(start_frame), 0, exch)
+        if fused:
+            flow = model.forward_stages([task])[0]
+        else:
+            flow = model.forward_stages([task], fused=False, rope_fn=torch_rope, separate_qkv=True)[0]
+        x0 = (xt.double() - (float(step) / 1000.0) * flow.double()).to(xt.dtype)  # [C, F, H, W]
+        return x0.permute(1, 0, 2, 3).unsqueeze(0).contiguous()
+
+    return forward

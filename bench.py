@@ -51,7 +51,10 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="wf", choices=["wf", "reference"])
+    ap.add_argument("--impl", default="wf", choices=["wf", "reference", "reference-gpu"],
+                    help="reference: the reference's CPU torch path on the host cores (the driver's reference "
+                         "arm); reference-gpu: the reference's own wavefront engine and paged exchange on GPUs "
+                         "(one rank per stage, torch SDPA, bf16 K/V), for the comparison on the same box")
     ap.add_argument("--preset", default="1.3b")
     ap.add_argument("--kv", default="fp8", choices=["fp8", "bf16"])
     ap.add_argument("--w8a8", default="none", choices=["none", "e4m3", "int8"])
@@ -341,6 +344,98 @@ def run_reference_arm(args):
         "config1_layer_ms": 1e3 * m["config1_layer_s"],
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------- reference on GPUs
+def run_reference_gpu_arm(args):
+    """The reference's own GPU path on this box: wave_rt's WaveDenoiser
+    (wave_rt/denoiser/engine.py) in ``paged`` mode with the reference's own
+    PagedExchangeMixin and CUDA-IPC layer (wave_rt/distributed/ipc.py), bf16
+    K/V, torch SDPA attention, over the Wan-shaped DiT in plain torch ops
+    (baseline/harness.py: SGLang's backend and RoPE helpers stood in).  The
+    reference needs one rank per stage, rf_step + 1 (wave_rt/config.py:79-83),
+    so it runs only at that world size.  Metric as the reference reports it:
+    steady FPS = 12000 / p50(per-tick ms [12:-4]) from the engine's own tick
+    timer (max over ranks per tick), DiT FPS = 1596 / diffusion seconds
+    (scripts/sweep_matrix.py:34-35,137-138,213-228; wave_rt/bench.py:81)."""
+    import datetime
+
+    steps_list = tuple(int(x) for x in args.denoise_steps.split(","))
+    S = len(steps_list)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != S + 1:
+        if rank == 0:
+            print(json.dumps({"impl": "reference-gpu", "unavailable":
+                              f"the reference runs one rank per stage: world {S + 1} for {S} steps, got {world}"}))
+        return
+    from baseline import harness
+
+    if harness.reference_checkout() is None:
+        if rank == 0:
+            print(json.dumps({"impl": "reference-gpu", "unavailable": "no reference package in baseline/_ref "
+                                                                      "(python baseline/install_ref.py <checkout>)"}))
+        return
+    from waveforcing_b200.runtime import backend
+    from waveforcing_b200.wavefront.dit import DiTConfig, FlowMatch, WanDiT
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=180))
+    torch.set_grad_enabled(False)
+    engine = harness.import_reference()
+    backend.select_backend("torch_sdpa")
+    cfg = DiTConfig.preset(args.preset)
+    model = WanDiT.random(cfg, dev, seed=0)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    model.set_text(torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(dev))
+    fm = FlowMatch()
+    dsl = [fm.timestep(x) for x in steps_list]
+    gn = torch.Generator(device="cpu").manual_seed(0)
+    nf = 399
+    noise = torch.randn((cfg.in_ch, nf, cfg.lat_h, cfg.lat_w), generator=gn).to(torch.bfloat16)
+    be = harness.StubBackend(rank=rank, device=dev, dtype=torch.bfloat16, num_layers=cfg.layers, heads=cfg.heads,
+                             head_dim=cfg.head_dim, channels=cfg.in_ch, lat_h=cfg.lat_h, lat_w=cfg.lat_w,
+                             tokens_per_frame=cfg.tokens_per_frame, steps=dsl, full_noise=noise[None].to(dev),
+                             model=harness.wan_forward(model, fused=False))
+    wcfg = harness.make_config(engine, rf_step=S, steps=dsl, num_frames=nf, exchange_mode="paged")
+    den = engine.WaveDenoiser(be, wcfg)
+    den._warmup(n_iters=max(1, min(3, args.warmup)))
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    t0 = time.perf_counter()
+    final, tick_ms, _ = den._systolic(be.full_noise_bcthw, warmup_pass=False, num_ticks=den.num_ticks)
+    torch.cuda.synchronize()
+    dist.barrier()
+    wall = time.perf_counter() - t0
+    clocks = sampler.stop() if sampler else None
+    t = torch.tensor(tick_ms, device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    tick_ms = t.tolist()
+    wt = torch.tensor([wall], device=dev, dtype=torch.float64)
+    dist.all_reduce(wt, op=dist.ReduceOp.MAX)
+    wall = wt.item()
+    den.close()
+    if rank == 0:
+        steady = tick_ms[12:-4]
+        p50 = statistics.median(steady)
+        print(json.dumps({
+            "impl": "reference-gpu", "metric": METRIC, "value": FRAMES_PER_TICK * 1000.0 / p50, "unit": "FPS",
+            "n_gpus": world, "tick_ms_p50": p50, "higher_is_better": True,
+            "dit_fps": {"value": 4 * nf / wall, "unit": "FPS", "diffusion_s": wall},
+            "ticks": len(tick_ms), "steady_ticks": len(steady), "dtype": "bf16", "data": "synthetic",
+            "config": dict(bench_config(args, world), kv_transport="bf16", attention="torch SDPA",
+                           engine="reference wave_rt WaveDenoiser + PagedExchangeMixin (CUDA IPC)"),
+            "timing": "the engine's own per-tick host timer (no per-tick sync), max over ranks; "
+                      "DiT FPS from the barrier-bracketed wall time of all ticks",
+            "clocks": clocks}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------- GPU side
@@ -867,6 +962,8 @@ def main():
         run_kernel_bench(args)
     elif args.impl == "reference":
         run_reference_arm(args)
+    elif args.impl == "reference-gpu":
+        run_reference_gpu_arm(args)
     else:
         run_gpu_arm(args)
 

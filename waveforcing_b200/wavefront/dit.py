@@ -278,11 +278,16 @@ class WanDiT(nn.Module):
             cache[(start_frame, dev)] = tab
         return tab
 
-    def forward_stages(self, tasks: list[StageTask], layer_hook=None, fused: bool = True) -> list[torch.Tensor]:
+    def forward_stages(self, tasks: list[StageTask], layer_hook=None, fused: bool = True, rope_fn=None,
+                       separate_qkv: bool = False) -> list[torch.Tensor]:
         """Run every task's 30/40-layer forward, layer-interleaved.  Returns the
         flow prediction of each task as [C, F, H, W] (f32).  ``fused`` selects
         the libwfk row kernels for norms/modulation/residuals/RoPE; False runs
-        the same math as plain torch ops (used by the tests as a cross-check)."""
+        the same math as plain torch ops (used by the tests as a cross-check).
+        With ``fused=False``, ``rope_fn(x [T, H, D], cos, sin) -> bf16`` replaces
+        libwfk's RoPE and ``separate_qkv`` runs q, k and v as three linears, as
+        the reference's SGLang block does; with the attention backend on
+        torch_sdpa that is a forward without any libwfk call."""
         cfg = self.cfg
         dev = self.patch_embedding.weight.device
         dt = self.patch_embedding.weight.dtype
@@ -322,7 +327,7 @@ class WanDiT(nn.Module):
         for li, b in enumerate(self.blocks):
             e_all = (b.modulation.float() + mods).contiguous()  # [S, 6, dim]
             h = ln_mod(xs, e_all, 0)
-            fq = self._fused_qkv(b)
+            fq = None if (separate_qkv and not fused) else self._fused_qkv(b)
             if fused and fq is not None:
                 qkv = self._qkv_gemm(fq, h)
                 rq_all, rk_all, ku_all = kernels.qk_norm_rope(qkv, dim, b.self_attn.norm_q.weight,
@@ -338,8 +343,9 @@ class WanDiT(nn.Module):
                 q = b.self_attn.norm_q(q).view(S, T, H, D)
                 ku_all = b.self_attn.norm_k(k).view(S, T, H, D)
                 v = v.reshape(S, T, H, D)
-                rq_all = torch.stack([kernels.rope_apply(q[i], *ropes[i]) for i in range(S)])
-                rk_all = torch.stack([kernels.rope_apply(ku_all[i], *ropes[i]) for i in range(S)])
+                rope = rope_fn if rope_fn is not None else kernels.rope_apply
+                rq_all = torch.stack([rope(q[i], *ropes[i]) for i in range(S)])
+                rk_all = torch.stack([rope(ku_all[i], *ropes[i]) for i in range(S)])
             o = torch.empty((S, T, H, D), device=dev, dtype=dt)
             for i in order:
                 tk = tasks[i]
