@@ -231,6 +231,30 @@ int wf_qk_norm_rope(const void* qkv, int64_t ld, const void* wq, const void* wk,
                     const float* sin_t, int head_dim, void* q_out, void* k_out, void* k_unroped, int64_t rows,
                     int64_t dim, int64_t rows_per_stage, float eps, void* stream);
 
+/* One destination slot of a fused FP8 K/V publish: codes [T, dim] u8 (8-byte
+ * aligned) and per-row scales [T] f32 for K and for V. */
+typedef struct wf_kv_publish_dst {
+  uint8_t* codes_k;
+  uint8_t* codes_v;
+  float* scales_k;
+  float* scales_v;
+} wf_kv_publish_dst;
+
+/* wf_qk_norm_rope fused with the per-token FP8 publish of the same layer:
+ * for every stage s < n_stages with n_dst[s] > 0, the stage's roped K rows
+ * (as written to k_out) and its V rows (columns [2 dim, 3 dim) of qkv) are
+ * quantised per token, with the codec of wf_kv_quant_publish, bit for bit,
+ * and written to dsts[s * 8 + d], d < n_dst[s] (local or peer memory; row
+ * r of the stage goes to row r of each slot).  This is the layer-wise K/V
+ * publish of wave_rt/denoiser/exchange/paged.py:120-145 moved into the
+ * kernel that produces K, so the bf16 K and V are not read a second time.
+ * dsts: host array of n_stages * 8 entries; n_stages <= 8, n_dst[s] <= 8.
+ * The caller orders the consumers' release flags after this call. */
+int wf_qk_norm_rope_publish(const void* qkv, int64_t ld, const void* wq, const void* wk, const float* cos_t,
+                            const float* sin_t, int head_dim, void* q_out, void* k_out, void* k_unroped,
+                            int64_t rows, int64_t dim, int64_t rows_per_stage, float eps,
+                            const wf_kv_publish_dst* dsts, const int32_t* n_dst, int n_stages, void* stream);
+
 /* out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), model.py:70-88. */
 int wf_rms_norm(const void* x, int64_t x_stride, const void* w, void* out, int64_t out_stride, int64_t rows,
                 int64_t dim, float eps, void* stream);

@@ -527,6 +527,47 @@ def test_fused_rows_match_torch(dim):
     assert (r.float() - rms(x, wq).float()).abs().max().item() <= 0.01 * r.float().abs().max().item()
 
 
+@pytest.mark.parametrize("dim", [256, 1536, 5120])
+def test_qk_norm_rope_publish_matches_separate_passes(dim):
+    """wf_qk_norm_rope_publish: q, k and the un-roped k bit-identical to
+    wf_qk_norm_rope; every destination's codes and scales bit-identical to
+    wf_kv_quant_publish on the same K and V rows and to the oracle's per-token
+    codec (the torch-CPU form); stages without destinations publish nothing."""
+    K = _kernels()
+    torch.manual_seed(dim + 1)
+    S, T, hd = 3, 40, 128
+    qkv = (torch.randn(S * T, 3 * dim, device=DEV) * torch.rand(S * T, 1, device=DEV) * 4).bfloat16()
+    qkv[5, 2 * dim:] = 0  # an all-zero V row (the scale clamps to bf16(1e-8))
+    wq = (torch.randn(dim, device=DEV) * 0.5 + 1).bfloat16()
+    wk = (torch.randn(dim, device=DEV) * 0.5 + 1).bfloat16()
+    cos = torch.rand(S * T, hd // 2, device=DEV) * 2 - 1
+    sin = torch.sqrt(1 - cos * cos)
+    ndst = [2, 0, 5]
+    slots = [[(torch.full((T, dim), 0xAB, device=DEV, dtype=torch.uint8),
+               torch.full((T, dim), 0xAB, device=DEV, dtype=torch.uint8),
+               torch.full((T,), -7.0, device=DEV), torch.full((T,), -7.0, device=DEV)) for _ in range(n)]
+             for n in ndst]
+    pub = [[tuple(t.data_ptr() for t in d) for d in st] for st in slots]
+    q, k, ku = K.qk_norm_rope_publish(qkv, dim, wq, wk, cos, sin, hd, T, 1e-6, pub)
+    q0, k0, ku0 = K.qk_norm_rope(qkv, dim, wq, wk, cos, sin, hd, T, 1e-6)
+    assert torch.equal(q, q0) and torch.equal(k, k0) and torch.equal(ku, ku0)
+    for s, st in enumerate(slots):
+        rows = slice(s * T, (s + 1) * T)
+        if not st:
+            continue
+        ref = [(torch.empty(T, dim, device=DEV, dtype=torch.uint8), torch.empty(T, dim, device=DEV, dtype=torch.uint8),
+                torch.empty(T, device=DEV), torch.empty(T, device=DEV))]
+        K.kv_quant_publish(k0[rows], qkv[rows, 2 * dim:], *[[t.data_ptr()] for t in ref[0]])
+        ok_c, ok_s = o_codec.quant_per_token_torch(k0[rows].cpu())
+        ov_c, ov_s = o_codec.quant_per_token_torch(qkv[rows, 2 * dim:].cpu())
+        for ck, cv, sk, sv in st:
+            assert torch.equal(ck, ref[0][0]) and torch.equal(cv, ref[0][1]), s
+            assert torch.equal(sk, ref[0][2]) and torch.equal(sv, ref[0][3]), s
+            assert torch.equal(ck.cpu(), ok_c) and torch.equal(sk.cpu(), ok_s), s
+            assert torch.equal(cv.cpu(), ov_c) and torch.equal(sv.cpu(), ov_s), s
+    assert K.LAUNCHES[0] > 0
+
+
 def test_softmax_exp2_paths_error_bounds():
     """The FMA-pipe polynomial 2^x used for part of the softmax stays within
     1e-4 relative error of exp2 on the range the kernel feeds it ([-125, 8]),

@@ -15,7 +15,7 @@ pytestmark = [pytest.mark.gpu,
 
 
 def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2, fused_assembly=True,
-         w8a8=None):
+         w8a8=None, fused_publish=True):
     from waveforcing_b200.runtime import backend
     from waveforcing_b200.wavefront.dit import DiTConfig, WanDiT
     from waveforcing_b200.wavefront.engine import EngineConfig, WavefrontEngine
@@ -32,6 +32,7 @@ def _run(backend_name, fp8, steps=(1000, 750, 500, 250), num_frames=30, layers=2
     model.set_text(torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(dev))
     eng = WavefrontEngine(model, EngineConfig(steps=steps, num_frames=num_frames, fp8_kv=fp8), device=dev)
     eng.xport.fused_assembly = fused_assembly
+    eng.xport.fused_publish = fused_publish
     for t in range(eng.num_ticks):
         eng.tick(t)
     torch.cuda.synchronize()
@@ -108,3 +109,12 @@ def test_w8a8_ffn_fusion_matches_unfused(qtype):
     a = _run("wf_b200", True, w8a8=qtype)
     assert torch.isfinite(a).all()
     assert _cos(a, b) >= 0.999
+
+
+def test_fused_fp8_publish_is_bit_identical():
+    """Per-token FP8 K/V published by the kernel that produces K
+    (wf_qk_norm_rope_publish) gives exactly the latents of the separate
+    quantise-and-publish pass (wf_kv_quant_publish) through the wavefront."""
+    a = _run("wf_b200", True, fused_publish=True)
+    b = _run("wf_b200", True, fused_publish=False)
+    assert torch.equal(a, b)

@@ -43,6 +43,15 @@ class KvSegment(C.Structure):
                 ("dst_row_stride", C.c_int64)]
 
 
+class KvPublishDst(C.Structure):
+    """wf_kv_publish_dst (include/wfk.h)."""
+
+    _fields_ = [("codes_k", C.c_void_p), ("codes_v", C.c_void_p), ("scales_k", C.c_void_p),
+                ("scales_v", C.c_void_p)]
+
+
+PUBLISH_MAX_STAGES, PUBLISH_MAX_DST = 8, 8
+
 # name -> (restype, argtypes)
 _SIGS = {
     "wf_last_error": (C.c_char_p, []),
@@ -66,6 +75,8 @@ _SIGS = {
     "wf_ln_modulate": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _f32, _vp]),
     "wf_gate_residual": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
     "wf_qk_norm_rope": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),
+    "wf_qk_norm_rope_publish": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32,
+                                       C.POINTER(KvPublishDst), C.POINTER(C.c_int32), _i32, _vp]),
     "wf_rms_norm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),
     "wf_ipc_export": (_i32, [_vp, C.POINTER(C.c_uint8), C.POINTER(_u64)]),
     "wf_ipc_open": (_i32, [C.POINTER(C.c_uint8), C.POINTER(_vp)]),

@@ -7,10 +7,14 @@
 //                    (model.py:70-88, rounding to bf16 before the weight as
 //                    .type_as(x) * weight does), then interleaved RoPE per head
 //                    (wave_rt/runtime/backend.py:119-121) with per-stage tables.
+//   wf_qk_norm_rope_publish  the same, plus the per-token FP8 quantise-and-
+//                    publish of each stage's roped K and its V (from the same
+//                    QKV output) into that stage's destination slots.
 // s = row / rows_per_stage selects the stage's modulation vector / RoPE table.
 #include <cuda_runtime.h>
 
 #include "host_util.h"
+#include "quant_rows.cuh"
 #include "sm100.cuh"
 
 namespace wfk {
@@ -258,6 +262,122 @@ extern "C" int wf_gate_residual(void* x, int64_t x_stride, const void* y, int64_
   return WF_OK;
 }
 
+// ------------------------------------------------ fused FP8 K/V publish
+// Destination slots per stage, kept in parameter space (__grid_constant__:
+// indexed in place, not copied to local memory).
+constexpr int PUB_STAGES = 8, PUB_DST = 8;
+struct PublishTable {
+  int n[PUB_STAGES];
+  uint8_t* ck[PUB_STAGES][PUB_DST];
+  uint8_t* cv[PUB_STAGES][PUB_DST];
+  float* sk[PUB_STAGES][PUB_DST];
+  float* sv[PUB_STAGES][PUB_DST];
+};
+
+// Three warps per token row r of the fused QKV output [rows, >= 3 dim]:
+// role 0 writes roped q; role 1 writes roped k and the normalised un-roped k,
+// exactly as qk_norm_rope_kernel, and, when the row's stage s has
+// destinations, quantises the bf16 roped-k row per token (the codec's row
+// helpers, bit-identical to wf_kv_quant_publish on k_out) into every
+// destination; role 2 does the same for the row's V (columns [2 dim, 3 dim)
+// of the QKV output), which needs no other pass.  Destination rows are
+// indexed by the row's position within its stage, r % rows_per_stage.
+template <int NCH>
+__global__ void __launch_bounds__(256) qk_norm_rope_publish_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int64_t ld, const __nv_bfloat16* __restrict__ wq,
+    const __nv_bfloat16* __restrict__ wk, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+    int head_dim, __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out,
+    __nv_bfloat16* __restrict__ k_unroped, int64_t rows, int64_t rows_per_stage, float eps,
+    const __grid_constant__ PublishTable pub) {
+  using namespace wfk::quant;
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (wid >= 3 * rows) return;
+  const int64_t r = wid / 3;
+  const int role = static_cast<int>(wid - 3 * r);
+  constexpr int DIM = NCH * 256;
+  const int64_t tok = r % rows_per_stage;
+  const int64_t st = r / rows_per_stage;
+  const int nd = (role == 0 || st >= PUB_STAGES) ? 0 : pub.n[st];
+  if (role == 2) {
+    if (nd == 0) return;
+    const uint4* src = reinterpret_cast<const uint4*>(qkv + r * ld + 2 * DIM);
+    uint4 buf[NCH];
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      buf[c] = __ldg(src + lane + 32 * c);
+      m2 = amax8_bits(buf[c], m2);
+    }
+    const RowQuant q = make_rowq(warp_amax_bits(m2));
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint2 code = quant8(buf[c], q);
+      for (int d = 0; d < nd; ++d) reinterpret_cast<uint2*>(pub.cv[st][d] + tok * DIM)[lane + 32 * c] = code;
+    }
+    if (lane == 0)
+      for (int d = 0; d < nd; ++d) pub.sv[st][d][tok] = q.s;
+    return;
+  }
+  const bool is_k = role == 1;
+  const uint4* src = reinterpret_cast<const uint4*>(qkv + r * ld + (is_k ? DIM : 0));
+  const uint4* w4 = reinterpret_cast<const uint4*>(is_k ? wk : wq);
+  float v[NCH][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    unpack8(__ldg(src + lane + 32 * c), v[c]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+  }
+  const float rn = rsqrtf(warp_sum(ss) * (1.f / DIM) + eps);
+  const int half = head_dim / 2;
+  const float* ct = cos_t + (st * rows_per_stage + tok) * half;
+  const float* stab = sin_t + (st * rows_per_stage + tok) * half;
+  __nv_bfloat16* dst = (is_k ? k_out : q_out) + r * DIM;
+  constexpr bool KEEP = NCH <= 12;  // roped k rows of up to 3072 stay in registers for the quantiser
+  uint4 kept[KEEP ? NCH : 1];
+  uint32_t m2 = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int e0 = (lane + 32 * c) * 8;
+    float w[8];
+    unpack8(__ldg(w4 + lane + 32 * c), w);
+    float n[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = bf(bf(v[c][i] * rn) * w[i]);
+    if (is_k && k_unroped) reinterpret_cast<uint4*>(k_unroped + r * DIM)[lane + 32 * c] = pack8(n);
+    const int pd = (e0 % head_dim) / 2;
+    const float4 cv = *reinterpret_cast<const float4*>(ct + pd);
+    const float4 sv = *reinterpret_cast<const float4*>(stab + pd);
+    const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
+    float o[8];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float re = n[2 * p], im = n[2 * p + 1];
+      o[2 * p] = fmaf(re, cc[p], -im * sn[p]);
+      o[2 * p + 1] = fmaf(re, sn[p], im * cc[p]);
+    }
+    const uint4 packed = pack8(o);
+    reinterpret_cast<uint4*>(dst)[lane + 32 * c] = packed;
+    if (nd > 0) {
+      m2 = amax8_bits(packed, m2);
+      if constexpr (KEEP) kept[c] = packed;
+    }
+  }
+  if (nd == 0) return;
+  const RowQuant q = make_rowq(warp_amax_bits(m2));
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    // wider rows read back this lane's own stores of k_out
+    const uint4 packed = KEEP ? kept[c] : reinterpret_cast<const uint4*>(dst)[lane + 32 * c];
+    const uint2 code = quant8(packed, q);
+    for (int d = 0; d < nd; ++d) reinterpret_cast<uint2*>(pub.ck[st][d] + tok * DIM)[lane + 32 * c] = code;
+  }
+  if (lane == 0)
+    for (int d = 0; d < nd; ++d) pub.sk[st][d][tok] = q.s;
+}
+
 extern "C" int wf_qk_norm_rope(const void* qkv, int64_t ld, const void* wq, const void* wk, const float* cos_t,
                                const float* sin_t, int head_dim, void* q_out, void* k_out, void* k_unroped,
                                int64_t rows, int64_t dim, int64_t rows_per_stage, float eps, void* stream) {
@@ -273,6 +393,54 @@ extern "C" int wf_qk_norm_rope(const void* qkv, int64_t ld, const void* wq, cons
         static_cast<const __nv_bfloat16*>(qkv), ld, static_cast<const __nv_bfloat16*>(wq),
         static_cast<const __nv_bfloat16*>(wk), cos_t, sin_t, head_dim, static_cast<__nv_bfloat16*>(q_out),
         static_cast<__nv_bfloat16*>(k_out), static_cast<__nv_bfloat16*>(k_unroped), rows, rows_per_stage, eps);
+  });
+  if (rc != WF_OK) return rc;
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_qk_norm_rope_publish(const void* qkv, int64_t ld, const void* wq, const void* wk,
+                                       const float* cos_t, const float* sin_t, int head_dim, void* q_out,
+                                       void* k_out, void* k_unroped, int64_t rows, int64_t dim,
+                                       int64_t rows_per_stage, float eps, const wf_kv_publish_dst* dsts,
+                                       const int32_t* n_dst, int n_stages, void* stream) {
+  if (!qkv || !wq || !wk || !cos_t || !sin_t || !q_out || !k_out || rows < 0 || rows_per_stage < 1 ||
+      head_dim < 8 || head_dim % 8 || dim % head_dim || ld % 8 || !aligned16(qkv) || !aligned16(q_out) ||
+      !aligned16(k_out) || !aligned16(cos_t) || !aligned16(sin_t) || (k_unroped && !aligned16(k_unroped)))
+    return fail(WF_ERR_INVALID_ARG, "wf_qk_norm_rope_publish: bad arguments");
+  if (n_stages < 0 || n_stages > PUB_STAGES || (n_stages > 0 && (!dsts || !n_dst)))
+    return fail(WF_ERR_INVALID_ARG, "wf_qk_norm_rope_publish: n_stages %d (at most %d, with dsts and n_dst)",
+                n_stages, PUB_STAGES);
+  if (rows > static_cast<int64_t>(PUB_STAGES) * rows_per_stage && n_stages > 0)
+    return fail(WF_ERR_INVALID_ARG, "wf_qk_norm_rope_publish: rows of more than %d stages", PUB_STAGES);
+  PublishTable tab{};
+  for (int s = 0; s < n_stages; ++s) {
+    if (n_dst[s] < 0 || n_dst[s] > PUB_DST)
+      return fail(WF_ERR_INVALID_ARG, "wf_qk_norm_rope_publish: stage %d has %d destinations (0..%d)", s,
+                  n_dst[s], PUB_DST);
+    tab.n[s] = n_dst[s];
+    for (int d = 0; d < n_dst[s]; ++d) {
+      const wf_kv_publish_dst& e = dsts[s * PUB_DST + d];
+      if (!e.codes_k || !e.codes_v || !e.scales_k || !e.scales_v ||
+          (reinterpret_cast<uintptr_t>(e.codes_k) | reinterpret_cast<uintptr_t>(e.codes_v)) & 7 ||
+          (reinterpret_cast<uintptr_t>(e.scales_k) | reinterpret_cast<uintptr_t>(e.scales_v)) & 3)
+        return fail(WF_ERR_INVALID_ARG,
+                    "wf_qk_norm_rope_publish: stage %d destination %d: null or misaligned (codes 8 B, scales 4 B)",
+                    s, d);
+      tab.ck[s][d] = e.codes_k;
+      tab.cv[s][d] = e.codes_v;
+      tab.sk[s][d] = e.scales_k;
+      tab.sv[s][d] = e.scales_v;
+    }
+  }
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((3 * rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = by_dim(dim, [&](auto n) {
+    qk_norm_rope_publish_kernel<decltype(n)::value><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(qkv), ld, static_cast<const __nv_bfloat16*>(wq),
+        static_cast<const __nv_bfloat16*>(wk), cos_t, sin_t, head_dim, static_cast<__nv_bfloat16*>(q_out),
+        static_cast<__nv_bfloat16*>(k_out), static_cast<__nv_bfloat16*>(k_unroped), rows, rows_per_stage, eps, tab);
   });
   if (rc != WF_OK) return rc;
   WFK_CUDA_TRY(cudaGetLastError());

@@ -93,6 +93,10 @@ class PagedTransport:
         # assemble each layer's context with one wf_kv_assemble launch (when the
         # caller passes RoPE tables); False keeps the per-page copies
         self.fused_assembly = True
+        # per-token FP8 publishes may be done by the kernel that produces K
+        # (wf_qk_norm_rope_publish): the closures then expose their targets
+        # (``exch.fp8_publish_targets(layer)``) and only write the flags
+        self.fused_publish = True
         self.naw_max, self.Wmax = slab_geometry(max_attn_frames, rf_step, npb)
         self.local = [s for s in range(rf_step + 1) if self.stage_rank[s] == rank]
         # a CPU device is accepted only to exercise the host-side bookkeeping in tests
@@ -206,24 +210,41 @@ class PagedTransport:
         tok = (gen * self.Ln + layer) * W + slot * self.T
         return tok
 
-    def publish(self, s: int, k: torch.Tensor, v: torch.Tensor, send, layer: int, gen: int, tick: int) -> None:
+    def fp8_targets(self, s: int, send, layer: int, gen: int):
+        """Producer stage ``s``'s FP8 destination slots for (layer, gen): one
+        (codes_k, codes_v, scales_k, scales_v) pointer tuple per (stage, slot)
+        of ``send``, local or peer."""
+        HD = self.H * self.D
+        out = []
+        for m, slot in send:
+            d = self.dst[m]
+            tok = self._slot_offsets(m, gen, layer, slot)
+            out.append((d["kc"] + tok * HD, d["vc"] + tok * HD, d["ks"] + tok * 4, d["vs"] + tok * 4))
+        return out
+
+    def _expose_targets(self, exch, s: int, send, gen: int) -> None:
+        """Let the K-producing kernel publish for this closure (per-token FP8)."""
+        if self.fp8 and self.fp8_gran == "token" and self.fused_publish and send:
+            exch.fp8_publish_targets = lambda layer: self.fp8_targets(s, send, layer, gen)
+            exch.prepublished = set()
+
+    def publish(self, s: int, k: torch.Tensor, v: torch.Tensor, send, layer: int, gen: int, tick: int,
+                prepublished: bool = False) -> None:
         """Producer stage ``s`` publishes one layer's K, V [T, H, D] into each
-        consumer slot of ``send`` [(stage, slot)] (paged.py:120-145)."""
+        consumer slot of ``send`` [(stage, slot)] (paged.py:120-145).  With
+        ``prepublished`` the codes and scales are already in place (written
+        earlier on this stream by wf_qk_norm_rope_publish) and only the
+        release flags remain."""
         if not send:
             return
         T, HD = self.T, self.H * self.D
         src_i = {m: self.src_index_of(m, s) for m, _ in send}
         cur_h = self._cur_stream_handle()
         if self.fp8:
-            ck, cv, sk, sv = [], [], [], []
-            for m, slot in send:
-                d = self.dst[m]
-                tok = self._slot_offsets(m, gen, layer, slot)
-                ck.append(d["kc"] + tok * HD)
-                cv.append(d["vc"] + tok * HD)
-                sk.append(d["ks"] + tok * 4)
-                sv.append(d["vs"] + tok * 4)
-            if self.fp8_gran == "token":
+            ck, cv, sk, sv = (list(x) for x in zip(*self.fp8_targets(s, send, layer, gen)))
+            if prepublished:
+                pass
+            elif self.fp8_gran == "token":
                 kernels.kv_quant_publish(k.reshape(T, HD), v.reshape(T, HD), ck, cv, sk, sv)
             else:
                 self._publish_tensor_scaled(k, v, ck, cv, sk, sv, cur_h)
@@ -426,7 +447,7 @@ class PagedTransport:
             v = value[0]
             lp = prof() if prof is not None else None
             e_en = self._lp_mark(lp)
-            self.publish(m, k, v, send, Lh, gen, tick)
+            self.publish(m, k, v, send, Lh, gen, tick, prepublished=Lh in getattr(exch, "prepublished", ()))
             e_pub = self._lp_mark(lp)
             if self.fp8:
                 Kb, Vb = sl["kb"], sl["vb"]
@@ -480,6 +501,7 @@ class PagedTransport:
                 lp["layers"].append(dict(layer=Lh, enter=e_en, pub=e_pub, wait=e_wt, cat=self._lp_mark(lp)))
             return Kb[:active_len].unsqueeze(0), Vb[:active_len].unsqueeze(0)
 
+        self._expose_targets(exch, m, send, gen)
         return exch
 
     def make_store_exch(self, clean, store_kv: list, chunk: int, act, tick, rope_fn=None, rope_tab_fn=None,
@@ -503,7 +525,8 @@ class PagedTransport:
             v = value[0]
             lp = prof() if prof is not None else None
             e_en = self._lp_mark(lp)
-            self.publish(self.store, k, v, send, layer_idx, gen, tick)
+            self.publish(self.store, k, v, send, layer_idx, gen, tick,
+                         prepublished=layer_idx in getattr(exch, "prepublished", ()))
             e_pub = self._lp_mark(lp)
             if rope_tab_fn is not None and self.fused_assembly:
                 parts = self.anchor_working_parts(clean[layer_idx], chunk * self.npb, self.npb)
@@ -527,6 +550,7 @@ class PagedTransport:
                                          cat=self._lp_mark(lp)))
             return Kbuf[:off + T].unsqueeze(0), Vbuf[:off + T].unsqueeze(0)
 
+        self._expose_targets(exch, self.store, send, gen)
         return exch
 
 

@@ -7,6 +7,7 @@ CPU tensors or a missing libwfk.so raise.
 
 from __future__ import annotations
 
+import ctypes as C
 import math
 
 import torch
@@ -299,6 +300,43 @@ def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor
                                     sin.data_ptr(), head_dim, q.data_ptr(), k.data_ptr(),
                                     ku.data_ptr() if ku is not None else None, rows, dim, rows_per_stage, eps,
                                     _stream()), "wf_qk_norm_rope")
+    return q, k, ku
+
+
+def qk_norm_rope_publish(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor, cos: torch.Tensor,
+                         sin: torch.Tensor, head_dim: int, rows_per_stage: int, eps: float, publish,
+                         want_unroped: bool = True):
+    """qk_norm_rope plus the per-token FP8 publish of every stage's roped K and
+    V (wf_qk_norm_rope_publish).  ``publish[s]`` lists stage s's destination
+    slots as (codes_k, codes_v, scales_k, scales_v) device pointers (ints),
+    each slot [rows_per_stage, dim] codes and [rows_per_stage] f32 scales."""
+    _check(qkv.dim() == 2 and qkv.dtype == torch.bfloat16 and qkv.shape[1] >= 3 * dim,
+           "qk_norm_rope_publish: qkv must be a bf16 [rows, >= 3*dim] matrix")
+    rows = qkv.shape[0]
+    _check(all(w.numel() == dim and w.dtype == torch.bfloat16 and w.is_contiguous() for w in (wq, wk)),
+           "qk_norm_rope_publish: norm weights must be contiguous bf16 with dim elements")
+    for tab in (cos, sin):
+        _check(tab.dtype == torch.float32 and tab.dim() == 2 and tab.shape[0] >= rows
+               and tab.shape[1] == head_dim // 2 and tab.is_contiguous(),
+               "qk_norm_rope_publish: cos/sin must be contiguous f32 [>= rows, head_dim/2]")
+    n_stages = len(publish)
+    _check(n_stages <= L.PUBLISH_MAX_STAGES and n_stages * rows_per_stage >= rows
+           and all(len(p) <= L.PUBLISH_MAX_DST for p in publish),
+           "qk_norm_rope_publish: one destination list per stage, at most 8 stages of 8 destinations")
+    _need_cuda(qkv)
+    dsts = (L.KvPublishDst * max(1, n_stages * L.PUBLISH_MAX_DST))()
+    counts = (C.c_int32 * max(1, n_stages))()
+    for s, lst in enumerate(publish):
+        counts[s] = len(lst)
+        for d, (ck, cv, sk, sv) in enumerate(lst):
+            dsts[s * L.PUBLISH_MAX_DST + d] = L.KvPublishDst(int(ck), int(cv), int(sk), int(sv))
+    q = torch.empty((rows, dim), device=qkv.device, dtype=torch.bfloat16)
+    k = torch.empty_like(q)
+    ku = torch.empty_like(q) if want_unroped else None
+    L.check(L.lib().wf_qk_norm_rope_publish(qkv.data_ptr(), qkv.stride(0), wq.data_ptr(), wk.data_ptr(),
+                                            cos.data_ptr(), sin.data_ptr(), head_dim, q.data_ptr(), k.data_ptr(),
+                                            ku.data_ptr() if ku is not None else None, rows, dim, rows_per_stage,
+                                            eps, dsts, counts, n_stages, _stream()), "wf_qk_norm_rope_publish")
     return q, k, ku
 
 

@@ -330,8 +330,21 @@ class WanDiT(nn.Module):
             fq = None if (separate_qkv and not fused) else self._fused_qkv(b)
             if fused and fq is not None:
                 qkv = self._qkv_gemm(fq, h)
-                rq_all, rk_all, ku_all = kernels.qk_norm_rope(qkv, dim, b.self_attn.norm_q.weight,
-                                                              b.self_attn.norm_k.weight, cos_all, sin_all, D, T, eps)
+                # exchange closures that publish per-token FP8 K/V expose their
+                # destination slots; the kernel that produces K publishes them
+                targets = [getattr(t.exch, "fp8_publish_targets", None) for t in tasks]
+                if any(tg is not None for tg in targets):
+                    pub = [tg(li) if tg is not None else [] for tg in targets]
+                    rq_all, rk_all, ku_all = kernels.qk_norm_rope_publish(
+                        qkv, dim, b.self_attn.norm_q.weight, b.self_attn.norm_k.weight, cos_all, sin_all, D, T, eps,
+                        pub)
+                    for t, tg in zip(tasks, targets):
+                        if tg is not None:
+                            t.exch.prepublished.add(li)
+                else:
+                    rq_all, rk_all, ku_all = kernels.qk_norm_rope(qkv, dim, b.self_attn.norm_q.weight,
+                                                                  b.self_attn.norm_k.weight, cos_all, sin_all, D, T,
+                                                                  eps)
                 v = qkv[:, 2 * dim:].reshape(S, T, H, D)
                 rq_all, rk_all, ku_all = (t.view(S, T, H, D) for t in (rq_all, rk_all, ku_all))
             else:
