@@ -70,6 +70,9 @@ def parse():
                          "batched cross-attention of six stages)")
     ap.add_argument("--library", action="store_true",
                     help="--kernel attn: also time torch SDPA, the reference's attention call, on the same buffers")
+    ap.add_argument("--trace", action="store_true",
+                    help="profile two steady ticks with torch.profiler (CUPTI): in-stream kernel time, device idle "
+                         "inside the tick, per-kernel shares (one JSON line; no bench line)")
     ap.add_argument("--forward", action="store_true",
                     help="BASELINE config 2: one full DiT forward of a 3-frame chunk at t=600 with a 6-chunk context")
     return ap.parse_args()
@@ -438,6 +441,64 @@ def run_reference_gpu_arm(args):
     dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ trace
+def trace_ticks(args, make_engine, noise_cpu, fill, dev, rank, n_trace: int = 2):
+    """Device activity of ``n_trace`` steady ticks from a CUPTI trace
+    (torch.profiler): every kernel's in-stream start and end.  Reports the
+    union of kernel intervals against the span from the first kernel to the
+    last (device idle inside the ticks), the host time to issue the ticks,
+    and each kernel family's share of the summed kernel time."""
+    from torch.profiler import ProfilerActivity, profile
+
+    eng = make_engine(noise_cpu.to(dev))
+    for t in range(fill + max(1, args.warmup)):
+        eng.tick(t)
+    torch.cuda.synchronize()
+    t0 = fill + max(1, args.warmup)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        h0 = time.perf_counter()
+        for i in range(n_trace):
+            eng.tick(t0 + i)
+        host_ms = (time.perf_counter() - h0) * 1e3
+        torch.cuda.synchronize()
+    eng.close()
+    ivs = []
+    by_name: dict = {}
+    for e in prof.events():
+        if e.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        start = e.time_range.start
+        end = e.time_range.end
+        if end <= start:
+            continue
+        ivs.append((start, end))
+        key = e.name.split("(")[0].split("<")[0].strip()
+        by_name[key] = by_name.get(key, 0.0) + (end - start)
+    ivs.sort()
+    busy, cur_s, cur_e = 0.0, None, None
+    for s_, e_ in ivs:
+        if cur_e is None or s_ > cur_e:
+            if cur_e is not None:
+                busy += cur_e - cur_s
+            cur_s, cur_e = s_, e_
+        else:
+            cur_e = max(cur_e, e_)
+    if cur_e is not None:
+        busy += cur_e - cur_s
+    span = (ivs[-1][1] - ivs[0][0]) if ivs else 0.0
+    total = sum(by_name.values())
+    top = sorted(by_name.items(), key=lambda kv: -kv[1])[:16]
+    if rank == 0:
+        print(json.dumps({
+            "trace": f"{n_trace} steady ticks, rank {rank}", "kernels": len(ivs),
+            "kernels_per_tick": len(ivs) / n_trace, "span_ms_per_tick": span / 1e3 / n_trace,
+            "busy_ms_per_tick": busy / 1e3 / n_trace, "idle_frac": 1 - busy / span if span else None,
+            "kernel_sum_ms_per_tick": total / 1e3 / n_trace, "host_issue_ms_per_tick": host_ms / n_trace,
+            "shares": [{"kernel": k, "ms_per_tick": v / 1e3 / n_trace, "share": v / total} for k, v in top],
+            "note": "CUPTI kernel timestamps (profiler overhead on the host side; kernel durations in-stream)"}),
+            flush=True)
+
+
 # ---------------------------------------------------------------- GPU side
 def run_gpu_arm(args):
     from waveforcing_b200 import kernels
@@ -487,6 +548,13 @@ def run_gpu_arm(args):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.tolist()
+
+    if args.trace:
+        trace_ticks(args, make_engine, noise_cpu, fill, dev, rank)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     # ---------------- device-resident run (value)
     gn = torch.Generator(device="cpu").manual_seed(ecfg.seed)

@@ -210,3 +210,32 @@ def test_dit_routes_only_self_attention_through_the_backend(monkeypatch):
     assert [tuple(o.shape) for o in out] == [(cfg.in_ch, cfg.frames_per_block, cfg.lat_h, cfg.lat_w)] * 2
     assert all(torch.isfinite(o).all() for o in out)
     assert calls == {"self": cfg.layers * len(tasks), "cross": cfg.layers}
+
+
+def test_fp8_compact_slots_cover_received_chunks(golden):
+    """FP8 slabs keep only received chunks: for every tick of the reference's
+    5- and 4-step geometry, each consumer's producers (higher stages, then
+    the store's live slot) land on distinct compact slots below rf_step - m,
+    and the consumer's read ranges cover exactly those slots."""
+    recs = golden("geometry.json")
+    seen = 0
+    for r in recs:
+        if r["role"] != "denoise":
+            continue
+        S, t, act, live = r["rf_step"], r["tick"], r["act_ranks"], r["store_active"]
+        for m in act:
+            gm = paged.tick_geometry(m, t, act, live, S, 21, 3)
+            got = []
+            for s in act:
+                if s <= m:
+                    continue
+                gs = paged.tick_geometry(s, t, act, live, S, 21, 3)
+                slot = dict(gs["send"])[m]
+                got.append(paged.PagedTransport.fp8_slot(gm, slot))
+            if live:
+                got.append(0)  # the store's live slot
+            n_in = gm["active_slots"] - gm["base_infl"] - 1
+            assert sorted(got) == list(range(gm["live"] + n_in)), (S, t, m, got)
+            assert all(0 <= c < S - m for c in got)
+            seen += 1
+    assert seen > 50

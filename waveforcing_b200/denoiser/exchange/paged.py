@@ -107,7 +107,6 @@ class PagedTransport:
         self.slabs: dict = {}
         self.flags: dict = {}
         self.src_index: dict = {}
-        THD = T * H * D
         W = self.Wmax * T
         for m in self.local:
             if m >= rf_step:
@@ -115,10 +114,15 @@ class PagedTransport:
             srcs = list(range(m + 1, rf_step)) + [self.store]
             self.src_index[m] = {s: i for i, s in enumerate(srcs)}
             if fp8:
-                sl = dict(kc=torch.zeros((GT, Ln, W, H * D), device=self.device, dtype=torch.uint8),
-                          vc=torch.zeros((GT, Ln, W, H * D), device=self.device, dtype=torch.uint8),
-                          ks=torch.ones((GT, Ln, W), device=self.device, dtype=torch.float32),
-                          vs=torch.ones((GT, Ln, W), device=self.device, dtype=torch.float32),
+                # FP8 slabs hold only what is received: the live store slot and
+                # the higher stages' in-flight chunks, rf_step - m compact slots
+                # (fp8_slot); anchor, working and own pages reach the bf16
+                # context buffer (kb, vb) from local memory
+                W8 = self.slab_rows(m)
+                sl = dict(kc=torch.zeros((GT, Ln, W8, H * D), device=self.device, dtype=torch.uint8),
+                          vc=torch.zeros((GT, Ln, W8, H * D), device=self.device, dtype=torch.uint8),
+                          ks=torch.ones((GT, Ln, W8), device=self.device, dtype=torch.float32),
+                          vs=torch.ones((GT, Ln, W8), device=self.device, dtype=torch.float32),
                           kb=torch.zeros((W, H, D), device=self.device, dtype=dtype),
                           vb=torch.zeros((W, H, D), device=self.device, dtype=dtype))
             else:
@@ -204,11 +208,30 @@ class PagedTransport:
         self.dst.clear()
 
     # ---------------------------------------------------------------- publish
+    def slab_rows(self, m: int) -> int:
+        """Token rows per (generation, layer) block of consumer stage m's slab:
+        Wmax slots of the bf16 context (paged.py:26-30), or the rf_step - m
+        compact received slots of an FP8 slab (at most one live slot and the
+        in-flight chunks of stages m+1 .. rf_step-1)."""
+        return ((self.rf_step - m) if self.fp8 else self.Wmax) * self.T
+
+    @staticmethod
+    def fp8_slot(g: dict, slot: int) -> int:
+        """The compact FP8 slab slot of context slot ``slot`` of a tick with
+        geometry ``g`` (tick_geometry): the live store slot (slot naw) -> 0;
+        the in-flight chunk at base_infl + k (k >= 1; base_infl itself is the
+        consumer's own chunk) -> live + k - 1."""
+        if g["live"] and slot == g["naw"]:
+            return 0
+        k = slot - g["base_infl"]
+        if k < 1:
+            raise ValueError(f"context slot {slot} is not received (naw={g['naw']}, base_infl={g['base_infl']})")
+        return g["live"] + k - 1
+
     def _slot_offsets(self, m, gen, layer, slot):
-        """Element offsets of (gen, layer, slot) in consumer m's slabs."""
-        W = self.Wmax * self.T
-        tok = (gen * self.Ln + layer) * W + slot * self.T
-        return tok
+        """Token-row offset of (gen, layer, slot) in consumer m's slabs (slot is
+        compact for FP8 slabs, see fp8_slot)."""
+        return (gen * self.Ln + layer) * self.slab_rows(m) + slot * self.T
 
     def fp8_targets(self, s: int, send, layer: int, gen: int):
         """Producer stage ``s``'s FP8 destination slots for (layer, gen): one
@@ -438,6 +461,13 @@ class PagedTransport:
         naw, base_infl, act_slots = g["naw"], g["base_infl"], g["active_slots"]
         self_off, live_off, active_len = base_infl * T, naw * T, act_slots * T
         recv, send = g["recv"], g["send"]
+        if self.fp8:  # FP8 slabs are addressed by compact slot; consumers share this tick's geometry
+            send = [(mm, self.fp8_slot(g, slot)) for mm, slot in send]
+        live = g["live"]
+        n_in = act_slots - base_infl - 1  # in-flight chunks of higher stages
+        # received FP8 rows: (context rows, compact slab rows) of the live slot and the in-flight chunks
+        recv_rows = [(slice(naw * T, base_infl * T), slice(0, live * T)),
+                     (slice((base_infl + 1) * T, act_slots * T), slice(live * T, (live + n_in) * T))]
         sl = self.slabs[m]
 
         def exch(*, layer_idx, roped_query, roped_key, unroped_key, value, current_start, tokens_per_frame,
@@ -462,11 +492,10 @@ class PagedTransport:
                 e_wt = self._lp_mark(lp)
                 deq = []
                 if self.fp8:
-                    for a, b in ((naw, base_infl), (base_infl + 1, act_slots)):
-                        if b > a:
-                            rows = slice(a * T, b * T)
-                            deq.append((rows, sl["kc"][gen, Lh, rows], sl["ks"][gen, Lh, rows],
-                                        sl["vc"][gen, Lh, rows], sl["vs"][gen, Lh, rows]))
+                    for rows, src in recv_rows:
+                        if rows.stop > rows.start:
+                            deq.append((rows, sl["kc"][gen, Lh, src], sl["ks"][gen, Lh, src],
+                                        sl["vc"][gen, Lh, src], sl["vs"][gen, Lh, src]))
                 tabs = (lambda start: rope_tab_fn(start, post_patch_height, post_patch_width, dim,
                                                   rope_num_heads))
                 self.assemble(Kb, Vb, parts, tabs, (k, v), self_off, deq)
@@ -486,13 +515,12 @@ class PagedTransport:
                 e_wt = self._lp_mark(lp)
                 if self.fp8:
                     HD = self.H * self.D
-                    for a, b in ((naw, base_infl), (base_infl + 1, act_slots)):
-                        if b <= a:
+                    for rows, src in recv_rows:
+                        if rows.stop <= rows.start:
                             continue
-                        rows = slice(a * T, b * T)
-                        kernels.kv_dequant(sl["kc"][gen, Lh, rows], sl["ks"][gen, Lh, rows], L.WF_SCALE_TOKEN,
+                        kernels.kv_dequant(sl["kc"][gen, Lh, src], sl["ks"][gen, Lh, src], L.WF_SCALE_TOKEN,
                                            out=Kb[rows].view(-1, HD))
-                        kernels.kv_dequant(sl["vc"][gen, Lh, rows], sl["vs"][gen, Lh, rows], L.WF_SCALE_TOKEN,
+                        kernels.kv_dequant(sl["vc"][gen, Lh, src], sl["vs"][gen, Lh, src], L.WF_SCALE_TOKEN,
                                            out=Vb[rows].view(-1, HD))
             if store_active and store_slot_sink is not None:
                 # torch.stack copies: the live slot outlives this layer's buffers
@@ -514,7 +542,8 @@ class PagedTransport:
         clean_len = min(8, max(0, tick - self.store))
         wmax_chunks = max(0, (self.max_attn_frames - len(act) * self.npb - self.npb) // self.npb)
         naw = 0 if clean_len == 0 else 1 + min(wmax_chunks, clean_len - 1)
-        send = [(m, naw) for m in act]
+        # the live slot of every active denoise stage; compact slot 0 of an FP8 slab
+        send = [(m, 0 if self.fp8 else naw) for m in act]
         gen = tick % self.GT
         T = self.T
         Kbuf, Vbuf = self.store_buf
@@ -632,6 +661,8 @@ class PagedExchangeMixin:
         return out[0], out[1]
 
     def _publish_paged(self, k, v, dst_slots, layer: int, gen: int, tick: int) -> None:
+        """paged.py:120-145.  ``dst_slots`` are (stage, slot) pairs; with FP8
+        transport the slots are compact slab slots (PagedTransport.fp8_slot)."""
         self._pg.publish(self.rank, k, v, dst_slots, layer, gen, tick)
 
     def _wait_paged_flag(self, src: int, layer: int, gen: int, tick: int) -> None:
