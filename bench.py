@@ -60,7 +60,8 @@ def parse():
     ap.add_argument("--w8a8", default="none", choices=["none", "e4m3", "int8"])
     ap.add_argument("--denoise-steps", default="1000,800,600,400,200")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["attn", "gemm", "codec", "dequant", "assemble", "publish"],
+    ap.add_argument("--kernel", default=None,
+                    choices=["attn", "attn8", "gemm", "codec", "dequant", "assemble", "publish"],
                     help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
     ap.add_argument("--kv-len", type=int, default=0,
@@ -756,6 +757,41 @@ def run_kernel_bench(args):
                     del ref
         work, unit, bound = 4.0 * T * Lk * H * D / 1e12, "TFLOP/s", "tensor"
         name = f"attn_fwd q{T} kv{Lk} h{H}"
+    elif args.kernel == "attn8":
+        # FP8-input attention: e4m3 K/V codes with per-token scales, expanded
+        # to f16 in shared memory; the library leg (--library) times the path
+        # it replaces, per-token dequantisation to bf16 + the bf16 kernel
+        Lk = args.kv_len if args.kv_len > 0 else args.ctx_chunks * T
+        if args.q_len > 0:
+            T = args.q_len
+        HD = H * D
+        set_bytes = 2 * 2 * T * HD + 2 * Lk * (HD + 4)
+        for i in range(n_sets(set_bytes)):
+            q = torch.randn(1, T, H, D, device=dev, generator=g).bfloat16()
+            kx = torch.randn(Lk, HD, device=dev, generator=g).bfloat16()
+            vx = torch.randn(Lk, HD, device=dev, generator=g).bfloat16()
+            kc, ks = kernels.kv_quant(kx, L.WF_SCALE_TOKEN)
+            vc, vs = kernels.kv_quant(vx, L.WF_SCALE_TOKEN)
+            o = torch.empty_like(q)
+            kc4, vc4 = kc.view(1, Lk, H, D), vc.view(1, Lk, H, D)
+            fns.append(lambda q=q, kc4=kc4, vc4=vc4, ks=ks, vs=vs, o=o: kernels.attention_fp8(
+                q, kc4, vc4, ks, vs, L.WF_SCALE_TOKEN, out=o))
+            if args.library:
+                kb = torch.empty(1, Lk, H, D, device=dev, dtype=torch.bfloat16)
+                vb = torch.empty_like(kb)
+
+                def deq_attn(q=q, kc=kc, vc=vc, ks=ks, vs=vs, kb=kb, vb=vb, o=o):
+                    kernels.kv_dequant(kc, ks, L.WF_SCALE_TOKEN, out=kb.view(Lk, HD))
+                    kernels.kv_dequant(vc, vs, L.WF_SCALE_TOKEN, out=vb.view(Lk, HD))
+                    kernels.attention(q, kb, vb, out=o)
+
+                lib_fns.append(deq_attn)
+                if i == 0:
+                    a8 = kernels.attention_fp8(q, kc4, vc4, ks, vs, L.WF_SCALE_TOKEN)
+                    deq_attn()
+                    lib_diff = float((a8.float() - o.float()).abs().max() / o.float().abs().max())
+        work, unit, bound = 4.0 * T * Lk * H * D / 1e12, "TFLOP/s", "tensor"
+        name = f"attn_fwd e4m3 K/V (per-token scales) q{T} kv{Lk} h{H}"
     elif args.kernel == "gemm":
         set_bytes = T * cfg.dim + cfg.ffn * cfg.dim + 2 * T * cfg.ffn
         for _ in range(n_sets(set_bytes)):
@@ -855,7 +891,8 @@ def run_kernel_bench(args):
     library = None
     if lib_fns:
         lms = graph_ms(lib_fns)
-        library = {"name": "torch SDPA, default dispatch (cuDNN on B200)", "ms": lms,
+        library = {"name": ("per-token dequant to bf16 + bf16 wf_attn_fwd" if args.kernel == "attn8"
+                            else "torch SDPA, default dispatch (cuDNN on B200)"), "ms": lms,
                    "achieved": work / (lms * 1e-3), "max_abs_diff_vs_wf": lib_diff,
                    # the product kernel once more after the library leg, to expose clock drift
                    "wf_ms_after": graph_ms(fns)}

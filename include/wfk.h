@@ -61,10 +61,18 @@ unsigned int wf_status_take(void);
  * sageattn on (roped_query, ctx_k, ctx_v)); block causality is given by which
  * chunks the caller places in K/V (wave_rt/denoiser/exchange/paged.py:247-248).
  * Shapes: q/o [batch, Lq, H, D], k/v [batch, Lk, H, D]; strides are
- * {batch, token, head} in elements.  kv_dtype must be WF_DTYPE_BF16 (FP8 K/V
- * pages are dequantised on receive by wf_kv_dequant); k_scale, v_scale and
- * scale_mode are reserved and must be NULL/NULL/WF_SCALE_NONE.
- * Requires 16-byte aligned base pointers and strides that are multiples of 8. */
+ * {batch, token, head} in elements.  Requires 16-byte aligned base pointers
+ * and strides that are multiples of 8.
+ *   kv_dtype WF_DTYPE_BF16: k/v bf16; k_scale/v_scale NULL, WF_SCALE_NONE.
+ *   kv_dtype WF_DTYPE_E4M3: k/v are e4m3 codes (one byte per element, strides
+ *   multiples of 16), as the FP8 transport carries them; scale_mode
+ *   WF_SCALE_TOKEN reads one f32 scale per token row, k_scale[b * Lk + key]
+ *   (the per-token codec, over all heads of the row), WF_SCALE_TENSOR reads
+ *   k_scale[0] (common.py:143-164), WF_SCALE_NONE uses the codes as values
+ *   (onesided.py:151-153).  The kernel expands each TMA-loaded code tile in
+ *   shared memory to f16 products f16(e4m3(code) * scale) and runs both
+ *   contractions on f16 operands (q converted from bf16, P written as f16),
+ *   so |q| and |code * scale| must stay below 65504. */
 int wf_attn_fwd(const void* q, const void* k, const void* v, void* o, int batch, int Lq, int Lk, int H, int D,
                 const int64_t* q_stride, const int64_t* k_stride, const int64_t* v_stride,
                 const int64_t* o_stride, int kv_dtype, const float* k_scale, const float* v_scale,

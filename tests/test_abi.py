@@ -72,6 +72,16 @@ def test_constants_match_the_header():
 
 
 @pytest.mark.parametrize("name,args,code", [
+    ("wf_attn_fwd", (None, None, None, None, 1, 1, 1, 1, 128, None, None, None, None, 7, None, None, 0, 1.0, None),
+     2),                                                                      # unknown kv_dtype
+    ("wf_attn_fwd", (None, None, None, None, 1, 1, 1, 1, 128, None, None, None, None, 0, 16, None, 0, 1.0, None),
+     1),                                                                      # bf16 K/V given a scale
+    ("wf_attn_fwd", (None, None, None, None, 1, 1, 1, 1, 128, None, None, None, None, 1, None, None, 2, 1.0, None),
+     1),                                                                      # e4m3 token mode without scales
+    ("wf_attn_fwd", (None, None, None, None, 1, 1, 1, 1, 128, None, None, None, None, 1, 16, 16, 9, 1.0, None),
+     1),                                                                      # e4m3 unknown scale_mode
+    ("wf_qk_norm_rope_publish", (16, 16, 16, 16, 16, 16, 128, 16, 16, None, 4, 1536, 4, 1e-6, None, None, 9, None),
+     1),                                                                      # more than 8 stages
     ("wf_kv_quant", (None, None, None, 4, 16, 16, 2, None, None), 1),
     ("wf_kv_quant", (16, 16, 16, 4, 12, 16, 2, None, None), 1),                # cols not a multiple of 8
     ("wf_kv_dequant", (16, None, 16, 4, 16, 16, 2, None), 1),                 # token mode without scales

@@ -286,3 +286,178 @@ def test_model_detects_the_exchange_race():
     with pytest.raises(AssertionError):
         for seed in range(200):
             Early(4, 2, seed).run()
+
+
+class SimFP8(Sim):
+    """The FP8 K/V variant (attn_fwd_e4m3_kernel): TMA lands raw tiles (Q in
+    bf16, K/V as e4m3 codes in the upper half of their slots) on q_raw /
+    raw_k / raw_v; two converter warps, each owning half of every tile's rows,
+    rewrite the tiles in place as f16 and arrive on the operand barriers the
+    MMA waits on (q, full_k, full_v; two arrivals per phase here, one per
+    converter warp).  A raw tile aliases the converted tile of its slot: a
+    copy that lands while an MMA still reads the slot, or a conversion that
+    writes it then, is a race."""
+
+    def __init__(self, nk, n_items, seed, warps_per_wg=2):
+        super().__init__(nk, n_items, seed, warps_per_wg)
+        self.b["q"] = Bar(2)
+        self.b["q_raw"] = Bar(1)
+        for s in range(NSK):
+            self.b[f"full_k{s}"], self.b[f"raw_k{s}"] = Bar(2), Bar(1)
+        for h in range(2):
+            self.b[f"full_v{h}"], self.b[f"raw_v{h}"] = Bar(2), Bar(1)
+
+    def land(self, i):
+        buf, tag, bar, nbytes = self.tma.pop(i)
+        alias = buf.replace(".raw", ".")
+        assert not self.reads.get(alias), f"TMA overwrote {alias} while an MMA still reads it"
+        self.smem[buf] = tag
+        self.smem[alias] = "clobbered"
+        self.b[bar].complete_tx(nbytes)
+
+    def producer(self):
+        kt = vt = 0
+        nk = self.nk
+
+        def load_k(item, j):
+            nonlocal kt
+            s = kt % NSK
+            if kt >= NSK:
+                yield from self.wait(f"empty_k{s}", ((kt // NSK) - 1) & 1)
+            self.b[f"raw_k{s}"].arrive(expect_tx=2)
+            for w in range(2):
+                self.load(f"K{s}.raw{w}", ("raw", (item, j)), f"raw_k{s}", 1)
+            kt += 1
+
+        for n_it in range(self.n_items):
+            if n_it > 0:
+                yield from self.wait("q_empty", (n_it - 1) & 1)
+            self.b["q_raw"].arrive(expect_tx=2)
+            for w in range(2):
+                self.load(f"Q.raw{w}", ("raw", n_it), "q_raw", 1)
+            yield
+            yield from load_k(n_it, 0)
+            for j in range(nk):
+                if j + 1 < nk:
+                    yield from load_k(n_it, j + 1)
+                for half in range(2):
+                    if vt >= 1:
+                        yield from self.wait(f"empty_v{half}", (vt - 1) & 1)
+                    self.b[f"raw_v{half}"].arrive(expect_tx=2)
+                    for w in range(2):
+                        self.load(f"V{half}.raw{w}", ("raw", (n_it, j, half)), f"raw_v{half}", 1)
+                    yield
+                vt += 1
+
+    def _convert(self, raw, out, tag):
+        assert self.smem.get(raw) == ("raw", tag), f"converter read {raw}={self.smem.get(raw)}, expected raw {tag}"
+        assert not self.reads.get(out), f"converter overwrote {out} while an MMA still reads it"
+        self.smem[out] = ("f16", tag)
+        self.smem[raw] = None
+
+    def converter(self, w):
+        kt = vt = 0
+        nk = self.nk
+
+        def conv_k(item, j):
+            nonlocal kt
+            s = kt % NSK
+            yield from self.wait(f"raw_k{s}", (kt // NSK) & 1)
+            yield
+            self._convert(f"K{s}.raw{w}", f"K{s}.{w}", (item, j))
+            self.b[f"full_k{s}"].arrive()
+            kt += 1
+
+        for n_it in range(self.n_items):
+            yield from self.wait("q_raw", n_it & 1)
+            yield
+            self._convert(f"Q.raw{w}", f"Q.{w}", n_it)
+            self.b["q"].arrive()
+            yield from conv_k(n_it, 0)
+            for j in range(nk):
+                if j + 1 < nk:
+                    yield from conv_k(n_it, j + 1)
+                for half in range(2):
+                    yield from self.wait(f"raw_v{half}", vt & 1)
+                    yield
+                    self._convert(f"V{half}.raw{w}", f"V{half}.{w}", (n_it, j, half))
+                    self.b[f"full_v{half}"].arrive()
+                vt += 1
+
+    def mma(self):
+        kt = st = 0
+        nk = self.nk
+        for n_it in range(self.n_items):
+            yield from self.wait("q", n_it & 1)
+            for j in range(nk + 1):
+                if j < nk:
+                    s = kt % NSK
+                    yield from self.wait(f"full_k{s}", (kt // NSK) & 1)
+                    if st + j >= 1:
+                        yield from self.wait("sfree", (st + j - 1) & 1)
+                    bufs = ["Q.0", "Q.1", f"K{s}.0", f"K{s}.1"]
+                    self.issue("QK", bufs=bufs, want=[("f16", n_it)] * 2 + [("f16", (n_it, j))] * 2, tag=(n_it, j))
+                    self.commit(f"empty_k{s}")
+                    self.commit("s")
+                    if j == nk - 1:
+                        self.commit("q_empty")
+                    kt += 1
+                if j >= 1:
+                    g = st + j - 1
+                    yield from self.wait("p", g & 1)
+                    if j == 1 and n_it > 0:
+                        yield from self.wait("o_free", (n_it - 1) & 1)
+                    for half in range(2):
+                        yield from self.wait(f"full_v{half}", g & 1)
+                        bufs = [f"V{half}.0", f"V{half}.1"]
+                        self.issue("PV", bufs=bufs, want=[("f16", (n_it, j - 1, half))] * 2, half=half,
+                                   tag=(n_it, j - 1))
+                        self.commit(f"empty_v{half}")
+                    self.commit("pv")
+                yield
+            st += nk
+            self.commit("last")
+        self.commit("fin")
+        yield from self.wait("fin", 0)
+
+    def run(self):
+        agents = ([self.producer(), self.mma(), self.converter(0), self.converter(1)]
+                  + [self.softmax(wg, w) for wg in range(2) for w in range(self.W)])
+        alive = list(range(len(agents)))
+        idle = 0
+        while alive:
+            r = self.rnd.random()
+            if self.tma and r < 0.25:
+                self.land(self.rnd.randrange(len(self.tma)))
+                idle = 0
+            elif self.pipe and r < 0.5:
+                self.execute()
+                idle = 0
+            else:
+                i = self.rnd.choice(alive)
+                try:
+                    next(agents[i])
+                except StopIteration:
+                    alive.remove(i)
+                idle += 1
+            assert idle < 100000, "deadlock: no role can make progress"
+        assert not self.tma and not self.pipe
+
+
+@pytest.mark.parametrize("nk,n_items", [(1, 1), (1, 3), (2, 1), (2, 4), (3, 3), (5, 2)])
+def test_fp8_attention_protocol_random_interleavings(nk, n_items):
+    for seed in range(60):
+        SimFP8(nk, n_items, seed * 1000 + nk * 10 + n_items + 7).run()
+
+
+def test_fp8_model_detects_early_operand_release():
+    """Arriving on the operand barrier before the conversion is written must
+    trip the model (the MMA would read raw codes)."""
+
+    class Early(SimFP8):
+        def _convert(self, raw, out, tag):
+            pass  # the converted tile is never written
+
+    with pytest.raises(AssertionError):
+        for seed in range(20):
+            Early(2, 2, seed).run()

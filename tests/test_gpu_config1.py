@@ -12,7 +12,8 @@ Two codecs are covered:
   * per-token: one scale per token row of K and of V (over H*D).
 
 GPU side: libwfk's codec (wf_kv_quant, wf_kv_dequant) and attention
-(wf_attn_fwd) on the bf16 runtime copies of q/k/v.  CPU side: the oracle's
+(wf_attn_fwd) on the bf16 runtime copies of q/k/v, and the same codes fed
+straight to the FP8-input attention (wf_attn_fwd with kv_dtype e4m3).  CPU side: the oracle's
 codec (its torch-CPU form, pinned bit for bit to the numpy restatement by
 the oracle tests; bit-exact bar for codes and scales) and the
 reference's attention call, F.scaled_dot_product_attention on CPU in fp32
@@ -71,6 +72,11 @@ def test_config1_per_tensor_round_trip(config1):
     out = K.attention(q.cuda().bfloat16(), deq[0], deq[1])
     rel = _rel(out.cpu(), ref)
     assert rel <= 1e-2, rel
+    # the same codes straight into the FP8-input attention (per-tensor scale)
+    c2 = codes.view(2, 1, CTX, H, D)
+    out8 = K.attention_fp8(q.cuda().bfloat16(), c2[0], c2[1], scale, scale, L.WF_SCALE_TENSOR)
+    rel8 = _rel(out8.cpu(), ref)
+    assert rel8 <= 1e-2, rel8
     assert L.status_take() == 0
 
 
@@ -81,6 +87,7 @@ def test_config1_per_token_round_trip(config1):
     q, k, v = config1
     deq_ref = []
     deq_gpu = []
+    pages = []
     for x in (k, v):
         x2 = x.reshape(CTX, H * D)
         codes_ref, scales_ref = o_codec.quant_per_token_torch(x2)
@@ -89,8 +96,14 @@ def test_config1_per_token_round_trip(config1):
         assert torch.equal(scales.cpu(), scales_ref)
         deq_ref.append(o_codec.dequant_torch(codes_ref, scales_ref, per_token=True))
         deq_gpu.append(K.kv_dequant(codes, scales, L.WF_SCALE_TOKEN).view(1, CTX, H, D))
+        pages.append((codes.view(1, CTX, H, D), scales))
     ref = _cpu_attention(q, deq_ref[0], deq_ref[1])
     out = K.attention(q.cuda().bfloat16(), deq_gpu[0], deq_gpu[1])
     rel = _rel(out.cpu(), ref)
     assert rel <= 1e-2, rel
+    # the same codes straight into the FP8-input attention (per-token scales)
+    (kc, ks), (vc, vs) = pages
+    out8 = K.attention_fp8(q.cuda().bfloat16(), kc, vc, ks, vs, L.WF_SCALE_TOKEN)
+    rel8 = _rel(out8.cpu(), ref)
+    assert rel8 <= 1e-2, rel8
     assert L.status_take() == 0

@@ -65,6 +65,79 @@ def test_attention_matches_oracle(Lq, Lk, H):
     assert _rel(_f32(out), ref) <= 1e-2
 
 
+FP8_CASES = [(130, 300, 2), (4680, 4680, 1), (256, 1000, 12), (5, 517, 3), (200, 700, 40), (2048, 100, 20)]
+
+
+def _fp8_pages(x2, mode):
+    """Codes and scales of a [rows, cols] bf16 page for an attention scale mode."""
+    from waveforcing_b200 import _lib as L
+
+    K = _kernels()
+    if mode == L.WF_SCALE_NONE:
+        return K.kv_quant(x2, L.WF_SCALE_NONE)[0], None
+    return K.kv_quant(x2, mode)
+
+
+@pytest.mark.parametrize("Lq,Lk,H", FP8_CASES)
+@pytest.mark.parametrize("mode", ["token", "tensor", "none"])
+def test_attention_fp8_kv_matches_oracle(Lq, Lk, H, mode):
+    """wf_attn_fwd on e4m3 K/V codes (kv_dtype WF_DTYPE_E4M3) against the fp64
+    oracle on the dequantised K/V (common.py:162): <= 1e-2 max relative."""
+    from waveforcing_b200 import _lib as L
+
+    K = _kernels()
+    m = {"token": L.WF_SCALE_TOKEN, "tensor": L.WF_SCALE_TENSOR, "none": L.WF_SCALE_NONE}[mode]
+    rng = np.random.default_rng(Lq * 3 + Lk + H)
+    q = o_codec.bf16_round(rng.standard_normal((Lq, H, 128)).astype(np.float32))
+    kscale = 1.0 if mode == "none" else 3.0
+    k = o_codec.bf16_round((rng.standard_normal((Lk, H, 128)) * kscale).astype(np.float32))
+    v = o_codec.bf16_round((rng.standard_normal((Lk, H, 128)) * kscale).astype(np.float32))
+    kc, ks = _fp8_pages(_bf16_gpu(k).view(Lk, H * 128), m)
+    vc, vs = _fp8_pages(_bf16_gpu(v).view(Lk, H * 128), m)
+    out = K.attention_fp8(_bf16_gpu(q)[None], kc.view(1, Lk, H, 128), vc.view(1, Lk, H, 128), ks, vs, m)
+    torch.cuda.synchronize()
+    per_token = mode == "token"
+    if mode == "none":
+        kd = o_codec.e4m3_decode(kc.cpu().numpy())
+        vd = o_codec.e4m3_decode(vc.cpu().numpy())
+    else:
+        kd = o_codec.dequant(kc.cpu().numpy(), ks.cpu().numpy() if per_token else ks.item(), per_token)
+        vd = o_codec.dequant(vc.cpu().numpy(), vs.cpu().numpy() if per_token else vs.item(), per_token)
+    ref = o_attn.sdpa_numpy(q, kd.reshape(Lk, H, 128), vd.reshape(Lk, H, 128))
+    assert _rel(_f32(out[0]), ref) <= 1e-2
+    from waveforcing_b200 import _lib as L2
+
+    assert L2.status_take() == 0
+
+
+def test_attention_fp8_strided_batch_and_large_logits():
+    """FP8 K/V views into a wider slab, batch 2, and late keys that dominate
+    (the lazy O rescale), against the bf16 kernel on the dequantised pages."""
+    from waveforcing_b200 import _lib as L
+
+    K = _kernels()
+    torch.manual_seed(3)
+    B, Lq, Lk, H = 2, 200, 700, 3
+    k = torch.randn(B, 900, H, 128, device=DEV)
+    k[:, 600:700] *= 6.0
+    v = torch.randn(B, 900, H, 128, device=DEV)
+    q = (torch.randn(B, Lq, H, 128, device=DEV) * 3).bfloat16()
+    kc, ks = K.kv_quant(k.bfloat16().view(-1, H * 128), L.WF_SCALE_TOKEN)
+    vc, vs = K.kv_quant(v.bfloat16().view(-1, H * 128), L.WF_SCALE_TOKEN)
+    kc, vc = kc.view(B, 900, H, 128), vc.view(B, 900, H, 128)
+    ks, vs = ks.view(B, 900), vs.view(B, 900)
+    # the first Lk tokens of each batch entry; scales follow the view as [B, Lk]
+    out = K.attention_fp8(q, kc[:, :Lk], vc[:, :Lk], ks[:, :Lk].contiguous(), vs[:, :Lk].contiguous(),
+                          L.WF_SCALE_TOKEN)
+    kd = K.kv_dequant(kc.reshape(-1, H * 128), ks.reshape(-1), L.WF_SCALE_TOKEN).view(B, 900, H, 128)
+    vd = K.kv_dequant(vc.reshape(-1, H * 128), vs.reshape(-1), L.WF_SCALE_TOKEN).view(B, 900, H, 128)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q.float().transpose(1, 2), kd[:, :Lk].float().transpose(1, 2), vd[:, :Lk].float().transpose(1, 2))
+    ref = ref.transpose(1, 2)
+    assert (out.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+    assert L.status_take() == 0
+
+
 def test_attention_golden(golden):
     K = _kernels()
     g = golden("sdpa.npz")

@@ -24,10 +24,17 @@
 // S is released as soon as both warpgroups have read it into registers, so
 // QK^T of tile j+1 runs on the tensor pipe while P_j is being computed; P is
 // written only after PV_{j-1} has completed.
+// FP8 K/V (attn_fwd_e4m3_kernel): K and V arrive as e4m3 codes with a scale
+// per token row (or one per tensor).  Each code tile lands by TMA in the upper
+// half of its operand slot and warps 2-3 expand it in place to f16 products
+// f16(e4m3(code) * scale) in the operand layout the bf16 path gets from TMA;
+// Q is converted bf16 -> f16 in place once per item and P is written as f16,
+// so both MMAs run kind::f16 on f16 operands with the same protocol.
 // Barrier phases run on per-CTA counters that continue across items (tiles
 // for the S/P/PV/K/V barriers, items for Q/last/o_free).  Every wait is
 // bounded (sm100.cuh mbar_wait); a timed-out wait raises the status word and
 // the CTA drains its in-flight work and exits.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -50,7 +57,8 @@ constexpr int VSLOT = KH * HD * 2;   // 32 KB: [d 0-63: 128 rows x 128 B][d 64-1
 constexpr int VHALF = VSLOT / 2;     // 16 KB
 constexpr int QHALF = QTILE / 2;     // 16 KB
 constexpr int BIG = QTILE + NSK * KTILE + 2 * VSLOT;  // 224 KB
-constexpr int NBARS = 1 + 2 * NSK + 4 + 9;
+constexpr int NBARS = 1 + 2 * NSK + 4 + 9 + (1 + NSK + 2);  // + FP8 arrival barriers (q_raw, raw_k, raw_v)
+constexpr int NCONV = 64;                                     // converter threads (warps 2-3), FP8 K/V only
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + BIG + NBARS * 8 + 2 * BM * 4 /*row exchange*/ + 16;
 constexpr int THREADS = 384;
 
@@ -91,11 +99,82 @@ __device__ __forceinline__ Item item_of(int it, int n_qt, int H) {
   return r;
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
-    attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,
-                         long long o_head, long long o_batch, int Lq, int Lk, int H, int n_items,
-                         float scale_log2) {
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t cvt_f16x2_e4m3x2(uint32_t two_codes) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(static_cast<uint16_t>(two_codes)));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Scale of one K or V token row as the conversion multiplies it (f16x2).
+// Rows past Lk (zero-filled by TMA) get 0.
+__device__ __forceinline__ uint32_t row_scale_f16x2(const float* __restrict__ scale, int mode, int bz, int Lk,
+                                                    int key) {
+  float sc = 1.f;
+  if (mode == WF_SCALE_TOKEN)
+    sc = key < Lk ? __ldg(scale + (long long)bz * Lk + key) : 0.f;
+  else if (mode == WF_SCALE_TENSOR)
+    sc = __ldg(scale);
+  return pack_f16x2(sc, sc);
+}
+
+// Expands `rows` e4m3 rows of 128 codes, TMA-landed (128-byte swizzle) in
+// the upper half of an operand slot at base + half_bytes, into f16 products
+// over both halves [d 0-63 | d 64-127] at base, in the layout a bf16/f16 TMA
+// load of the same tile produces.  Row r's codes and the upper half's row r
+// share one 128-byte line: the 8 lanes converting a row read all of it
+// before any of them writes (__syncwarp), and rows are split between warps.
+__device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int rows, int cw, int lane,
+                                             const float* __restrict__ scale, int mode, int bz, int Lk, int key0) {
+  const int c = lane & 7;
+  const int rows_per_warp = rows / 2;
+  for (int i = 0; i < rows_per_warp; i += 4) {
+    const int r = cw * rows_per_warp + i + (lane >> 3);
+    const uint32_t s2 = row_scale_f16x2(scale, mode, bz, Lk, key0 + r);
+    const uint4 raw = *reinterpret_cast<const uint4*>(base + half_bytes + r * 128 + ((c ^ (r & 7)) << 4));
+    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t h[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      h[2 * k] = hmul2(cvt_f16x2_e4m3x2(w4[k] & 0xFFFFu), s2);
+      h[2 * k + 1] = hmul2(cvt_f16x2_e4m3x2(w4[k] >> 16), s2);
+    }
+    __syncwarp();
+    uint8_t* row = base + (c >> 2) * half_bytes + r * 128;
+    const int q0 = (2 * (c & 3)) ^ (r & 7), q1 = (2 * (c & 3) + 1) ^ (r & 7);
+    *reinterpret_cast<uint4*>(row + (q0 << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(row + (q1 << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+  }
+}
+
+// bf16 -> f16 in place over `bytes` of shared memory (element order is kept,
+// so the swizzled layout is unchanged).
+__device__ __forceinline__ void convert_q_f16(uint8_t* base, int bytes, int t) {
+  for (int off = t * 16; off < bytes; off += NCONV * 16) {
+    uint4 v = *reinterpret_cast<const uint4*>(base + off);
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = pack_f16x2(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xFFFF0000u));
+    *reinterpret_cast<uint4*>(base + off) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <bool KV8>
+__device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                                          __nv_bfloat16* __restrict__ out, long long o_tok, long long o_head,
+                                          long long o_batch, int Lq, int Lk, int H, int n_items, float scale_log2,
+                                          const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+                                          int scale_mode) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
@@ -116,7 +195,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* q_empty = bar_last + 1;   // the current item's last QK^T has completed (Q may be reloaded)
   uint64_t* o_free = q_empty + 1;     // the epilogue has read O (the next item's first PV may overwrite it)
   uint64_t* bar_fin = o_free + 1;
-  float* xch = reinterpret_cast<float*>(bar_fin + 1);  // [2][BM]
+  uint64_t* q_raw = bar_fin + 1;      // FP8 K/V: the bf16 Q tile landed (bar_q: converted to f16)
+  uint64_t* raw_k = q_raw + 1;        // [NSK] FP8 K codes landed (full_k: converted)
+  uint64_t* raw_v = raw_k + NSK;      // [2]   FP8 V codes landed (full_v: converted)
+  float* xch = reinterpret_cast<float*>(raw_v + 2);  // [2][BM]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xch + 2 * BM);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -126,15 +208,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n_qt = (Lq + BM - 1) / BM;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_q, 1);
+    // With FP8 K/V the operand barriers complete on the converters' arrivals
+    // instead of TMA transaction bytes.
+    const uint32_t operand_arrivals = KV8 ? NCONV : 1;
+    mbar_init(bar_q, operand_arrivals);
     for (int s = 0; s < NSK; ++s) {
-      mbar_init(&full_k[s], 1);
+      mbar_init(&full_k[s], operand_arrivals);
       mbar_init(&empty_k[s], 1);
+      mbar_init(&raw_k[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&full_v[s], 1);
+      mbar_init(&full_v[s], operand_arrivals);
       mbar_init(&empty_v[s], 1);
+      mbar_init(&raw_v[s], 1);
     }
+    mbar_init(q_raw, 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_sfree, 256);
     mbar_init(bar_p, 256);
@@ -189,20 +277,27 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = kt % NSK;
         if (kt >= NSK && !mbar_wait(&empty_k[s], ((kt / NSK) - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) return false;
         uint8_t* dst = sK + s * KTILE;
-        mbar_arrive_expect_tx(&full_k[s], KTILE);
-        tma_load_4d(dst, &tmK, &full_k[s], 0, w.h, j * BN, w.bz);
-        tma_load_4d(dst + KH * 128, &tmK, &full_k[s], 0, w.h, j * BN + KH, w.bz);
-        tma_load_4d(dst + KHALF, &tmK, &full_k[s], 64, w.h, j * BN, w.bz);
-        tma_load_4d(dst + KHALF + KH * 128, &tmK, &full_k[s], 64, w.h, j * BN + KH, w.bz);
+        if constexpr (KV8) {
+          // 256 rows of 128 codes into the upper half; the converters expand them
+          mbar_arrive_expect_tx(&raw_k[s], BN * 128);
+          tma_load_4d(dst + KHALF, &tmK, &raw_k[s], 0, w.h, j * BN, w.bz);
+        } else {
+          mbar_arrive_expect_tx(&full_k[s], KTILE);
+          tma_load_4d(dst, &tmK, &full_k[s], 0, w.h, j * BN, w.bz);
+          tma_load_4d(dst + KH * 128, &tmK, &full_k[s], 0, w.h, j * BN + KH, w.bz);
+          tma_load_4d(dst + KHALF, &tmK, &full_k[s], 64, w.h, j * BN, w.bz);
+          tma_load_4d(dst + KHALF + KH * 128, &tmK, &full_k[s], 64, w.h, j * BN + KH, w.bz);
+        }
         ++kt;
         return true;
       };
       for (int it = blockIdx.x; run && it < n_items; it += gridDim.x, ++n_it) {
         const Item w = item_of(it, n_qt, H);
         if (n_it > 0 && !mbar_wait(q_empty, (n_it - 1) & 1, abort_flag, ST_ATTN_PRODUCER)) break;
-        mbar_arrive_expect_tx(bar_q, QTILE);
-        tma_load_4d(sQ, &tmQ, bar_q, 0, w.h, w.q0, w.bz);
-        tma_load_4d(sQ + QHALF, &tmQ, bar_q, 64, w.h, w.q0, w.bz);
+        uint64_t* qb = KV8 ? q_raw : bar_q;
+        mbar_arrive_expect_tx(qb, QTILE);
+        tma_load_4d(sQ, &tmQ, qb, 0, w.h, w.q0, w.bz);
+        tma_load_4d(sQ + QHALF, &tmQ, qb, 64, w.h, w.q0, w.bz);
         ++q_loads;
         if (!(run = load_k(w, 0))) break;
         for (int j = 0; run && j < nk; ++j) {
@@ -213,9 +308,14 @@ __global__ void __launch_bounds__(THREADS, 1)
               break;
             }
             uint8_t* dst = sV + half * VSLOT;
-            mbar_arrive_expect_tx(&full_v[half], VSLOT);
-            tma_load_4d(dst, &tmV, &full_v[half], 0, w.h, j * BN + half * KH, w.bz);
-            tma_load_4d(dst + VHALF, &tmV, &full_v[half], 64, w.h, j * BN + half * KH, w.bz);
+            if constexpr (KV8) {
+              mbar_arrive_expect_tx(&raw_v[half], KH * 128);
+              tma_load_4d(dst + VHALF, &tmV, &raw_v[half], 0, w.h, j * BN + half * KH, w.bz);
+            } else {
+              mbar_arrive_expect_tx(&full_v[half], VSLOT);
+              tma_load_4d(dst, &tmV, &full_v[half], 0, w.h, j * BN + half * KH, w.bz);
+              tma_load_4d(dst + VHALF, &tmV, &full_v[half], 64, w.h, j * BN + half * KH, w.bz);
+            }
             ++v_loads[half];
           }
           if (run) ++vt;
@@ -225,16 +325,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Let the copies this thread issued land before the CTA exits: the
         // last Q, the last NSK K tiles and the last load of each V half
         // (the phase of load n on a barrier is n & 1).
-        if (q_loads > 0) mbar_wait_drain(bar_q, (q_loads - 1) & 1, 200000000ull);
+        // (With FP8 K/V the copies complete on the raw barriers.)
+        if (q_loads > 0) mbar_wait_drain(KV8 ? q_raw : bar_q, (q_loads - 1) & 1, 200000000ull);
         for (int t = (kt > NSK ? kt - NSK : 0); t < kt; ++t)
-          mbar_wait_drain(&full_k[t % NSK], (t / NSK) & 1, 200000000ull);
+          mbar_wait_drain(KV8 ? &raw_k[t % NSK] : &full_k[t % NSK], (t / NSK) & 1, 200000000ull);
         for (int half = 0; half < 2; ++half)
-          if (v_loads[half] > 0) mbar_wait_drain(&full_v[half], (v_loads[half] - 1) & 1, 200000000ull);
+          if (v_loads[half] > 0)
+            mbar_wait_drain(KV8 ? &raw_v[half] : &full_v[half], (v_loads[half] - 1) & 1, 200000000ull);
       }
     } else if (warp == 1 && lane == 0) {
       // ----------------------------------------------------------------- MMA
-      constexpr uint32_t idesc_qk = make_idesc(1, FMT_BF16, FMT_BF16, 0, BM, BN);
-      constexpr uint32_t idesc_pv = make_idesc(1, FMT_BF16, FMT_BF16, 1, BM, HD);
+      constexpr uint32_t OPF = KV8 ? FMT_F16 : FMT_BF16;  // operand type (A and B alike)
+      constexpr uint32_t idesc_qk = make_idesc(1, OPF, OPF, 0, BM, BN);
+      constexpr uint32_t idesc_pv = make_idesc(1, OPF, OPF, 1, BM, HD);
       const uint32_t aQ = smem_u32(sQ);
       int kt = 0, st = 0, n_it = 0;  // K tiles, S tiles (= PV tiles) issued, items
       bool ok = true;
@@ -303,6 +406,48 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Nothing of ours may still be running when TMEM is released.
       umma_commit(bar_fin);
       mbar_wait_drain(bar_fin, 0, 200000000ull);
+    } else if (KV8 && (warp == 2 || warp == 3)) {
+      // ----------------------------------------------------------- converter
+      // The producer's order: per item Q, K_0, then per tile j K_{j+1} and the
+      // two halves of V_j.  Each converted tile is made visible to the
+      // tensor pipe (fence.proxy.async) before the arrival on its operand
+      // barrier.  kt / vt / n_it count like the producer's.
+      const int cw = warp - 2;
+      const int t = cw * 32 + lane;
+      int kt = 0, vt = 0, n_it = 0;
+      bool ok = true;
+      auto conv_k = [&](const Item& w, int j) -> bool {
+        const int s = kt % NSK;
+        if (!__all_sync(0xffffffffu, mbar_wait(&raw_k[s], (kt / NSK) & 1, abort_flag, ST_ATTN_CONVERT)))
+          return false;
+        convert_rows(sK + s * KTILE, KHALF, BN, cw, lane, k_scale, scale_mode, w.bz, Lk, j * BN);
+        fence_proxy_async_smem();
+        mbar_arrive(&full_k[s]);
+        ++kt;
+        return true;
+      };
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++n_it) {
+        const Item w = item_of(it, n_qt, H);
+        ok = __all_sync(0xffffffffu, mbar_wait(q_raw, n_it & 1, abort_flag, ST_ATTN_CONVERT));
+        if (!ok) break;
+        convert_q_f16(sQ, QTILE, t);
+        fence_proxy_async_smem();
+        mbar_arrive(bar_q);
+        if (!(ok = conv_k(w, 0))) break;
+        for (int j = 0; ok && j < nk; ++j) {
+          if (j + 1 < nk && !(ok = conv_k(w, j + 1))) break;
+          for (int half = 0; half < 2; ++half) {
+            if (!(ok = __all_sync(0xffffffffu,
+                                  mbar_wait(&raw_v[half], vt & 1, abort_flag, ST_ATTN_CONVERT))))
+              break;
+            convert_rows(sV + half * VSLOT, VHALF, KH, cw, lane, v_scale, scale_mode, w.bz, Lk,
+                         j * BN + half * KH);
+            fence_proxy_async_smem();
+            mbar_arrive(&full_v[half]);
+          }
+          if (ok) ++vt;
+        }
+      }
     }
     __syncwarp();
     teardown();
@@ -381,7 +526,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             pr.y = ex2_approx(x.y);
           }
           sum2 = fadd2(sum2, pr);
-          pk[i] = pack_bf16x2(pr.x, pr.y);
+          pk[i] = KV8 ? pack_f16x2(pr.x, pr.y) : pack_bf16x2(pr.x, pr.y);
         }
         const float sum = sum2.x + sum2.y;
         const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
@@ -460,6 +605,26 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,
+                         long long o_head, long long o_batch, int Lq, int Lk, int H, int n_items,
+                         float scale_log2) {
+  attn_body<false>(tmQ, tmK, tmV, out, o_tok, o_head, o_batch, Lq, Lk, H, n_items, scale_log2, nullptr, nullptr,
+                   WF_SCALE_NONE);
+}
+
+// K/V as e4m3 codes [batch, Lk, H, 128] with per-token (k_scale[bz * Lk +
+// key]), per-tensor (k_scale[0]) or no scales.
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_fwd_e4m3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,
+                         long long o_head, long long o_batch, int Lq, int Lk, int H, int n_items, float scale_log2,
+                         const float* __restrict__ k_scale, const float* __restrict__ v_scale, int scale_mode) {
+  attn_body<true>(tmQ, tmK, tmV, out, o_tok, o_head, o_batch, Lq, Lk, H, n_items, scale_log2, k_scale, v_scale,
+                  scale_mode);
+}
+
 // Tensor map over a [batch, L, H, 128] bf16 tensor with {batch, token, head}
 // element strides; box = 64 head-dim columns x 1 head x 128 tokens.
 static int make_qkv_map(CUtensorMap* m, const void* p, int batch, int L, int H, const int64_t* st) {
@@ -468,6 +633,16 @@ static int make_qkv_map(CUtensorMap* m, const void* p, int batch, int L, int H, 
                             (uint64_t)(batch > 1 ? st[0] : st[1] * (int64_t)L) * 2};
   const uint32_t box[4] = {64, 1, 128, 1};
   return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, p, gdim, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Tensor map over [batch, L, H, 128] e4m3 codes (one byte per element) with
+// {batch, token, head} strides in bytes; box = 128 codes x 1 head x `rows`
+// tokens (one 128-byte swizzled line per token).
+static int make_code_map(CUtensorMap* m, const void* p, int batch, int L, int H, const int64_t* st, int rows) {
+  const uint64_t gdim[4] = {(uint64_t)HD, (uint64_t)H, (uint64_t)L, (uint64_t)batch};
+  const uint64_t gstr[3] = {(uint64_t)st[2], (uint64_t)st[1], (uint64_t)(batch > 1 ? st[0] : st[1] * (int64_t)L)};
+  const uint32_t box[4] = {128, 1, (uint32_t)rows, 1};
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, p, gdim, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 static bool strides_ok(const int64_t* st, int batch) {
@@ -488,8 +663,15 @@ extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o,
   using namespace wfk;
   using namespace wfk::attn;
   if (D != HD) return fail(WF_ERR_UNSUPPORTED, "wf_attn_fwd: head_dim %d unsupported (only 128)", D);
-  if (kv_dtype != WF_DTYPE_BF16 || k_scale != nullptr || v_scale != nullptr || scale_mode != WF_SCALE_NONE)
-    return fail(WF_ERR_UNSUPPORTED, "wf_attn_fwd: K/V must be bf16 (dequantise FP8 pages with wf_kv_dequant)");
+  const bool kv8 = kv_dtype == WF_DTYPE_E4M3;
+  if (kv_dtype != WF_DTYPE_BF16 && !kv8)
+    return fail(WF_ERR_UNSUPPORTED, "wf_attn_fwd: kv_dtype %d unsupported (bf16 or e4m3)", kv_dtype);
+  if (!kv8 && (k_scale != nullptr || v_scale != nullptr || scale_mode != WF_SCALE_NONE))
+    return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: bf16 K/V take no scales (k_scale/v_scale NULL, WF_SCALE_NONE)");
+  if (kv8 && scale_mode != WF_SCALE_NONE && scale_mode != WF_SCALE_TENSOR && scale_mode != WF_SCALE_TOKEN)
+    return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: unknown scale_mode %d", scale_mode);
+  if (kv8 && scale_mode != WF_SCALE_NONE && (!k_scale || !v_scale))
+    return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: e4m3 K/V with scales need k_scale and v_scale");
   if (batch < 1 || Lq < 1 || Lk < 1 || H < 1 || H > 65535 || batch > 65535)
     return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: bad sizes batch=%d Lq=%d Lk=%d H=%d", batch, Lq, Lk, H);
   if (!q || !k || !v || !o) return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: null tensor pointer");
@@ -498,20 +680,30 @@ extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o,
   if (!strides_ok(q_stride, batch) || !strides_ok(k_stride, batch) || !strides_ok(v_stride, batch) ||
       !strides_ok(o_stride, batch))
     return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: strides must be positive multiples of 8 elements");
+  if (kv8)
+    for (int i = 0; i < 3; ++i)
+      if (k_stride[i] % 16 || v_stride[i] % 16)
+        return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: e4m3 K/V strides must be multiples of 16 bytes");
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
     return fail(WF_ERR_INVALID_ARG, "wf_attn_fwd: softmax_scale must be positive");
 
   CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_qkv_map(&tq, q, batch, Lq, H, q_stride)) != WF_OK) return rc;
-  if ((rc = make_qkv_map(&tk, k, batch, Lk, H, k_stride)) != WF_OK) return rc;
-  if ((rc = make_qkv_map(&tv, v, batch, Lk, H, v_stride)) != WF_OK) return rc;
+  if (kv8) {
+    if ((rc = make_code_map(&tk, k, batch, Lk, H, k_stride, BN)) != WF_OK) return rc;
+    if ((rc = make_code_map(&tv, v, batch, Lk, H, v_stride, KH)) != WF_OK) return rc;
+  } else {
+    if ((rc = make_qkv_map(&tk, k, batch, Lk, H, k_stride)) != WF_OK) return rc;
+    if ((rc = make_qkv_map(&tv, v, batch, Lk, H, v_stride)) != WF_OK) return rc;
+  }
 
   static thread_local int configured_dev = -1;
   int dev = 0;
   WFK_CUDA_TRY(cudaGetDevice(&dev));
   if (configured_dev != dev) {
     WFK_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    WFK_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_e4m3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     configured_dev = dev;
   }
   const long long items = (long long)((Lq + BM - 1) / BM) * H * batch;
@@ -531,9 +723,14 @@ extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o,
     grid = (items + per - 1) / per;
   }
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
-  attn_fwd_bf16_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
-      tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
-      (long long)o_stride[0], Lq, Lk, H, (int)items, scale_log2);
+  if (kv8)
+    attn_fwd_e4m3_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+        tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
+        (long long)o_stride[0], Lq, Lk, H, (int)items, scale_log2, k_scale, v_scale, scale_mode);
+  else
+    attn_fwd_bf16_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+        tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
+        (long long)o_stride[0], Lq, Lk, H, (int)items, scale_log2);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

@@ -16,6 +16,7 @@ enum StatusCode : uint32_t {
   ST_GEMM_EPILOGUE = 1u << 5,
   ST_FLAG_TIMEOUT = 1u << 6,
   ST_DRAIN_TIMEOUT = 1u << 7,
+  ST_ATTN_CONVERT = 1u << 8,
 };
 
 static __device__ unsigned int g_status;  // one word per translation unit

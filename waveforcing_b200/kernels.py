@@ -78,6 +78,48 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: 
     return out
 
 
+def attention_fp8(q: torch.Tensor, k_codes: torch.Tensor, v_codes: torch.Tensor, k_scale: torch.Tensor | None,
+                  v_scale: torch.Tensor | None, scale_mode: int = L.WF_SCALE_TOKEN, softmax_scale: float | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention over FP8 K/V pages: q bf16 [B, Lq, H, 128]; k_codes/v_codes
+    uint8 e4m3 codes [B, Lk, H, 128]; scales f32 per token row [B, Lk]
+    (WF_SCALE_TOKEN), one per tensor [1] (WF_SCALE_TENSOR) or none.  The
+    kernel expands the codes to f16 products code * scale in shared memory and
+    runs both contractions on f16 operands (|q| and |k|, |v| below 65504)."""
+    if q.dtype != torch.bfloat16 or k_codes.dtype != torch.uint8 or v_codes.dtype != torch.uint8:
+        raise TypeError("attention_fp8: q must be bfloat16, k/v uint8 e4m3 codes")
+    for t in (q, k_codes, v_codes):
+        if t.stride(-1) != 1:
+            raise ValueError("attention_fp8: last dim must be contiguous")
+    B, Lq, H, D, qs = _strides_bthd(q)
+    Bk, Lk, Hk, Dk, ks = _strides_bthd(k_codes)
+    Bv, Lv, Hv, Dv, vs = _strides_bthd(v_codes)
+    if (Bk, Hk, Dk) != (B, H, D) or (Bv, Lv, Hv, Dv) != (B, Lk, H, D):
+        raise ValueError(f"attention_fp8: shape mismatch q{tuple(q.shape)} k{tuple(k_codes.shape)} "
+                         f"v{tuple(v_codes.shape)}")
+    need = {L.WF_SCALE_TOKEN: B * Lk, L.WF_SCALE_TENSOR: 1, L.WF_SCALE_NONE: 0}.get(scale_mode)
+    _check(need is not None, "attention_fp8: unknown scale_mode")
+    if need:
+        _check(all(t is not None and t.dtype == torch.float32 and t.is_contiguous() and t.numel() >= need
+                   for t in (k_scale, v_scale)),
+               "attention_fp8: k_scale/v_scale must be contiguous f32 with B*Lk (token) or 1 (tensor) elements")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    _check(out.shape == q.shape and out.dtype == torch.bfloat16 and out.stride(-1) == 1,
+           "attention_fp8: out must be bf16 with q's shape and a contiguous last dim")
+    _need_cuda(q, k_codes, v_codes, out)
+    _, _, _, _, os_ = _strides_bthd(out)
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    L.check(
+        L.lib().wf_attn_fwd(q.data_ptr(), k_codes.data_ptr(), v_codes.data_ptr(), out.data_ptr(), B, Lq, Lk, H, D,
+                            L.i64_array(qs), L.i64_array(ks), L.i64_array(vs), L.i64_array(os_),
+                            L.WF_DTYPE_E4M3, k_scale.data_ptr() if need else None,
+                            v_scale.data_ptr() if need else None, scale_mode, scale, _stream()),
+        "wf_attn_fwd(e4m3)",
+    )
+    return out
+
+
 def _as_rows(x: torch.Tensor):
     """View x as [rows, cols] with a row stride (last dim contiguous)."""
     if x.dim() == 1:
