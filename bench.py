@@ -550,16 +550,15 @@ def run_gpu_arm(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.tolist()
 
+    # ---------------- device-resident run (value)
+    gn = torch.Generator(device="cpu").manual_seed(ecfg.seed)
+    noise_cpu = torch.randn((cfg.in_ch, ecfg.num_frames, cfg.lat_h, cfg.lat_w), generator=gn).to(torch.bfloat16)
     if args.trace:
         trace_ticks(args, make_engine, noise_cpu, fill, dev, rank)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
         return
-
-    # ---------------- device-resident run (value)
-    gn = torch.Generator(device="cpu").manual_seed(ecfg.seed)
-    noise_cpu = torch.randn((cfg.in_ch, ecfg.num_frames, cfg.lat_h, cfg.lat_w), generator=gn).to(torch.bfloat16)
     eng = make_engine(noise_cpu.to(dev))
     for t in range(fill + args.warmup):
         eng.tick(t)

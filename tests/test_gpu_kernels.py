@@ -112,7 +112,10 @@ def test_attention_fp8_kv_matches_oracle(Lq, Lk, H, mode):
 
 def test_attention_fp8_strided_batch_and_large_logits():
     """FP8 K/V views into a wider slab, batch 2, and late keys that dominate
-    (the lazy O rescale), against the bf16 kernel on the dequantised pages."""
+    (the lazy O rescale), against fp32 SDPA on the exactly dequantised pages
+    (e4m3(code) * scale in f32, common.py:162).  The logits here spread over
+    tens of units, so a bf16 rounding of K (as wf_kv_dequant writes it) would
+    move them more than the kernel's f16 products do: the reference keeps f32."""
     from waveforcing_b200 import _lib as L
 
     K = _kernels()
@@ -129,8 +132,8 @@ def test_attention_fp8_strided_batch_and_large_logits():
     # the first Lk tokens of each batch entry; scales follow the view as [B, Lk]
     out = K.attention_fp8(q, kc[:, :Lk], vc[:, :Lk], ks[:, :Lk].contiguous(), vs[:, :Lk].contiguous(),
                           L.WF_SCALE_TOKEN)
-    kd = K.kv_dequant(kc.reshape(-1, H * 128), ks.reshape(-1), L.WF_SCALE_TOKEN).view(B, 900, H, 128)
-    vd = K.kv_dequant(vc.reshape(-1, H * 128), vs.reshape(-1), L.WF_SCALE_TOKEN).view(B, 900, H, 128)
+    kd = kc.view(torch.float8_e4m3fn).float() * ks[:, :, None, None]
+    vd = vc.view(torch.float8_e4m3fn).float() * vs[:, :, None, None]
     ref = torch.nn.functional.scaled_dot_product_attention(
         q.float().transpose(1, 2), kd[:, :Lk].float().transpose(1, 2), vd[:, :Lk].float().transpose(1, 2))
     ref = ref.transpose(1, 2)

@@ -116,31 +116,48 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   return r;
 }
 
-// Scale of one K or V token row as the conversion multiplies it (f16x2).
-// Rows past Lk (zero-filled by TMA) get 0.
-__device__ __forceinline__ uint32_t row_scale_f16x2(const float* __restrict__ scale, int mode, int bz, int Lk,
-                                                    int key) {
-  float sc = 1.f;
-  if (mode == WF_SCALE_TOKEN)
-    sc = key < Lk ? __ldg(scale + (long long)bz * Lk + key) : 0.f;
-  else if (mode == WF_SCALE_TENSOR)
-    sc = __ldg(scale);
-  return pack_f16x2(sc, sc);
+// Row scales of one K tile or V half, fetched before the converters wait for
+// the codes so the loads overlap that wait: warp cw converts rows
+// [cw * rpw, (cw + 1) * rpw) of the tile, and lane l holds the scales of its
+// rows l, l + 32, l + 64 and l + 96 (rows past rpw or past Lk read 0; with
+// per-tensor or no scales every slot holds the one value).
+template <int NS>
+__device__ __forceinline__ void fetch_row_scales(float (&sv)[NS], const float* __restrict__ scale, int mode,
+                                                 int bz, int Lk, int key0, int rpw, int cw, int lane) {
+#pragma unroll
+  for (int c = 0; c < NS; ++c) {
+    const int r = c * 32 + lane;
+    const int key = key0 + cw * rpw + r;
+    float sc = 1.f;
+    if (mode == WF_SCALE_TOKEN)
+      sc = (r < rpw && key < Lk) ? __ldg(scale + (long long)bz * Lk + key) : 0.f;
+    else if (mode == WF_SCALE_TENSOR)
+      sc = __ldg(scale);
+    sv[c] = sc;
+  }
 }
 
-// Expands `rows` e4m3 rows of 128 codes, TMA-landed (128-byte swizzle) in
-// the upper half of an operand slot at base + half_bytes, into f16 products
-// over both halves [d 0-63 | d 64-127] at base, in the layout a bf16/f16 TMA
-// load of the same tile produces.  Row r's codes and the upper half's row r
-// share one 128-byte line: the 8 lanes converting a row read all of it
-// before any of them writes (__syncwarp), and rows are split between warps.
-__device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int rows, int cw, int lane,
-                                             const float* __restrict__ scale, int mode, int bz, int Lk, int key0) {
+// Expands rpw e4m3 rows per converter warp (2 * rpw rows of 128 codes),
+// TMA-landed (128-byte swizzle) in the upper half of an operand slot at
+// base + half_bytes, into f16 products over both halves [d 0-63 | d 64-127]
+// at base, in the layout a 16-bit TMA load of the same tile produces.  Row
+// r's codes and the upper half's row r share one 128-byte line: the 8 lanes
+// converting a row read all of it before any of them writes (__syncwarp),
+// and rows are split between the two warps.  A warp converts 4 rows per
+// step; their scales come from the lanes that fetched them (the four rows
+// of a step lie in one group of 32, so the register index is static).
+template <int NS>
+__device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int cw, int lane, const float (&sv)[NS]) {
+  constexpr int RPW = NS * 32;
   const int c = lane & 7;
-  const int rows_per_warp = rows / 2;
-  for (int i = 0; i < rows_per_warp; i += 4) {
-    const int r = cw * rows_per_warp + i + (lane >> 3);
-    const uint32_t s2 = row_scale_f16x2(scale, mode, bz, Lk, key0 + r);
+#pragma unroll
+  for (int g = 0; g < NS; ++g) {
+#pragma unroll 2
+  for (int i = 0; i < 32; i += 4) {
+    const int rl = g * 32 + i + (lane >> 3);  // row within this warp's share
+    const int r = cw * RPW + rl;
+    const float sc = __shfl_sync(0xffffffffu, sv[g], rl & 31);
+    const uint32_t s2 = pack_f16x2(sc, sc);
     const uint4 raw = *reinterpret_cast<const uint4*>(base + half_bytes + r * 128 + ((c ^ (r & 7)) << 4));
     const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
     uint32_t h[8];
@@ -154,6 +171,7 @@ __device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int 
     const int q0 = (2 * (c & 3)) ^ (r & 7), q1 = (2 * (c & 3) + 1) ^ (r & 7);
     *reinterpret_cast<uint4*>(row + (q0 << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4*>(row + (q1 << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+  }
   }
 }
 
@@ -418,9 +436,11 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
       bool ok = true;
       auto conv_k = [&](const Item& w, int j) -> bool {
         const int s = kt % NSK;
+        float sv[BN / 64];  // this lane's 4 of the warp's 128 rows
+        fetch_row_scales(sv, k_scale, scale_mode, w.bz, Lk, j * BN, BN / 2, cw, lane);
         if (!__all_sync(0xffffffffu, mbar_wait(&raw_k[s], (kt / NSK) & 1, abort_flag, ST_ATTN_CONVERT)))
           return false;
-        convert_rows(sK + s * KTILE, KHALF, BN, cw, lane, k_scale, scale_mode, w.bz, Lk, j * BN);
+        convert_rows(sK + s * KTILE, KHALF, cw, lane, sv);
         fence_proxy_async_smem();
         mbar_arrive(&full_k[s]);
         ++kt;
@@ -437,11 +457,12 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
         for (int j = 0; ok && j < nk; ++j) {
           if (j + 1 < nk && !(ok = conv_k(w, j + 1))) break;
           for (int half = 0; half < 2; ++half) {
+            float sv[KH / 64];  // this lane's 2 of the warp's 64 rows
+            fetch_row_scales(sv, v_scale, scale_mode, w.bz, Lk, j * BN + half * KH, KH / 2, cw, lane);
             if (!(ok = __all_sync(0xffffffffu,
                                   mbar_wait(&raw_v[half], vt & 1, abort_flag, ST_ATTN_CONVERT))))
               break;
-            convert_rows(sV + half * VSLOT, VHALF, KH, cw, lane, v_scale, scale_mode, w.bz, Lk,
-                         j * BN + half * KH);
+            convert_rows(sV + half * VSLOT, VHALF, cw, lane, sv);
             fence_proxy_async_smem();
             mbar_arrive(&full_v[half]);
           }
