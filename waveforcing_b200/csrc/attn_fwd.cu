@@ -144,34 +144,46 @@ __device__ __forceinline__ void fetch_row_scales(float (&sv)[NS], const float* _
 // r's codes and the upper half's row r share one 128-byte line: the 8 lanes
 // converting a row read all of it before any of them writes (__syncwarp),
 // and rows are split between the two warps.  A warp converts 4 rows per
-// step; their scales come from the lanes that fetched them (the four rows
-// of a step lie in one group of 32, so the register index is static).
+// step and STEPS steps per batch: the batch's loads are issued together and
+// one __syncwarp separates all its reads from all its writes.  Scales come
+// from the lanes that fetched them (a batch's rows lie in one group of 32,
+// so the register index is static).
 template <int NS>
 __device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int cw, int lane, const float (&sv)[NS]) {
   constexpr int RPW = NS * 32;
+  constexpr int STEPS = 2;  // 4 spills under warpgroup 0's 72-register budget
+  static_assert(32 % (4 * STEPS) == 0, "a batch must not cross a group of 32 rows");
   const int c = lane & 7;
 #pragma unroll
   for (int g = 0; g < NS; ++g) {
-#pragma unroll 2
-  for (int i = 0; i < 32; i += 4) {
-    const int rl = g * 32 + i + (lane >> 3);  // row within this warp's share
-    const int r = cw * RPW + rl;
-    const float sc = __shfl_sync(0xffffffffu, sv[g], rl & 31);
-    const uint32_t s2 = pack_f16x2(sc, sc);
-    const uint4 raw = *reinterpret_cast<const uint4*>(base + half_bytes + r * 128 + ((c ^ (r & 7)) << 4));
-    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-    uint32_t h[8];
+#pragma unroll 1
+    for (int i0 = 0; i0 < 32; i0 += 4 * STEPS) {
+      uint32_t h[STEPS][8];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      h[2 * k] = hmul2(cvt_f16x2_e4m3x2(w4[k] & 0xFFFFu), s2);
-      h[2 * k + 1] = hmul2(cvt_f16x2_e4m3x2(w4[k] >> 16), s2);
+      for (int t = 0; t < STEPS; ++t) {
+        const int rl = g * 32 + i0 + 4 * t + (lane >> 3);  // row within this warp's share
+        const int r = cw * RPW + rl;
+        const float sc = __shfl_sync(0xffffffffu, sv[g], rl & 31);
+        const uint32_t s2 = pack_f16x2(sc, sc);
+        const uint4 raw = *reinterpret_cast<const uint4*>(base + half_bytes + r * 128 + ((c ^ (r & 7)) << 4));
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          h[t][2 * k] = hmul2(cvt_f16x2_e4m3x2(w4[k] & 0xFFFFu), s2);
+          h[t][2 * k + 1] = hmul2(cvt_f16x2_e4m3x2(w4[k] >> 16), s2);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int t = 0; t < STEPS; ++t) {
+        const int r = cw * RPW + g * 32 + i0 + 4 * t + (lane >> 3);
+        uint8_t* row = base + (c >> 2) * half_bytes + r * 128;
+        const int q0 = (2 * (c & 3)) ^ (r & 7), q1 = (2 * (c & 3) + 1) ^ (r & 7);
+        *reinterpret_cast<uint4*>(row + (q0 << 4)) = make_uint4(h[t][0], h[t][1], h[t][2], h[t][3]);
+        *reinterpret_cast<uint4*>(row + (q1 << 4)) = make_uint4(h[t][4], h[t][5], h[t][6], h[t][7]);
+      }
+      // the next batch reads other rows' lines, which this batch does not write
     }
-    __syncwarp();
-    uint8_t* row = base + (c >> 2) * half_bytes + r * 128;
-    const int q0 = (2 * (c & 3)) ^ (r & 7), q1 = (2 * (c & 3) + 1) ^ (r & 7);
-    *reinterpret_cast<uint4*>(row + (q0 << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(row + (q1 << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
-  }
   }
 }
 
