@@ -46,6 +46,15 @@ FRAMES_PER_TICK = 12  # 3 latent frames -> 12 output frames per chunk
 METRIC = "steady FPS p50 (1.3B 5-step wavefront, 399 latent frames, 480x832)"
 
 
+def metric_name(args) -> str:
+    """The metric of this run: BASELINE's name for its default workload, the
+    same form naming the preset and step count otherwise."""
+    S = len(args.denoise_steps.split(","))
+    if args.preset == "1.3b" and S == 5:
+        return METRIC
+    return f"steady FPS p50 ({args.preset.upper()} {S}-step wavefront, 399 latent frames, 480x832)"
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -289,8 +298,8 @@ def gpu_config1(cfg, dev, reps: int = 10) -> dict:
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    return {"gpu_ms": ms, "what": "BASELINE config 1 layer: per-tensor FP8 round trip of stack(K,V) + attention, "
-                                  "q 4680 x K/V 14040 x 12 heads (bf16 on the GPU, fp32 on the host)"}
+    return {"gpu_ms": ms, "what": f"BASELINE config 1 layer: per-tensor FP8 round trip of stack(K,V) + attention, "
+                                  f"q {cfg.tokens_per_chunk} x K/V {Lk} x {H} heads (bf16 on the GPU, fp32 on the host)"}
 
 
 def bench_config(args, world: int) -> dict:
@@ -337,7 +346,7 @@ def run_reference_arm(args):
             f"{cfg.tokens_per_chunk}x{3 * cfg.tokens_per_chunk}x{cfg.heads} heads, one dim x dim linear); value = "
             f"steady FPS of the tick at the measured rates (tick {m['tick_s']:.1f} s)")
     line = {
-        "impl": "reference", "metric": METRIC, "value": m["fps"], "unit": "FPS", "n_gpus": args.gpus,
+        "impl": "reference", "metric": metric_name(args), "value": m["fps"], "unit": "FPS", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(walls),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (config 1 inputs, seed 0)", "config": bench_config(args, world),
@@ -429,7 +438,7 @@ def run_reference_gpu_arm(args):
         steady = tick_ms[12:-4]
         p50 = statistics.median(steady)
         print(json.dumps({
-            "impl": "reference-gpu", "metric": METRIC, "value": FRAMES_PER_TICK * 1000.0 / p50, "unit": "FPS",
+            "impl": "reference-gpu", "metric": metric_name(args), "value": FRAMES_PER_TICK * 1000.0 / p50, "unit": "FPS",
             "n_gpus": world, "tick_ms_p50": p50, "higher_is_better": True,
             "dit_fps": {"value": 4 * nf / wall, "unit": "FPS", "diffusion_s": wall},
             "ticks": len(tick_ms), "steady_ticks": len(steady), "dtype": "bf16", "data": "synthetic",
@@ -670,7 +679,7 @@ def run_gpu_arm(args):
             config1["cpu_ms"] = cpu["config1_layer_ms"]
             config1["cpu_over_gpu"] = cpu["config1_layer_ms"] / config1["gpu_ms"]
         line = {
-            "metric": METRIC, "value": fps, "unit": "FPS", "n_gpus": args.gpus, "steps": args.steps,
+            "metric": metric_name(args), "value": fps, "unit": "FPS", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "tick_ms_p50": p50,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init N(0,0.02) weights, N(0,1) text, seed-0 Gaussian noise)",
