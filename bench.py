@@ -70,7 +70,7 @@ def parse():
     ap.add_argument("--denoise-steps", default="1000,800,600,400,200")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--kernel", default=None,
-                    choices=["attn", "attn8", "gemm", "codec", "dequant", "assemble", "publish"],
+                    choices=["attn", "attn8", "gemm", "codec", "dequant", "assemble", "publish", "qkpub"],
                     help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
     ap.add_argument("--kv-len", type=int, default=0,
@@ -800,6 +800,40 @@ def run_kernel_bench(args):
                     lib_diff = float((a8.float() - o.float()).abs().max() / o.float().abs().max())
         work, unit, bound = 4.0 * T * Lk * H * D / 1e12, "TFLOP/s", "tensor"
         name = f"attn_fwd e4m3 K/V (per-token scales) q{T} kv{Lk} h{H}"
+    elif args.kernel == "qkpub":
+        # the steady tick's QKV row kernel at N=1: six stages' rows (5 denoise
+        # + store) in one launch; stages 1..4 publish to the stages below
+        # them, the store to all five (per-token FP8, local slots)
+        S, dim, hd = 6, cfg.dim, cfg.head_dim
+        ndst = [0, 1, 2, 3, 4, 5]
+        rows = S * T
+        set_bytes = rows * 3 * dim * 2 + 3 * rows * dim * 2 + sum(ndst) * 2 * T * (dim + 4)
+        wq = (torch.randn(dim, device=dev, generator=g) * 0.5 + 1).bfloat16()
+        wk = (torch.randn(dim, device=dev, generator=g) * 0.5 + 1).bfloat16()
+        ang = torch.rand(rows, hd // 2, device=dev, generator=g) * 6.2831853
+        cos, sin = torch.cos(ang), torch.sin(ang)
+        for _ in range(n_sets(set_bytes)):
+            qkv = torch.randn(rows, 3 * dim, device=dev, generator=g).bfloat16()
+            slots = [[(torch.empty(T, dim, device=dev, dtype=torch.uint8),
+                       torch.empty(T, dim, device=dev, dtype=torch.uint8),
+                       torch.empty(T, device=dev), torch.empty(T, device=dev)) for _ in range(n)] for n in ndst]
+            pub = [[tuple(t.data_ptr() for t in d) for d in st] for st in slots]
+            keep = (qkv, slots)
+            fns.append(lambda qkv=qkv, pub=pub, keep=keep: kernels.qk_norm_rope_publish(
+                qkv, dim, wq, wk, cos, sin, hd, T, 1e-6, pub))
+            if args.library:
+                def unfused(qkv=qkv, slots=slots):
+                    q, k, ku = kernels.qk_norm_rope(qkv, dim, wq, wk, cos, sin, hd, T, 1e-6)
+                    for st, lst in enumerate(slots):
+                        if lst:
+                            r = slice(st * T, (st + 1) * T)
+                            kernels.kv_quant_publish(k[r], qkv[r, 2 * dim:], *[[d[i].data_ptr() for d in lst]
+                                                                                for i in range(4)])
+                lib_fns.append(unfused)
+        # read qkv; write q, k, un-roped k; codes + scales of K and V per destination
+        work = (rows * 3 * dim * 2 + 3 * rows * dim * 2 + sum(ndst) * 2 * T * (dim + 4)) / 1e9
+        unit, bound = "GB/s", "hbm"
+        name = f"qk_norm_rope_publish {rows}x{3 * dim} (6 stages, {sum(ndst)} FP8 destinations)"
     elif args.kernel == "gemm":
         set_bytes = T * cfg.dim + cfg.ffn * cfg.dim + 2 * T * cfg.ffn
         for _ in range(n_sets(set_bytes)):
@@ -899,8 +933,9 @@ def run_kernel_bench(args):
     library = None
     if lib_fns:
         lms = graph_ms(lib_fns)
-        library = {"name": ("per-token dequant to bf16 + bf16 wf_attn_fwd" if args.kernel == "attn8"
-                            else "torch SDPA, default dispatch (cuDNN on B200)"), "ms": lms,
+        library = {"name": {"attn8": "per-token dequant to bf16 + bf16 wf_attn_fwd",
+                            "qkpub": "wf_qk_norm_rope + wf_kv_quant_publish per stage (the unfused pair)"}.get(
+                                args.kernel, "torch SDPA, default dispatch (cuDNN on B200)"), "ms": lms,
                    "achieved": work / (lms * 1e-3), "max_abs_diff_vs_wf": lib_diff,
                    # the product kernel once more after the library leg, to expose clock drift
                    "wf_ms_after": graph_ms(fns)}
