@@ -158,6 +158,13 @@ __device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int 
   for (int g = 0; g < NS; ++g) {
 #pragma unroll 1
     for (int i0 = 0; i0 < 32; i0 += 4 * STEPS) {
+      // 16-byte stores are serviced 8 lanes (one row) at a time.  Lanes
+      // c < 4 write their even output chunk first and lanes c >= 4 (the
+      // other half, 32 or 16 KB away, so at the same banks) their odd one:
+      // each group of 8 stores then covers all 8 bank groups.  The order is
+      // chosen on the input words (codes 0-7 make the even chunk, 8-15 the
+      // odd one), and the odd chunk is the even one ^ 1 (2k + 1 = 2k ^ 1).
+      const int hi = c >> 2;
       uint32_t h[STEPS][8];
 #pragma unroll
       for (int t = 0; t < STEPS; ++t) {
@@ -166,7 +173,7 @@ __device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int 
         const float sc = __shfl_sync(0xffffffffu, sv[g], rl & 31);
         const uint32_t s2 = pack_f16x2(sc, sc);
         const uint4 raw = *reinterpret_cast<const uint4*>(base + half_bytes + r * 128 + ((c ^ (r & 7)) << 4));
-        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+        const uint32_t w4[4] = {hi ? raw.z : raw.x, hi ? raw.w : raw.y, hi ? raw.x : raw.z, hi ? raw.y : raw.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           h[t][2 * k] = hmul2(cvt_f16x2_e4m3x2(w4[k] & 0xFFFFu), s2);
@@ -177,10 +184,10 @@ __device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int 
 #pragma unroll
       for (int t = 0; t < STEPS; ++t) {
         const int r = cw * RPW + g * 32 + i0 + 4 * t + (lane >> 3);
-        uint8_t* row = base + (c >> 2) * half_bytes + r * 128;
-        const int q0 = (2 * (c & 3)) ^ (r & 7), q1 = (2 * (c & 3) + 1) ^ (r & 7);
-        *reinterpret_cast<uint4*>(row + (q0 << 4)) = make_uint4(h[t][0], h[t][1], h[t][2], h[t][3]);
-        *reinterpret_cast<uint4*>(row + (q1 << 4)) = make_uint4(h[t][4], h[t][5], h[t][6], h[t][7]);
+        uint8_t* row = base + hi * half_bytes + r * 128;
+        const int first = ((2 * (c & 3)) ^ (r & 7)) ^ hi;
+        *reinterpret_cast<uint4*>(row + (first << 4)) = make_uint4(h[t][0], h[t][1], h[t][2], h[t][3]);
+        *reinterpret_cast<uint4*>(row + ((first ^ 1) << 4)) = make_uint4(h[t][4], h[t][5], h[t][6], h[t][7]);
       }
       // the next batch reads other rows' lines, which this batch does not write
     }
