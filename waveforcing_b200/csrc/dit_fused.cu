@@ -283,7 +283,7 @@ struct PublishTable {
 // of the QKV output), which needs no other pass.  Destination rows are
 // indexed by the row's position within its stage, r % rows_per_stage.
 template <int NCH>
-__global__ void __launch_bounds__(256) qk_norm_rope_publish_kernel(
+__global__ void __launch_bounds__(256, NCH <= 6 ? 3 : 1) qk_norm_rope_publish_kernel(
     const __nv_bfloat16* __restrict__ qkv, int64_t ld, const __nv_bfloat16* __restrict__ wq,
     const __nv_bfloat16* __restrict__ wk, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
     int head_dim, __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out,

@@ -95,8 +95,10 @@ class PagedTransport:
         self.fused_assembly = True
         # per-token FP8 publishes may be done by the kernel that produces K
         # (wf_qk_norm_rope_publish): the closures then expose their targets
-        # (``exch.fp8_publish_targets(layer)``) and only write the flags
-        self.fused_publish = True
+        # (``exch.fp8_publish_targets(layer)``) and only write the flags.  Off
+        # by default: at the 1.3B tick shape the fused kernel moves fewer
+        # bytes but runs slower than wf_qk_norm_rope + wf_kv_quant_publish
+        self.fused_publish = False
         self.naw_max, self.Wmax = slab_geometry(max_attn_frames, rf_step, npb)
         self.local = [s for s in range(rf_step + 1) if self.stage_rank[s] == rank]
         # a CPU device is accepted only to exercise the host-side bookkeeping in tests
