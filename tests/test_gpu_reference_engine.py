@@ -2,7 +2,8 @@
 
 Both arms run inside the reference's WaveDenoiser (wave_rt/denoiser/engine.py,
 driven by baseline/harness.py), one rank per stage on its own GPU: a 2-step
-wavefront, ranks 0-1 denoise and rank 2 is the store, over a Wan-shaped DiT
+wavefront, ranks 0-1 denoise and rank 2 is the store (with 2 GPUs: a 1-step
+wavefront, rank 0 denoises and rank 1 is the store), over a Wan-shaped DiT
 of 1.3B width (dim 1536, 12 x 128 heads, FFN 8960; 2 layers) on 60 x 104
 latents (4680 tokens per chunk), 10 chunks.
 
@@ -16,8 +17,9 @@ latents (4680 tokens per chunk), 10 chunks.
      scales (tcgen05 kind::f8f6f4).
 
 Bar: the store's final latents at cosine >= 0.999 (the north-star bar for
-full-step latents).  Needs 3 GPUs and the reference package (baseline/_ref or
-WF_REFERENCE); NVLS is off and the process group has a short timeout.
+full-step latents).  Needs 2 or more GPUs and the reference package
+(baseline/_ref or WF_REFERENCE); NVLS is off and the process group has a short
+timeout.
 """
 
 import datetime
@@ -32,10 +34,12 @@ import torch.multiprocessing as mp
 from baseline import harness
 
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(torch.cuda.device_count() < 3, reason="needs >= 3 GPUs"),
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs"),
               pytest.mark.skipif(harness.reference_checkout() is None, reason="needs the reference package")]
 
-STEPS = (1000, 500)
+# 2-step wavefront on 3 GPUs; with 2 GPUs a 1-step wavefront (one denoise
+# rank and the store: the store's live-slot publishes, promotion, the anchor)
+STEPS = (1000, 500) if torch.cuda.device_count() >= 3 else (1000,)
 NUM_FRAMES = 30
 
 VARIANTS = {  # name -> (arm, env for this repository's mixin, W8A8)
