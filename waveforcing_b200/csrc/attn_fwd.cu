@@ -38,6 +38,8 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 
 #include "host_util.h"
 #include "sm100.cuh"
@@ -206,7 +208,7 @@ __device__ __forceinline__ void convert_q_f16(uint8_t* base, int bytes, int t) {
   }
 }
 
-template <bool KV8>
+template <bool KV8, bool PX>
 __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                                           __nv_bfloat16* __restrict__ out, long long o_tok, long long o_head,
                                           long long o_batch, int Lq, int Lk, int H, int n_items, float scale_log2,
@@ -565,25 +567,48 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
           m_new = mx2;
           grow = true;
         }
-        // P = 2^(s * scale_log2 - m): pairs through packed f32x2 FMAs; 3 of
-        // every 8 pairs take the FMA-pipe polynomial, the rest MUFU ex2, so
-        // the two pipes finish together.
         const float2 sc2 = make_float2(scale_log2, scale_log2);
         const float2 nm2 = make_float2(-m_new, -m_new);
         float2 sum2 = make_float2(0.f, 0.f);
         uint32_t pk[KH / 2];
+        if constexpr (PX) {
+          // P = 2^(s * scale_log2 - m) on MUFU's packed 16-bit path: the
+          // exponent pair is rounded to the MMA's P type (bf16, or f16 for
+          // FP8 K/V) and one ex2 gives both P values in that type.  The row
+          // sum adds exactly the P the MMA multiplies.
 #pragma unroll
-        for (int i = 0; i < KH / 2; ++i) {
-          const float2 x = ffma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
-          float2 pr;
-          if ((i & 7) < 3) {
-            pr = exp2_poly2(x);
-          } else {
-            pr.x = ex2_approx(x.x);
-            pr.y = ex2_approx(x.y);
+          for (int i = 0; i < KH / 2; ++i) {
+            const float2 x = ffma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
+            uint32_t p;
+            float2 pr;
+            if constexpr (KV8) {
+              asm("ex2.approx.f16x2 %0, %1;" : "=r"(p) : "r"(pack_f16x2(x.x, x.y)));
+              const __half2 h = *reinterpret_cast<const __half2*>(&p);
+              pr = __half22float2(h);
+            } else {
+              asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(p) : "r"(pack_bf16x2(x.x, x.y)));
+              pr = make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u));
+            }
+            sum2 = fadd2(sum2, pr);
+            pk[i] = p;
           }
-          sum2 = fadd2(sum2, pr);
-          pk[i] = KV8 ? pack_f16x2(pr.x, pr.y) : pack_bf16x2(pr.x, pr.y);
+        } else {
+          // P = 2^(s * scale_log2 - m): pairs through packed f32x2 FMAs; 3 of
+          // every 8 pairs take the FMA-pipe polynomial, the rest MUFU ex2, so
+          // the two pipes finish together.
+#pragma unroll
+          for (int i = 0; i < KH / 2; ++i) {
+            const float2 x = ffma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
+            float2 pr;
+            if ((i & 7) < 3) {
+              pr = exp2_poly2(x);
+            } else {
+              pr.x = ex2_approx(x.x);
+              pr.y = ex2_approx(x.y);
+            }
+            sum2 = fadd2(sum2, pr);
+            pk[i] = KV8 ? pack_f16x2(pr.x, pr.y) : pack_bf16x2(pr.x, pr.y);
+          }
         }
         const float sum = sum2.x + sum2.y;
         const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
@@ -662,25 +687,24 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
   }
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
-    attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,
-                         long long o_head, long long o_batch, int Lq, int Lk, int H, int n_items,
-                         float scale_log2) {
-  attn_body<false>(tmQ, tmK, tmV, out, o_tok, o_head, o_batch, Lq, Lk, H, n_items, scale_log2, nullptr, nullptr,
-                   WF_SCALE_NONE);
-}
+#define WFK_ATTN_KERNELS(NAME, KV8, PX)                                                                       \
+  __global__ void __launch_bounds__(THREADS, 1)                                                               \
+      NAME(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,                  \
+           const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,         \
+           long long o_head, long long o_batch, int Lq, int Lk, int H, int n_items, float scale_log2,         \
+           const float* __restrict__ k_scale, const float* __restrict__ v_scale, int scale_mode) {           \
+    attn_body<KV8, PX>(tmQ, tmK, tmV, out, o_tok, o_head, o_batch, Lq, Lk, H, n_items, scale_log2, k_scale,  \
+                       v_scale, scale_mode);                                                                 \
+  }
 
-// K/V as e4m3 codes [batch, Lk, H, 128] with per-token (k_scale[bz * Lk +
-// key]), per-tensor (k_scale[0]) or no scales.
-__global__ void __launch_bounds__(THREADS, 1)
-    attn_fwd_e4m3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, long long o_tok,
-                         long long o_head, long long o_batch, int Lq, int Lk, int H, int n_items, float scale_log2,
-                         const float* __restrict__ k_scale, const float* __restrict__ v_scale, int scale_mode) {
-  attn_body<true>(tmQ, tmK, tmV, out, o_tok, o_head, o_batch, Lq, Lk, H, n_items, scale_log2, k_scale, v_scale,
-                  scale_mode);
-}
+// bf16 K/V (scales unused) and e4m3 K/V codes [batch, Lk, H, 128] with
+// per-token (k_scale[bz * Lk + key]), per-tensor (k_scale[0]) or no scales;
+// the _px forms take the exponentials on MUFU's packed 16-bit path.
+WFK_ATTN_KERNELS(attn_fwd_bf16_kernel, false, false)
+WFK_ATTN_KERNELS(attn_fwd_bf16_px_kernel, false, true)
+WFK_ATTN_KERNELS(attn_fwd_e4m3_kernel, true, false)
+WFK_ATTN_KERNELS(attn_fwd_e4m3_px_kernel, true, true)
+#undef WFK_ATTN_KERNELS
 
 // Tensor map over a [batch, L, H, 128] bf16 tensor with {batch, token, head}
 // element strides; box = 64 head-dim columns x 1 head x 128 tokens.
@@ -759,8 +783,8 @@ extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o,
   int dev = 0;
   WFK_CUDA_TRY(cudaGetDevice(&dev));
   if (configured_dev != dev) {
-    WFK_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    WFK_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_e4m3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    for (auto fn : {attn_fwd_bf16_kernel, attn_fwd_bf16_px_kernel, attn_fwd_e4m3_kernel, attn_fwd_e4m3_px_kernel})
+      WFK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     configured_dev = dev;
   }
   const long long items = (long long)((Lq + BM - 1) / BM) * H * batch;
@@ -780,14 +804,18 @@ extern "C" int wf_attn_fwd(const void* q, const void* k, const void* v, void* o,
     grid = (items + per - 1) / per;
   }
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
-  if (kv8)
-    attn_fwd_e4m3_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
-        tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
-        (long long)o_stride[0], Lq, Lk, H, (int)items, scale_log2, k_scale, v_scale, scale_mode);
-  else
-    attn_fwd_bf16_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
-        tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
-        (long long)o_stride[0], Lq, Lk, H, (int)items, scale_log2);
+  // Exponential path: WFK_ATTN_EXP=packed selects MUFU's packed 16-bit ex2,
+  // =split the f32 MUFU / FMA-polynomial split (read once per process).
+  static const bool packed_exp = [] {
+    const char* e = std::getenv("WFK_ATTN_EXP");
+    return e != nullptr && std::strcmp(e, "packed") == 0;
+  }();
+  auto kern = kv8 ? (packed_exp ? attn_fwd_e4m3_px_kernel : attn_fwd_e4m3_kernel)
+                  : (packed_exp ? attn_fwd_bf16_px_kernel : attn_fwd_bf16_kernel);
+  kern<<<(unsigned)grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+      tq, tk, tv, static_cast<__nv_bfloat16*>(o), (long long)o_stride[1], (long long)o_stride[2],
+      (long long)o_stride[0], Lq, Lk, H, (int)items, scale_log2, kv8 ? k_scale : nullptr, kv8 ? v_scale : nullptr,
+      kv8 ? scale_mode : WF_SCALE_NONE);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }
