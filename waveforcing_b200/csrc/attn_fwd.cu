@@ -153,7 +153,7 @@ __device__ __forceinline__ void fetch_row_scales(float (&sv)[NS], const float* _
 template <int NS>
 __device__ __forceinline__ void convert_rows(uint8_t* base, int half_bytes, int cw, int lane, const float (&sv)[NS]) {
   constexpr int RPW = NS * 32;
-  constexpr int STEPS = 1;  // with the scale prefetch, 2 spills under warpgroup 0's 72 registers
+  constexpr int STEPS = 2;  // 4 spills under warpgroup 0's 72-register budget
   static_assert(32 % (4 * STEPS) == 0, "a batch must not cross a group of 32 rows");
   const int c = lane & 7;
 #pragma unroll
@@ -455,23 +455,10 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
       const int t = cw * 32 + lane;
       int kt = 0, vt = 0, n_it = 0;
       bool ok = true;
-      // Row scales are fetched a whole tile body ahead: while body j (K_{j+1},
-      // the two halves of V_j) converts, the loads for body j + 1 are in
-      // flight, so no conversion waits on an L2 round trip.
-      struct Body {
-        float k[BN / 64];   // K_{j+1}: this lane's 4 of the warp's 128 rows
-        float v0[KH / 64];  // V_j, keys [0, 128): 2 of the warp's 64 rows
-        float v1[KH / 64];  // V_j, keys [128, 256)
-      };
-      auto fetch_body = [&](Body& b, const Item& w, int j) {
-        if (j + 1 < nk) fetch_row_scales(b.k, k_scale, scale_mode, w.bz, Lk, (j + 1) * BN, BN / 2, cw, lane);
-        if (j < nk) {
-          fetch_row_scales(b.v0, v_scale, scale_mode, w.bz, Lk, j * BN, KH / 2, cw, lane);
-          fetch_row_scales(b.v1, v_scale, scale_mode, w.bz, Lk, j * BN + KH, KH / 2, cw, lane);
-        }
-      };
-      auto conv_k = [&](const float (&sv)[BN / 64]) -> bool {
+      auto conv_k = [&](const Item& w, int j) -> bool {
         const int s = kt % NSK;
+        float sv[BN / 64];  // this lane's 4 of the warp's 128 rows
+        fetch_row_scales(sv, k_scale, scale_mode, w.bz, Lk, j * BN, BN / 2, cw, lane);
         if (!__all_sync(0xffffffffu, mbar_wait(&raw_k[s], (kt / NSK) & 1, abort_flag, ST_ATTN_CONVERT)))
           return false;
         convert_rows(sK + s * KTILE, KHALF, cw, lane, sv);
@@ -480,31 +467,27 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
         ++kt;
         return true;
       };
-      auto conv_v = [&](int half, const float (&sv)[KH / 64]) -> bool {
-        if (!__all_sync(0xffffffffu, mbar_wait(&raw_v[half], vt & 1, abort_flag, ST_ATTN_CONVERT))) return false;
-        convert_rows(sV + half * VSLOT, VHALF, cw, lane, sv);
-        fence_proxy_async_smem();
-        mbar_arrive(&full_v[half]);
-        return true;
-      };
       for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++n_it) {
         const Item w = item_of(it, n_qt, H);
-        float k0[BN / 64];
-        fetch_row_scales(k0, k_scale, scale_mode, w.bz, Lk, 0, BN / 2, cw, lane);
-        Body nxt;
-        fetch_body(nxt, w, 0);
         ok = __all_sync(0xffffffffu, mbar_wait(q_raw, n_it & 1, abort_flag, ST_ATTN_CONVERT));
         if (!ok) break;
         convert_q_f16(sQ, QTILE, t);
         fence_proxy_async_smem();
         mbar_arrive(bar_q);
-        if (!(ok = conv_k(k0))) break;
+        if (!(ok = conv_k(w, 0))) break;
         for (int j = 0; ok && j < nk; ++j) {
-          const Body cur = nxt;
-          fetch_body(nxt, w, j + 1);
-          if (j + 1 < nk && !(ok = conv_k(cur.k))) break;
-          if (!(ok = conv_v(0, cur.v0)) || !(ok = conv_v(1, cur.v1))) break;
-          ++vt;
+          if (j + 1 < nk && !(ok = conv_k(w, j + 1))) break;
+          for (int half = 0; half < 2; ++half) {
+            float sv[KH / 64];  // this lane's 2 of the warp's 64 rows
+            fetch_row_scales(sv, v_scale, scale_mode, w.bz, Lk, j * BN + half * KH, KH / 2, cw, lane);
+            if (!(ok = __all_sync(0xffffffffu,
+                                  mbar_wait(&raw_v[half], vt & 1, abort_flag, ST_ATTN_CONVERT))))
+              break;
+            convert_rows(sV + half * VSLOT, VHALF, cw, lane, sv);
+            fence_proxy_async_smem();
+            mbar_arrive(&full_v[half]);
+          }
+          if (ok) ++vt;
         }
       }
     }
