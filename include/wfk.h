@@ -224,6 +224,16 @@ int wf_ln_modulate(const void* x, int64_t x_stride, const float* shift, const fl
                    void* out, int64_t out_stride, int64_t rows, int64_t dim, int64_t rows_per_stage, float eps,
                    void* stream);
 
+/* wf_ln_modulate whose bf16 output goes straight into the per-token W8A8
+ * activation quantiser of the linear that reads it (the QKV projection and
+ * FFN fc_in of causal_model.py:375-377, 405-408 with W8A8 linears,
+ * wave_rt/runtime/fp8.py:47-48 per row): xq [rows, dim] e4m3 or int8 codes
+ * (qtype) and x_scale [rows], equal bit for bit to wf_act_quant applied to
+ * wf_ln_modulate's output, without writing or re-reading that output. */
+int wf_ln_modulate_quant(const void* x, int64_t x_stride, const float* shift, const float* scale,
+                         int64_t mod_stride, void* xq, float* x_scale, int64_t rows, int64_t dim,
+                         int64_t rows_per_stage, float eps, int qtype, void* stream);
+
 /* x = bf16(x + y * gate[s]) in place, the gated residuals of
  * causal_model.py:383 and :411-413 (gate of ones for the cross-attention add). */
 int wf_gate_residual(void* x, int64_t x_stride, const void* y, int64_t y_stride, const float* gate,

@@ -82,6 +82,8 @@ def test_constants_match_the_header():
      1),                                                                      # e4m3 unknown scale_mode
     ("wf_qk_norm_rope_publish", (16, 16, 16, 16, 16, 16, 128, 16, 16, None, 4, 1536, 4, 1e-6, None, None, 9, None),
      1),                                                                      # more than 8 stages
+    ("wf_ln_modulate_quant", (16, 16, 16, 16, 16, 16, 16, 4, 1536, 4, 1e-6, 7, None), 2),  # unknown qtype
+    ("wf_ln_modulate_quant", (None, 16, 16, 16, 16, 16, 16, 4, 1536, 4, 1e-6, 1, None), 1),
     ("wf_kv_quant", (None, None, None, 4, 16, 16, 2, None, None), 1),
     ("wf_kv_quant", (16, 16, 16, 4, 12, 16, 2, None, None), 1),                # cols not a multiple of 8
     ("wf_kv_dequant", (16, None, 16, 4, 16, 16, 2, None), 1),                 # token mode without scales

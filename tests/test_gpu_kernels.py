@@ -603,6 +603,28 @@ def test_fused_rows_match_torch(dim):
     assert (r.float() - rms(x, wq).float()).abs().max().item() <= 0.01 * r.float().abs().max().item()
 
 
+@pytest.mark.parametrize("dim", [256, 1536, 3072, 5120])
+@pytest.mark.parametrize("qtype", ["e4m3", "s8"])
+def test_ln_modulate_quant_matches_separate_passes(dim, qtype):
+    """wf_ln_modulate_quant: codes and scales bit-identical to wf_act_quant on
+    wf_ln_modulate's bf16 output (e4m3 and int8; rows of three stages, one
+    of them all zeros)."""
+    from waveforcing_b200 import _lib as L
+
+    K = _kernels()
+    qt = L.WF_DTYPE_E4M3 if qtype == "e4m3" else L.WF_DTYPE_S8
+    torch.manual_seed(dim + 7)
+    S, T = 3, 40
+    x = (torch.randn(S * T, dim, device=DEV) * torch.rand(S * T, 1, device=DEV) * 5).bfloat16()
+    x[17] = 0
+    e = torch.randn(S, 6, dim, device=DEV) * 0.3
+    xq, xs = K.ln_modulate_quant(x, e[:, 0], e[:, 1], T, 1e-6, qt)
+    h = K.ln_modulate(x, e[:, 0], e[:, 1], T, 1e-6)
+    rq, rs = K.act_quant(h, qt)
+    assert torch.equal(xq, rq) and torch.equal(xs, rs)
+    assert L.status_take() == 0
+
+
 @pytest.mark.parametrize("dim", [256, 1536, 5120])
 def test_qk_norm_rope_publish_matches_separate_passes(dim):
     """wf_qk_norm_rope_publish: q, k and the un-roped k bit-identical to

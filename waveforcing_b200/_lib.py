@@ -73,6 +73,7 @@ _SIGS = {
     "wf_rope_apply": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i64, _i64, _vp]),
     "wf_kv_assemble": (_i32, [C.POINTER(KvSegment), _i32, _i64, _i32, _vp]),
     "wf_ln_modulate": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _f32, _vp]),
+    "wf_ln_modulate_quant": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _vp]),
     "wf_gate_residual": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
     "wf_qk_norm_rope": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),
     "wf_qk_norm_rope_publish": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32,

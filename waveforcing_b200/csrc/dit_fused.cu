@@ -2,6 +2,8 @@
 // per token row, f32 math, bf16 in/out), replacing chains of 4-8 torch ops:
 //   wf_ln_modulate   out = LN(x) * (1 + scale[s]) + shift[s]
 //                    naive_rt/rolling_forcing/wan/modules/causal_model.py:375-377, 405-408
+//   wf_ln_modulate_quant  the same, quantised per token for the W8A8 linear
+//                    that reads it (codes + scale; the bf16 row is not written)
 //   wf_gate_residual x += y * gate[s]                       causal_model.py:383, 411-413
 //   wf_qk_norm_rope  q, k from the fused QKV GEMM output:  RMSNorm over dim
 //                    (model.py:70-88, rounding to bf16 before the weight as
@@ -88,6 +90,91 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const __nv_bfloat16* _
     for (int i = 0; i < 8; ++i) o[i] = fmaf((v[c][i] - mean) * rstd, 1.f + sc[i], sf[i]);
     orow[lane + 32 * c] = pack8(o);
   }
+}
+
+// ln_modulate_kernel fused with the per-token W8A8 activation quantiser of
+// the linear that reads its output (the QKV projection, FFN fc_in): the row
+// of bf16-rounded outputs stays in registers, its amax gives the row scale,
+// and only codes (e4m3, or int8 when I8) and the scale are written.  The
+// quantisation is act_quant_kernel's (gemm_w8a8.cu, the same row helpers),
+// so the codes and scales equal wf_act_quant(wf_ln_modulate(x)) bit for bit
+// while the bf16 output is neither written nor read back.
+template <int NCH, bool I8>
+__global__ void __launch_bounds__(256) ln_modulate_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs,
+                                                                const float* __restrict__ shift,
+                                                                const float* __restrict__ scale, int64_t mod_stride,
+                                                                uint8_t* __restrict__ xq, float* __restrict__ x_scale,
+                                                                int64_t rows, int64_t rows_per_stage, float eps) {
+  using namespace wfk::quant;
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  constexpr int DIM = NCH * 256;
+  float v[NCH][8];
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * xs);
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    unpack8(__ldg(xr + lane + 32 * c), v[c]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += v[c][i];
+  }
+  const float mean = warp_sum(sum) * (1.f / DIM);
+  float q2 = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = v[c][i] - mean;
+      q2 = fmaf(d, d, q2);
+    }
+  const float rstd = rsqrtf(warp_sum(q2) * (1.f / DIM) + eps);
+  const int64_t st = r / rows_per_stage;
+  const float4* sh4 = reinterpret_cast<const float4*>(shift + st * mod_stride);
+  const float4* sc4 = reinterpret_cast<const float4*>(scale + st * mod_stride);
+  uint4 packed[NCH];
+  uint32_t m2 = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int e = (lane + 32 * c) * 2;
+    const float4 a0 = __ldg(sc4 + e), a1 = __ldg(sc4 + e + 1);
+    const float4 b0 = __ldg(sh4 + e), b1 = __ldg(sh4 + e + 1);
+    const float sc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float sf[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = fmaf((v[c][i] - mean) * rstd, 1.f + sc[i], sf[i]);
+    packed[c] = pack8(o);
+    m2 = amax8_bits(packed[c], m2);
+  }
+  const RowQuant q = make_rowq(warp_amax_bits(m2), I8 ? 127.f : 448.f);
+  uint2* out = reinterpret_cast<uint2*>(xq + r * DIM);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const uint4& pv = packed[c];
+    uint2 code;
+    if (q.finite) {
+      if constexpr (I8)
+        code = make_uint2(i8x2_fast(pv.x, q.r) | (i8x2_fast(pv.y, q.r) << 16),
+                          i8x2_fast(pv.z, q.r) | (i8x2_fast(pv.w, q.r) << 16));
+      else
+        code = make_uint2(quant4_fast(pv.x, pv.y, q.r), quant4_fast(pv.z, pv.w, q.r));
+    } else {
+      const uint32_t w[4] = {pv.x, pv.y, pv.z, pv.w};
+      uint32_t o2[2] = {0, 0};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float b0 = bf16_round_f(__fdiv_rn(__uint_as_float(w[i] << 16), q.s));
+        const float b1 = bf16_round_f(__fdiv_rn(__uint_as_float(w[i] & 0xFFFF0000u), q.s));
+        const uint32_t cc =
+            I8 ? (i8_slow(b0) | (i8_slow(b1) << 8)) : (e4m3_encode_sw(b0) | (e4m3_encode_sw(b1) << 8));
+        o2[i >> 1] |= cc << ((i & 1) * 16);
+      }
+      code = make_uint2(o2[0], o2[1]);
+    }
+    out[lane + 32 * c] = code;
+  }
+  if (lane == 0) x_scale[r] = q.s;
 }
 
 // x[r] = bf16(x[r] + y[r] * gate[stage])   (f32 math)
@@ -237,6 +324,33 @@ extern "C" int wf_ln_modulate(const void* x, int64_t x_stride, const float* shif
     ln_modulate_kernel<decltype(n)::value><<<blocks, 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(x), x_stride, shift, scale, mod_stride, static_cast<__nv_bfloat16*>(out),
         out_stride, rows, rows_per_stage, eps);
+  });
+  if (rc != WF_OK) return rc;
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_ln_modulate_quant(const void* x, int64_t x_stride, const float* shift, const float* scale,
+                                    int64_t mod_stride, void* xq, float* x_scale, int64_t rows, int64_t dim,
+                                    int64_t rows_per_stage, float eps, int qtype, void* stream) {
+  if (!x || !shift || !scale || !xq || !x_scale || rows < 0 || rows_per_stage < 1 || !aligned16(x) ||
+      !aligned16(xq) || !aligned16(shift) || !aligned16(scale) || x_stride % 8 || mod_stride % 4)
+    return fail(WF_ERR_INVALID_ARG, "wf_ln_modulate_quant: bad arguments");
+  if (qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8)
+    return fail(WF_ERR_UNSUPPORTED, "wf_ln_modulate_quant: qtype must be WF_DTYPE_E4M3 or WF_DTYPE_S8");
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = by_dim(dim, [&](auto n) {
+    constexpr int N = decltype(n)::value;
+    if (qtype == WF_DTYPE_S8)
+      ln_modulate_quant_kernel<N, true><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), x_stride, shift,
+                                                               scale, mod_stride, static_cast<uint8_t*>(xq), x_scale,
+                                                               rows, rows_per_stage, eps);
+    else
+      ln_modulate_quant_kernel<N, false><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), x_stride,
+                                                                shift, scale, mod_stride, static_cast<uint8_t*>(xq),
+                                                                x_scale, rows, rows_per_stage, eps);
   });
   if (rc != WF_OK) return rc;
   WFK_CUDA_TRY(cudaGetLastError());

@@ -306,6 +306,26 @@ def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_
     return out
 
 
+def ln_modulate_quant(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_per_stage: int, eps: float,
+                      qtype: int = L.WF_DTYPE_E4M3):
+    """ln_modulate followed by the per-token W8A8 activation quantiser, in one
+    kernel: returns (codes uint8 [rows, dim], scales f32 [rows]), equal to
+    act_quant(ln_modulate(x)) without the bf16 output being written."""
+    _check(x.dim() == 2 and x.dtype == torch.bfloat16, "ln_modulate_quant: x must be a bf16 [rows, dim] matrix")
+    rows, dim = x.shape
+    for t in (shift, scale):
+        _check(t.dtype == torch.float32 and t.dim() == 2 and t.shape[1] == dim and t.stride(1) == 1
+               and t.shape[0] * rows_per_stage >= rows, "ln_modulate_quant: shift/scale must be f32 [stages, dim]")
+    _check(shift.stride(0) == scale.stride(0), "ln_modulate_quant: shift and scale must share their row stride")
+    _need_cuda(x)
+    xq = torch.empty((rows, dim), device=x.device, dtype=torch.uint8)
+    xs = torch.empty((rows,), device=x.device, dtype=torch.float32)
+    L.check(L.lib().wf_ln_modulate_quant(x.data_ptr(), x.stride(0), shift.data_ptr(), scale.data_ptr(),
+                                         shift.stride(0), xq.data_ptr(), xs.data_ptr(), rows, dim, rows_per_stage,
+                                         eps, qtype, _stream()), "wf_ln_modulate_quant")
+    return xq, xs
+
+
 def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, rows_per_stage: int) -> torch.Tensor:
     """x += y * gate[s] in place (f32 math, bf16 storage)."""
     _check(x.dim() == 2 and y.shape == x.shape and x.dtype == y.dtype == torch.bfloat16,

@@ -70,6 +70,15 @@ class WfW8A8Linear(nn.Module):
             mode = L.WF_SCALE_TENSOR
         return kernels.gemm_w8a8(xq, xs, self.w_q, self.w_scale, self.bias, self.qtype, mode, activation=activation)
 
+    def gemm_q(self, xq: torch.Tensor, xs: torch.Tensor, activation: int = L.WF_ACT_NONE) -> torch.Tensor:
+        """This linear on an input already quantised per token with this
+        module's qtype (codes [M, in_features], scales [M]), e.g. by
+        kernels.ln_modulate_quant.  Per-channel granularity only."""
+        if self.granularity != "channel":
+            raise ValueError("pre-quantised input needs per-token scales (granularity 'channel')")
+        return kernels.gemm_w8a8(xq, xs, self.w_q, self.w_scale, self.bias, self.qtype, L.WF_SCALE_TOKEN,
+                                 activation=activation)
+
     def forward(self, x: torch.Tensor):
         shape = x.shape
         y = self._raw(x.reshape(-1, shape[-1]))

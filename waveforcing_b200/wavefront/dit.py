@@ -324,12 +324,24 @@ class WanDiT(nn.Module):
             g = gate_all[:, k][:, None] if gate_all is not None else ones
             return (inp.float().view(S, T, dim) + y.float().view(S, T, dim) * g).to(dt).view(S * T, dim)
 
+        def w8a8_channel(mod):
+            return getattr(mod, "granularity", None) == "channel" and hasattr(mod, "gemm_q")
+
+        def ln_mod_linear(inp, e_all, k_shift, lin):
+            """lin(ln_mod(inp)); a per-token W8A8 linear gets its input from the
+            fused LN-modulate quantiser (the bf16 LN output is never written)."""
+            if fused and w8a8_channel(lin):
+                xq, xsc = kernels.ln_modulate_quant(inp, e_all[:, k_shift], e_all[:, k_shift + 1], T, eps, lin.qtype)
+                return lin.gemm_q(xq, xsc)
+            return _lin(lin, ln_mod(inp, e_all, k_shift))
+
         for li, b in enumerate(self.blocks):
             e_all = (b.modulation.float() + mods).contiguous()  # [S, 6, dim]
-            h = ln_mod(xs, e_all, 0)
             fq = None if (separate_qkv and not fused) else self._fused_qkv(b)
+            qkv_w8 = fused and fq is not None and not isinstance(fq[0], torch.Tensor) and w8a8_channel(fq[0])
+            h = None if qkv_w8 else ln_mod(xs, e_all, 0)
             if fused and fq is not None:
-                qkv = self._qkv_gemm(fq, h)
+                qkv = ln_mod_linear(xs, e_all, 0, fq[0]) if qkv_w8 else self._qkv_gemm(fq, h)
                 # exchange closures that publish per-token FP8 K/V expose their
                 # destination slots; the kernel that produces K publishes them
                 targets = [getattr(t.exch, "fp8_publish_targets", None) for t in tasks]
@@ -382,8 +394,17 @@ class WanDiT(nn.Module):
             kc, vc = self._cross_kv[li]
             oc = sdpa_elsewhere(qc, kc, vc)
             xs = gate_add(xs, _lin(b.cross_attn.o, oc.view(S * T, dim)), None, 0)
-            h = ln_mod(xs, e_all, 3)
             fi, fo = b.ffn.fc_in, b.ffn.fc_out
+            if fused and w8a8_channel(fi) and getattr(fo, "granularity", None) == "channel" and hasattr(
+                    fo, "forward_gelu_input"):
+                # W8A8, per-token: LN-modulate quantised in one kernel, plain
+                # fc_in GEMM, GELU(tanh) inside fc_out's input quantiser
+                y = fo.forward_gelu_input(ln_mod_linear(xs, e_all, 3, fi))
+                xs = gate_add(xs, y, e_all, 5)
+                if layer_hook is not None:
+                    layer_hook(li)
+                continue
+            h = ln_mod(xs, e_all, 3)
             if fused and type(fi) is nn.Linear:
                 a = torch._addmm_activation(fi.bias, h, fi.weight.t(), use_gelu=True)  # cuBLASLt bias+GELU(tanh)
                 y = _lin(fo, a)
