@@ -77,9 +77,10 @@ def _worker(rank, world, port, q):
         xp = paged.PagedTransport(device="cpu", rank=rank, world=world, stage_rank=[0, 0, 1, 1], rf_step=3, Ln=2,
                                   T=4, H=1, D=8, fp8=False)
         dst = {m: dict(d) for m, d in xp.dst.items()}
+        credit = ({m: len(a) for m, a in xp.credit_dst.items()}, xp.remote_consumers())
         xp.close()
         xp.close()  # idempotent
-        q.put((rank, sorted(dst), {m: d["local"] for m, d in dst.items()}, log))
+        q.put((rank, sorted(dst), {m: d["local"] for m, d in dst.items()}, log, credit))
     finally:
         dist.destroy_process_group()
 
@@ -101,14 +102,19 @@ def test_two_rank_handle_exchange_and_close_order():
         p.start()
     res = {}
     for _ in procs:
-        r, stages, local, log = q.get(timeout=120)
-        res[r] = (stages, local, log)
+        r, stages, local, log, credit = q.get(timeout=120)
+        res[r] = (stages, local, log, credit)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    # rank 0 hosts consumer stages 0,1 (local); it publishes only from 0/1 to lower stages -> no remote opens
+    # rank 0 hosts consumer stages 0,1 (local); it publishes only from 0/1 to lower stages, so its one
+    # remote mapping is rank 1's credit word array, which it signals for both stages (release_slots)
     assert res[0][0] == [0, 1] and all(res[0][1].values())
-    assert res[0][2] == []
+    assert [op for op, _ in res[0][2]] == ["open", "close"]
+    assert res[0][3] == ({0: 1, 1: 1}, [])
+    # rank 1's producers (stage 2, store) publish to stages 0 and 1 on rank 0: it waits on their
+    # credits (acquire_slots); its own consumer stage 2 is fed locally, so it signals no one
+    assert res[1][3] == ({}, [0, 1])
     # rank 1 hosts stage 2 (consumer, local) and the store, which publishes to stages 0,1 on rank 0
     assert res[1][0] == [0, 1, 2] and res[1][1] == {0: False, 1: False, 2: True}
     opens = [p for op, p in res[1][2] if op == "open"]

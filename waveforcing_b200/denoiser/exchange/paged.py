@@ -138,6 +138,12 @@ class PagedTransport:
             self.store_buf = (torch.zeros((cap, H, D), device=self.device, dtype=dtype),
                               torch.zeros((cap, H, D), device=self.device, dtype=dtype))
         self.timeout_word = torch.zeros(1, device=self.device, dtype=torch.int32)
+        # slab-generation credits, indexed by consumer stage: the rank hosting
+        # consumer stage m writes tick + 1 into credit[m] of every rank that
+        # publishes to m once its tick's reads are done (release_slots); a
+        # producer waits on it before reusing that generation (acquire_slots)
+        self.credit = torch.zeros(max(1, rf_step), device=self.device, dtype=torch.int32)
+        self.credit_dst: dict = {}  # local consumer stage -> [peer address of credit[m]]
         # when a list, every remote flag wait appends its (start, end) CUDA events:
         # the exposed part of the exchange on this rank's compute stream
         self.wait_timer = None
@@ -153,12 +159,21 @@ class PagedTransport:
                    if k in ("k", "v", "kc", "vc", "ks", "vs")}
             ent["flags"] = ipc.ipc_export(self.flags[m]) if self.world > 1 else None
             mine[m] = ent
+        credit_h = ipc.ipc_export(self.credit) if self.world > 1 else None
         if self.world > 1:
             gathered = [None] * self.world
-            dist.all_gather_object(gathered, (self.rank, mine), group=self.group)
+            dist.all_gather_object(gathered, (self.rank, mine, credit_h), group=self.group)
         else:
-            gathered = [(self.rank, mine)]
-        for rk, ents in gathered:
+            gathered = [(self.rank, mine, credit_h)]
+        for rk, _ents, ch in gathered:
+            if rk == self.rank:
+                continue
+            # consumer stages here that a stage on rank rk publishes to
+            for m in self.local:
+                if m < self.store and any(self.stage_rank[s] == rk for s in range(m + 1, self.store + 1)):
+                    h, off = ch
+                    self.credit_dst.setdefault(m, []).append(self._open(h) + off + 4 * m)
+        for rk, ents, _ch in gathered:
             for m, ent in ents.items():
                 if rk == self.rank:
                     sl = self.slabs[m]
@@ -351,6 +366,35 @@ class PagedTransport:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record(cur)
             sink.append((e0, e1))
+
+    def remote_consumers(self) -> list[int]:
+        """Consumer stages on other ranks that a stage on this rank publishes to."""
+        return [m for m in range(self.store) if self.stage_rank[m] != self.rank
+                and any(s > m for s in self.local)]
+
+    def acquire_slots(self, tick: int) -> None:
+        """Before the first publish of ``tick``: wait (bounded, on the device)
+        until every remote consumer has finished tick - GT, the last tick that
+        read the slab generation this tick writes.  A consumer on this rank
+        needs no wait: its reads precede these writes on the stream."""
+        if self.world == 1 or tick < self.GT:
+            return
+        h = self._cur_stream_handle()
+        for m in self.remote_consumers():
+            ipc.wait_flag_bounded(h, self.credit[m].data_ptr(), tick - self.GT + 1, self.timeout_s,
+                                  self.timeout_word.data_ptr())
+
+    def release_slots(self, tick: int) -> None:
+        """After the last read of this tick's slabs (the tick's attention and
+        assembly, on the compute stream): tell every remote producer of each
+        consumer stage hosted here that ``tick``'s generation is free.  Written
+        every tick, active or not, so producers never wait on an idle stage."""
+        if self.world == 1:
+            return
+        h = self._cur_stream_handle()
+        for _m, addrs in sorted(self.credit_dst.items()):
+            for a in addrs:
+                ipc.stream_write_u32(h, a, tick + 1)
 
     def drain(self) -> None:
         """onesided.py:181-187: order later work after this tick's publications."""

@@ -88,6 +88,19 @@ def place_stages(rf_step: int, world: int) -> list[int]:
     return out
 
 
+def migration_plan(stage_rank: list[int], rf_step: int, num_blocks: int, t: int) -> list[tuple[int, int, int]]:
+    """Latent hand-offs after tick ``t``: (receiving stage, source rank,
+    destination rank) for every denoise stage s active at t (engine.py:214-219),
+    whose result feeds stage s + 1 at t + 1 (s + 1 = rf_step is the store).
+    Stage s active at t is exactly stage s + 1 active at t + 1, so every rank
+    derives the same list without communicating."""
+    out = []
+    for s in range(rf_step):
+        if 0 <= t - s < num_blocks:
+            out.append((s + 1, stage_rank[s], stage_rank[s + 1]))
+    return out
+
+
 class _StoreKV(list):
     """``store_kv`` of one tick for merged stages.  The store closure assigns
     ``(roped_key, unroped_key, value)`` per layer, [1, T, H, D] views that the
@@ -205,8 +218,12 @@ class WavefrontEngine:
                 exch = self.xport.make_store_exch(self.clean, store_kv, c, act, t, self._rope,
                                                   rope_tab_fn=self._rope_tab)
                 tasks.append(StageTask(self.inputs[s], cfg.context_noise, c * cfg.npb, s, exch))
+        # no publish of this tick may land in a slab generation that a remote
+        # consumer is still reading (it read that generation two ticks ago)
+        self.xport.acquire_slots(t)
         flows = self.m.forward_stages(tasks) if tasks else []
         self.xport.drain()
+        self.xport.release_slots(t)
         out = {}
         for task, flow in zip(tasks, flows):
             if task.stage < S:
@@ -248,25 +265,41 @@ class WavefrontEngine:
         return self.fm.add_noise(x0.float(), nz, self.cfg.steps[stage + 1]).to(torch.bfloat16)
 
     def _migrate(self, t, out: dict) -> None:
-        """Hand each denoise stage's result to the next stage (engine.py:516-555)."""
+        """Hand each denoise stage's result to the next stage (engine.py:516-555).
+
+        The reference gathers every rank's payload with a world all_gather per
+        tick (engine.py:550).  Here each result goes point to point: kept in
+        place when the next stage is on the same rank, otherwise one NCCL
+        send/recv between the two ranks (``migration_plan``); ranks without a
+        hand-off this tick take no part.  The all_gather also served the
+        reference as the credit for reusing a slab generation two ticks later;
+        that role is the transport's credit flags (``PagedTransport.
+        release_slots`` / ``acquire_slots``)."""
         S = self.S
         payload = {}
         for s, x0 in out.items():
             c = t - s
             payload[s + 1] = self._renoise(x0, s, c) if s < S - 1 else x0
-        if self.world == 1:
-            self.inputs.update(payload)
-            return
-        buf = torch.zeros(self.mig_shape, device=self.device, dtype=torch.bfloat16)
-        for dst, x in payload.items():
-            buf[dst].copy_(x)
-        gathered = torch.empty((self.world,) + self.mig_shape, device=self.device, dtype=torch.bfloat16)
-        dist.all_gather_into_tensor(gathered, buf, group=self.group)
-        for s in self.local:
-            if s >= 1:
-                src = self.stage_rank[s - 1]
-                if self.act_denoise(s, t + 1) or (s == self.store and self.act_store(t + 1)):
-                    self.inputs[s] = gathered[src, s].clone()
+        recv, ops = {}, []
+        for dst_stage, src_rank, dst_rank in migration_plan(self.stage_rank, S, self.cfg.num_blocks, t):
+            if src_rank == dst_rank:
+                if src_rank == self.rank:
+                    self.inputs[dst_stage] = payload[dst_stage]
+            elif src_rank == self.rank:
+                ops.append(dist.P2POp(dist.isend, payload[dst_stage].contiguous(), self._peer(dst_rank),
+                                      group=self.group))
+            elif dst_rank == self.rank:
+                buf = torch.empty(self.mig_shape[1:], device=self.device, dtype=torch.bfloat16)
+                ops.append(dist.P2POp(dist.irecv, buf, self._peer(src_rank), group=self.group))
+                recv[dst_stage] = buf
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        self.inputs.update(recv)
+
+    def _peer(self, r: int) -> int:
+        """Global rank of group rank ``r`` (P2POp addresses global ranks)."""
+        return r if self.group is None else dist.get_global_rank(self.group, r)
 
     def close(self) -> None:
         self.xport.close()
