@@ -78,6 +78,7 @@ def parse():
     ap.add_argument("--q-len", type=int, default=0,
                     help="--kernel attn: query length in tokens (default one chunk; 28080 = the tick's "
                          "batched cross-attention of six stages)")
+    ap.add_argument("--gemm-nk", default="", help="--kernel gemm: N,K (default the FFN fc_in)")
     ap.add_argument("--library", action="store_true",
                     help="--kernel attn: also time torch SDPA, the reference's attention call, on the same buffers")
     ap.add_argument("--trace", action="store_true",
@@ -835,16 +836,29 @@ def run_kernel_bench(args):
         unit, bound = "GB/s", "hbm"
         name = f"qk_norm_rope_publish {rows}x{3 * dim} (6 stages, {sum(ndst)} FP8 destinations)"
     elif args.kernel == "gemm":
-        set_bytes = T * cfg.dim + cfg.ffn * cfg.dim + 2 * T * cfg.ffn
-        for _ in range(n_sets(set_bytes)):
-            x = torch.randn(T, cfg.dim, device=dev, generator=g).bfloat16()
-            w = (torch.randn(cfg.ffn, cfg.dim, device=dev, generator=g) * 0.02).bfloat16()
+        # M = --q-len (default one chunk); N, K = --gemm-nk (default the FFN
+        # fc_in); the library leg is the bf16 linear it replaces (cuBLAS)
+        M = args.q_len if args.q_len > 0 else T
+        N, K = (int(x) for x in args.gemm_nk.split(",")) if args.gemm_nk else (cfg.ffn, cfg.dim)
+        set_bytes = M * K + N * K + 2 * M * N + (2 * M * K + 2 * N * K if args.library else 0)
+        for i in range(n_sets(set_bytes)):
+            x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+            w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
             wq, ws = kernels.weight_quant(w)
             xq, xs = kernels.act_quant(x)
-            out = torch.empty(T, cfg.ffn, device=dev, dtype=torch.bfloat16)
+            out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
             fns.append(lambda xq=xq, xs=xs, wq=wq, ws=ws, out=out: kernels.gemm_w8a8(xq, xs, wq, ws, None, out=out))
-        work, unit, bound = 2.0 * T * cfg.dim * cfg.ffn / 1e12, "TFLOP/s", "tensor"
-        name = f"gemm_w8a8 e4m3 {T}x{cfg.ffn}x{cfg.dim}"
+            if args.library:
+                ob = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                lib_fns.append(lambda x=x, w=w, ob=ob: torch.matmul(x, w.t(), out=ob))
+                if i == 0:
+                    ref = torch.matmul(x, w.t())
+                    lib_diff = float((kernels.gemm_w8a8(xq, xs, wq, ws, None).float() - ref.float()).abs().max()
+                                     / ref.float().abs().max())
+            else:
+                del x, w
+        work, unit, bound = 2.0 * M * N * K / 1e12, "TFLOP/s", "tensor"
+        name = f"gemm_w8a8 e4m3 {M}x{N}x{K}"
     elif args.kernel == "assemble":
         HD = H * D
         n_deq = 5
@@ -934,6 +948,7 @@ def run_kernel_bench(args):
     if lib_fns:
         lms = graph_ms(lib_fns)
         library = {"name": {"attn8": "per-token dequant to bf16 + bf16 wf_attn_fwd",
+                            "gemm": "bf16 torch.matmul of the same shape (cuBLAS)",
                             "qkpub": "wf_qk_norm_rope + wf_kv_quant_publish per stage (the unfused pair)"}.get(
                                 args.kernel, "torch SDPA, default dispatch (cuDNN on B200)"), "ms": lms,
                    "achieved": work / (lms * 1e-3), "max_abs_diff_vs_wf": lib_diff,
