@@ -69,8 +69,12 @@ def parse():
     ap.add_argument("--w8a8", default="none", choices=["none", "e4m3", "int8"])
     ap.add_argument("--denoise-steps", default="1000,800,600,400,200")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--vae", action="store_true",
+                    help="also run the whole wavefront with streaming VAE decode of every finished chunk "
+                         "(on ranks without stages when there are any, else on the store rank)")
     ap.add_argument("--kernel", default=None,
-                    choices=["attn", "attn8", "gemm", "codec", "dequant", "assemble", "publish", "qkpub"],
+                    choices=["attn", "attn8", "gemm", "actq", "codec", "dequant", "assemble", "publish", "qkpub",
+                             "vae"],
                     help="time one hot-path kernel alone at the steady r0 shape (for ncu captures)")
     ap.add_argument("--ctx-chunks", type=int, default=8, help="--kernel attn: K/V length in chunks")
     ap.add_argument("--kv-len", type=int, default=0,
@@ -79,6 +83,8 @@ def parse():
                     help="--kernel attn: query length in tokens (default one chunk; 28080 = the tick's "
                          "batched cross-attention of six stages)")
     ap.add_argument("--gemm-nk", default="", help="--kernel gemm: N,K (default the FFN fc_in)")
+    ap.add_argument("--act-k", type=int, default=0, help="--kernel actq: row length K (default the FFN width)")
+    ap.add_argument("--act-gelu", action="store_true", help="--kernel actq: quantise GELU_tanh(x) (fc_out's input)")
     ap.add_argument("--library", action="store_true",
                     help="--kernel attn: also time torch SDPA, the reference's attention call, on the same buffers")
     ap.add_argument("--trace", action="store_true",
@@ -462,9 +468,12 @@ def trace_ticks(args, make_engine, noise_cpu, fill, dev, rank, n_trace: int = 2)
     from torch.profiler import ProfilerActivity, profile
 
     eng = make_engine(noise_cpu.to(dev))
+    eng_local = eng.local
     for t in range(fill + max(1, args.warmup)):
         eng.tick(t)
     torch.cuda.synchronize()
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
     t0 = fill + max(1, args.warmup)
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         h0 = time.perf_counter()
@@ -499,6 +508,18 @@ def trace_ticks(args, make_engine, noise_cpu, fill, dev, rank, n_trace: int = 2)
     span = (ivs[-1][1] - ivs[0][0]) if ivs else 0.0
     total = sum(by_name.values())
     top = sorted(by_name.items(), key=lambda kv: -kv[1])[:16]
+    # every rank's own device activity (stages hosted, kernel-busy time per
+    # tick); waits in flag/credit kernels count as busy, so they are listed
+    wait_keys = ("wait_flag_kernel",)
+    waits = sum(v for k, v in by_name.items() if any(w in k for w in wait_keys))
+    mine = {"rank": rank, "stages": list(eng_local), "busy_ms_per_tick": busy / 1e3 / n_trace,
+            "flag_wait_ms_per_tick": waits / 1e3 / n_trace,
+            "busy_minus_waits_ms_per_tick": (busy - waits) / 1e3 / n_trace,
+            "nccl_ms_per_tick": sum(v for k, v in by_name.items() if "nccl" in k.lower()) / 1e3 / n_trace}
+    per_rank = [mine]
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        per_rank = [None] * dist.get_world_size()
+        dist.all_gather_object(per_rank, mine)
     if rank == 0:
         print(json.dumps({
             "trace": f"{n_trace} steady ticks, rank {rank}", "kernels": len(ivs),
@@ -506,6 +527,7 @@ def trace_ticks(args, make_engine, noise_cpu, fill, dev, rank, n_trace: int = 2)
             "busy_ms_per_tick": busy / 1e3 / n_trace, "idle_frac": 1 - busy / span if span else None,
             "kernel_sum_ms_per_tick": total / 1e3 / n_trace, "host_issue_ms_per_tick": host_ms / n_trace,
             "shares": [{"kernel": k, "ms_per_tick": v / 1e3 / n_trace, "share": v / total} for k, v in top],
+            "per_rank": per_rank,
             "note": "CUPTI kernel timestamps (profiler overhead on the host side; kernel durations in-stream)"}),
             flush=True)
 
@@ -660,6 +682,9 @@ def run_gpu_arm(args):
         eng.close()
         del eng
 
+    vae_e2e = run_vae_e2e(args, make_engine, noise_cpu, cfg, dev, rank, world, barrier, max_over_ranks) \
+        if args.vae else None
+
     peaks, src = _peaks()
     if rank == 0:
         achieved = a_flops / (a_ms * 1e-3) / 1e12 if a_ms > 0 else None
@@ -697,6 +722,7 @@ def run_gpu_arm(args):
             "cpu_baseline": cpu,
             "config1": config1,
             "e2e": e2e,
+            **({"e2e_with_vae": vae_e2e} if vae_e2e is not None else {}),
             "dit_fps": dit,
             "exchange": {"critical_rank_wait_ms_per_tick": crit,
                          "critical_frac_of_tick": crit / p50 if p50 else None,
@@ -859,6 +885,21 @@ def run_kernel_bench(args):
                 del x, w
         work, unit, bound = 2.0 * M * N * K / 1e12, "TFLOP/s", "tensor"
         name = f"gemm_w8a8 e4m3 {M}x{N}x{K}"
+    elif args.kernel == "actq":
+        # per-token activation quantiser: M = --q-len (default the N=1 tick's
+        # six stages), K = --act-k; bytes = bf16 read + codes + scales
+        M = args.q_len if args.q_len > 0 else 6 * T
+        Kq = args.act_k if args.act_k > 0 else cfg.ffn
+        act = L.WF_ACT_GELU_TANH if args.act_gelu else L.WF_ACT_NONE
+        set_bytes = M * Kq * 3 + 4 * M
+        for _ in range(n_sets(set_bytes)):
+            x = torch.randn(M, Kq, device=dev, generator=g).bfloat16()
+            xq = torch.empty(M, Kq, device=dev, dtype=torch.uint8)
+            xs = torch.empty(M, device=dev)
+            fns.append(lambda x=x, xq=xq, xs=xs: kernels.act_quant(x, L.WF_DTYPE_E4M3, xq, xs, activation=act))
+        work = set_bytes / 1e9
+        unit, bound = "GB/s", "hbm"
+        name = f"act_quant{' GELU_tanh' if args.act_gelu else ''} e4m3 {M}x{Kq}"
     elif args.kernel == "assemble":
         HD = H * D
         n_deq = 5
@@ -963,6 +1004,144 @@ def run_kernel_bench(args):
                       "frac": ach / peak, "peak_source": src + (" bf16 burst x2" if args.kernel == "gemm" else ""),
                       "launches": launches, "buffer_sets": len(fns), "status": L.status_take(),
                       **({"library": library} if library else {})}), flush=True)
+
+
+def run_vae_e2e(args, make_engine, noise_cpu, cfg, dev, rank, world, barrier, max_over_ranks):
+    """The whole 399-frame wavefront with streaming VAE decode: every chunk the
+    store finishes is decoded to 12 pixel frames (9 for the first chunk) and
+    read back to pinned host memory.
+    * Ranks that host no stage (2 of 8 GPUs at 5 steps) form a VAE pipeline,
+      as the reference runs its VAE on the spare GPUs (wave_rt/pipelines/
+      vae.py:42-207).  The store rank sends each finished latent chunk to the
+      first of them, and the units are split between them by FLOPs.
+    * Without idle ranks the store rank decodes after each tick, on its own
+      stream order.
+    FPS = pixel frames / wall time from the first tick to the last pixel
+    frame on the host, max over ranks."""
+    from waveforcing_b200.pipelines import vae as V
+
+    eng = make_engine(noise_cpu.pin_memory())
+    stage_ranks = sorted(set(eng.stage_rank))
+    vae_ranks = [r for r in range(world) if r not in stage_ranks]
+    store_rank = eng.stage_rank[eng.store]
+    torch.backends.cudnn.benchmark = True
+    dec = V.VAEDecoder.random(V.VAEConfig(), seed=0).for_gpu(dev) if (rank in vae_ranks or (
+        not vae_ranks and rank == store_rank)) else None
+    cuts = V.partition_units(dec.unit_flops(cfg.lat_h, cfg.lat_w), len(vae_ranks)) if (dec and vae_ranks) else None
+    pix_host = torch.empty((3, 12, 8 * cfg.lat_h, 8 * cfg.lat_w), dtype=torch.bfloat16).pin_memory()
+    frames = 0
+    nt = eng.num_ticks
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    if rank in vae_ranks:
+        k = vae_ranks.index(rank)
+        st = V.VAEPipelineStage(dec, cuts, k, vae_ranks)
+        if k == 0:
+            import torch.distributed as dist_
+
+            zbuf = torch.empty((cfg.in_ch, 3, cfg.lat_h, cfg.lat_w), dtype=torch.bfloat16, device=dev)
+            for _ in range(ecfg_blocks(eng)):
+                dist_.recv(zbuf, store_rank)
+                for y in st.push_latents(zbuf):
+                    if st.last:
+                        pix_host[:, :y.shape[2]].copy_(y[0], non_blocking=True)
+                        frames += y.shape[2]
+                    else:
+                        st.send_next(y)
+            if not st.last:
+                st.send_next(None)
+        else:
+            while True:
+                x = st.recv_prev()
+                if x is None:
+                    if not st.last:
+                        st.send_next(None)
+                    break
+                y = st.run(x)
+                if st.last:
+                    pix_host[:, :y.shape[2]].copy_(y[0], non_blocking=True)
+                    frames += y.shape[2]
+                else:
+                    st.send_next(y)
+    else:
+        stream = V.DecodeStream(dec) if dec is not None else None
+        for t in range(nt):
+            eng.tick(t)
+            c = t - eng.store
+            if c in eng.final:
+                z = eng.final.pop(c)
+                if stream is not None:
+                    y = stream.push(z)
+                    pix_host[:, :y.shape[1]].copy_(y, non_blocking=True)
+                    frames += y.shape[1]
+                elif rank == store_rank:
+                    import torch.distributed as dist_
+
+                    dist_.send(z.contiguous(), vae_ranks[0])
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    barrier()
+    wall = max_over_ranks([wall])[0]
+    frames = int(max_over_ranks([float(frames)])[0])
+    eng.close()
+    del eng
+    return {"value": frames / wall, "unit": "FPS", "pixel_frames": frames, "wall_s": wall,
+            "vae_ranks": vae_ranks if vae_ranks else [store_rank],
+            "vae_cuts": cuts, "definition": "pixel frames (1 + 4 x (399 - 1)) / wall time from the first tick to "
+                                            "the last decoded frame in host memory, max over ranks; host clock",
+            "decoder": "Wan2.1-shaped VAE decoder (dim 96, z 16), random-init, bf16 channels-last on cuDNN"}
+
+
+def ecfg_blocks(eng) -> int:
+    return eng.cfg.num_blocks
+
+
+def run_vae_bench(args):
+    """Streaming VAE decode of one finished chunk (3 latent frames at the
+    480x832 latent 60x104 -> 12 pixel frames) by the Wan2.1-shaped decoder
+    (waveforcing_b200/pipelines/vae.py), bf16 channels-last on cuDNN, in
+    steady state: the stream has already decoded frame 0 and earlier chunks.
+    CUDA events around each push, ``--steps`` chunks after ``--warmup``."""
+    from waveforcing_b200.pipelines import vae as V
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.backends.cudnn.benchmark = True
+    cfg = V.VAEConfig()
+    dec = V.VAEDecoder.random(cfg, seed=0).for_gpu(dev)
+    lh, lw = 60, 104
+    g = torch.Generator(device="cpu").manual_seed(0)
+    n = 1 + 3 * (args.warmup + args.steps)
+    z = torch.randn(cfg.z_dim, n, lh, lw, generator=g).to(dev, torch.bfloat16)
+    s = V.DecodeStream(dec)
+    s.push(z[:, :1])
+    f = 1
+    for _ in range(args.warmup):
+        s.push(z[:, f:f + 3])
+        f += 3
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    evs[0].record()
+    out_frames = 0
+    for i in range(args.steps):
+        y = s.push(z[:, f:f + 3])
+        out_frames += y.shape[1]
+        f += 3
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    p50 = statistics.median(ms)
+    flops = 3 * sum(dec.unit_flops(lh, lw))
+    peaks, src = _peaks()
+    ach = flops / (p50 * 1e-3) / 1e12
+    print(json.dumps({"kernel": "streaming VAE decode, one 3-latent-frame chunk (60x104 -> 12 frames of 480x832)",
+                      "ms": p50, "pixel_fps": 12 * 1000.0 / p50, "achieved": ach, "unit": "TFLOP/s",
+                      "peak": peaks["bf16_tflops"], "frac": ach / peaks["bf16_tflops"],
+                      "peak_source": src + " bf16_tflops", "flops_per_chunk": flops,
+                      "output_frames": out_frames, "steps": args.steps,
+                      "note": "cuDNN convolutions and torch SDPA (library calls); FLOPs counted analytically"}),
+          flush=True)
 
 
 def run_publish_bench(args):
@@ -1121,6 +1300,8 @@ def main():
         run_forward_bench(args)
     elif args.kernel == "publish":
         run_publish_bench(args)
+    elif args.kernel == "vae":
+        run_vae_bench(args)
     elif args.kernel:
         run_kernel_bench(args)
     elif args.impl == "reference":

@@ -239,6 +239,23 @@ int wf_ln_modulate_quant(const void* x, int64_t x_stride, const float* shift, co
 int wf_gate_residual(void* x, int64_t x_stride, const void* y, int64_t y_stride, const float* gate,
                      int64_t gate_stride, int64_t rows, int64_t dim, int64_t rows_per_stage, void* stream);
 
+/* wf_gate_residual fused with the row op that reads its result, so the new
+ * row is used from registers instead of being read back:
+ *   shift == scale == NULL, xq/x_scale set: per-token W8A8 quantisation of
+ *     the new x (as wf_act_quant), for the cross-attention q projection;
+ *   shift, scale and out set: LN-modulate of the new x to bf16 out [rows,
+ *     out_stride] (as wf_ln_modulate), for the FFN input and the next
+ *     layer's QKV input;
+ *   shift, scale, xq and x_scale set: the same quantised per token (as
+ *     wf_ln_modulate_quant).
+ * Exactly one of out / xq is given.  gate rows select their stage by
+ * gate_rows_per_stage, modulation rows by mod_rows_per_stage.  Every output,
+ * and x itself, equals the two-launch form bit for bit. */
+int wf_gate_residual_then(void* x, int64_t x_stride, const void* y, int64_t y_stride, const float* gate,
+                          int64_t gate_stride, int64_t gate_rows_per_stage, const float* shift, const float* scale,
+                          int64_t mod_stride, int64_t mod_rows_per_stage, float eps, void* out, int64_t out_stride,
+                          void* xq, float* x_scale, int qtype, int64_t rows, int64_t dim, void* stream);
+
 /* From the fused QKV GEMM output qkv [rows, ld] (q at column 0, k at dim):
  * RMSNorm over dim (rounded to bf16, then times the bf16 weight, as
  * naive_rt/rolling_forcing/wan/modules/model.py:70-88) followed by interleaved

@@ -96,6 +96,13 @@ def test_constants_match_the_header():
     ("wf_rope_apply", (None, None, None, None, 4, 2, 128, 256, 256, None), 1),
     ("wf_ln_modulate", (None, 16, None, None, 16, None, 16, 4, 16, 4, 1e-6, None), 1),
     ("wf_gate_residual", (None, 16, None, 16, None, 16, 4, 16, 4, None), 1),
+    # gate_residual_then: both outputs, shift without scale, unknown qtype
+    ("wf_gate_residual_then", (16, 16, 16, 16, 16, 16, 4, 16, 16, 16, 4, 1e-6, 16, 16, 16, 16, 1, 4, 1536, None),
+     1),
+    ("wf_gate_residual_then", (16, 16, 16, 16, 16, 16, 4, 16, None, 16, 4, 1e-6, 16, 16, None, None, 1, 4, 1536,
+                               None), 1),
+    ("wf_gate_residual_then", (16, 16, 16, 16, 16, 16, 4, None, None, 0, 1, 1e-6, None, 16, 16, 16, 7, 4, 1536,
+                               None), 2),
     ("wf_rms_norm", (None, 16, None, None, 16, 4, 16, 1e-6, None), 1),
     ("wf_ipc_close", (None,), 1),
     ("wf_stream_write_u32", (None, 18, 1), 1),                                # misaligned flag address

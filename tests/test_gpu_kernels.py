@@ -7,6 +7,7 @@ Tolerances (stated per BASELINE north_star):
 """
 
 import math
+import os
 
 import numpy as np
 import pytest
@@ -22,6 +23,7 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
 
 DEV = "cuda"
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _kernels():
@@ -327,11 +329,12 @@ def test_kv_quant_publish_matches_oracle(n_dst):
 
 # ----------------------------------------------------------------------- W8A8
 @pytest.mark.parametrize("qtype", ["e4m3", "s8"])
-@pytest.mark.parametrize("Kd", [256, 1536, 5120, 8960])
+@pytest.mark.parametrize("Kd", [256, 1536, 4104, 5120, 8960, 13824])
 def test_quantisers_bit_exact(qtype, Kd):
     """Weight and activation quantisers against the oracle; K covers the
-    register-resident rows (1536, 5120) and the two-pass rows (256, 8960);
-    activations include wide magnitudes, zero rows and -0."""
+    warp-per-row kernel with the row in registers (1536) or read twice (256)
+    and the CTA-per-row kernel for wide rows (4104: a ragged last thread;
+    5120, 8960, 13824); activations include wide magnitudes, zero rows and -0."""
     K = _kernels()
     from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
 
@@ -355,7 +358,10 @@ def test_quantisers_bit_exact(qtype, Kd):
 
 @pytest.mark.parametrize("qtype", ["e4m3", "s8"])
 @pytest.mark.parametrize("M,N,K_", [(128, 256, 128), (300, 512, 384), (4680, 1536, 1536), (77, 96, 256),
-                                    (500, 13824, 5120), (300, 5120, 13824)])
+                                    (500, 13824, 5120), (300, 5120, 13824),
+                                    # M >= 1024 and K >= 4096: CTA-pair tiles (256 x 256); ragged M and N,
+                                    # one pair tile, the fc_out shape
+                                    (1100, 400, 4096), (1024, 256, 4608), (2049, 1536, 8960)])
 def test_gemm_w8a8_matches_oracle(qtype, M, N, K_):
     K = _kernels()
     from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
@@ -374,16 +380,56 @@ def test_gemm_w8a8_matches_oracle(qtype, M, N, K_):
     assert _rel(_f32(y), ref) <= 1e-2
 
 
+_PAIR_SCRIPT = r"""
+import sys, numpy as np, torch
+from waveforcing_b200 import kernels as K
+from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
+qt = WF_DTYPE_E4M3 if sys.argv[1] == "e4m3" else WF_DTYPE_S8
+g = torch.Generator(device="cuda").manual_seed(7)
+x = torch.randn(3000, 1536, device="cuda", generator=g).bfloat16()
+w = (torch.randn(4608, 1536, device="cuda", generator=g) * 0.02).bfloat16()
+b = (torch.randn(4608, device="cuda", generator=g) * 0.1).bfloat16()
+wq, ws = K.weight_quant(w, qt)
+xq, xs = K.act_quant(x, qt)
+y = K.gemm_w8a8(xq, xs, wq, ws, b, qt)
+np.save(sys.argv[2], y.float().cpu().numpy())
+"""
+
+
 @pytest.mark.parametrize("qtype", ["e4m3", "s8"])
-def test_gemm_w8a8_gelu_epilogue(qtype):
+def test_gemm_pair_matches_single_cta(qtype, tmp_path):
+    """The CTA-pair kernel (WFK_GEMM_PAIR=1) against the one-CTA kernel
+    (WFK_GEMM_PAIR=0) on the same inputs, each in its own process: both accumulate every
+    output in f32 (s32) over the same k order; outputs agree to one bf16 ulp."""
+    import subprocess
+    import sys
+
+    outs = []
+    for env_pair in ("1", "0"):  # forced on (the shape's K would pick one CTA per tile), then off
+        f = tmp_path / f"y{env_pair}.npy"
+        env = dict(os.environ, WFK_GEMM_PAIR=env_pair)
+        r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, qtype, str(f)], env=env, capture_output=True,
+                           text=True, timeout=300, cwd=ROOT)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(np.load(f))
+    a, b = outs
+    assert np.all(np.isfinite(a)) and np.abs(a).max() > 0
+    assert np.all(np.abs(a - b) <= np.abs(b) * 2.0**-7 + 1e-6)
+
+
+@pytest.mark.parametrize("qtype", ["e4m3", "s8"])
+@pytest.mark.parametrize("M_", [600, 1300])
+def test_gemm_w8a8_gelu_epilogue(qtype, M_):
     """fc_in + GELU(tanh) in one kernel against the oracle linear followed by
-    torch's tanh GELU on the bf16-rounded output."""
+    torch's tanh GELU on the bf16-rounded output (600 and 1300 rows; the
+    pair kernel's GELU epilogue is the same code, covered through the
+    WFK_GEMM_PAIR test)."""
     K = _kernels()
     from waveforcing_b200._lib import WF_ACT_GELU_TANH, WF_DTYPE_E4M3, WF_DTYPE_S8
 
     qt = WF_DTYPE_E4M3 if qtype == "e4m3" else WF_DTYPE_S8
     rng = np.random.default_rng(31)
-    M, N, K_ = 600, 8960, 1536
+    M, N, K_ = M_, 8960, 1536
     w = o_codec.bf16_round((rng.standard_normal((N, K_)) * 0.02).astype(np.float32))
     x = o_codec.bf16_round((rng.standard_normal((M, K_)) * 2).astype(np.float32))
     b = o_codec.bf16_round((rng.standard_normal(N) * 0.1).astype(np.float32))
@@ -401,9 +447,11 @@ def test_gemm_w8a8_gelu_epilogue(qtype):
 @pytest.mark.parametrize("Kd", [1536, 8960, 13824])
 def test_act_quant_with_gelu_input(qtype, Kd):
     """Per-token quantisation of bf16(GELU_tanh(x)) against the oracle applied
-    to the exactly computed GELU.  The kernel's tanh is the MUFU approximation
-    (relative error 2^-11), so a code may differ where the bf16 rounding of the
-    activation flips: at most 1 in 1000 codes, each by one step."""
+    to the exactly computed GELU.  The kernel evaluates x / (1 + e^(-2u)) with
+    ex2.approx and an approximate reciprocal (rcp.approx, or Newton steps on
+    the FMA pipe for the wide rows), so a code may differ where the bf16
+    rounding of the activation flips: at most 1 in 1000 codes, each by one
+    step."""
     K = _kernels()
     from waveforcing_b200._lib import WF_ACT_GELU_TANH, WF_DTYPE_E4M3, WF_DTYPE_S8
 
@@ -622,6 +670,43 @@ def test_ln_modulate_quant_matches_separate_passes(dim, qtype):
     h = K.ln_modulate(x, e[:, 0], e[:, 1], T, 1e-6)
     rq, rs = K.act_quant(h, qt)
     assert torch.equal(xq, rq) and torch.equal(xs, rs)
+    assert L.status_take() == 0
+
+
+@pytest.mark.parametrize("dim", [256, 1536, 5120])
+@pytest.mark.parametrize("mode", ["quant", "ln", "ln_quant_e4m3", "ln_quant_s8"])
+def test_gate_residual_then_matches_two_launches(dim, mode):
+    """wf_gate_residual_then: the updated x and its output (per-token codes and
+    scales, LN-modulate, or LN-modulate quantised) bit-identical to
+    wf_gate_residual followed by wf_act_quant / wf_ln_modulate /
+    wf_ln_modulate_quant; per-stage gates and modulation over three stages."""
+    from waveforcing_b200 import _lib as L
+
+    K = _kernels()
+    torch.manual_seed(dim + 11)
+    S, T = 3, 40
+    x0 = (torch.randn(S * T, dim, device=DEV) * 3).bfloat16()
+    y = (torch.randn(S * T, dim, device=DEV) * torch.rand(S * T, 1, device=DEV) * 2).bfloat16()
+    x0[9] = 0
+    y[9] = 0  # an all-zero row after the residual
+    g = torch.randn(S, dim, device=DEV) * 0.5
+    e = torch.randn(S, 6, dim, device=DEV) * 0.3
+    qt = L.WF_DTYPE_S8 if mode.endswith("s8") else L.WF_DTYPE_E4M3
+    xa = x0.clone()
+    K.gate_residual(xa, y, g, T)
+    xb = x0.clone()
+    if mode == "quant":
+        got = K.gate_residual_then(xb, y, g, T, quant=True, qtype=qt)
+        want = K.act_quant(xa, qt)
+    elif mode == "ln":
+        got = (K.gate_residual_then(xb, y, g, T, e[:, 3], e[:, 4], T, 1e-6),)
+        want = (K.ln_modulate(xa, e[:, 3], e[:, 4], T, 1e-6),)
+    else:
+        got = K.gate_residual_then(xb, y, g, T, e[:, 0], e[:, 1], T, 1e-6, quant=True, qtype=qt)
+        want = K.ln_modulate_quant(xa, e[:, 0], e[:, 1], T, 1e-6, qt)
+    assert torch.equal(xa, xb)
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
     assert L.status_take() == 0
 
 

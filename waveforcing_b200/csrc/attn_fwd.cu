@@ -528,9 +528,24 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
           for (int i = 0; i < KH; ++i)
             if (i >= kvalid) s[i] = -INFINITY;
         }
-        float mx = s[0];
+        // Row max of the 128 scores as four independent 3-input max chains
+        // (chain c takes keys c, c + 4, c + 8, ...) joined at the end: 19
+        // dependent steps instead of 127.  (Eight chains spill under the
+        // softmax warpgroups' register budget.)
+        static_assert(KH == 128, "max chains cover 128 keys");
+        float mx;
+        {
+          constexpr int NC = 4;
+          float mc[NC];
 #pragma unroll
-        for (int i = 1; i < KH; ++i) mx = fmaxf(mx, s[i]);
+          for (int c = 0; c < NC; ++c) mc[c] = fmaxf(s[c], s[NC + c]);
+#pragma unroll
+          for (int i = 2 * NC; i < KH; i += 2 * NC) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c) mc[c] = fmax3(mc[c], s[i + c], s[i + NC + c]);
+          }
+          mx = fmaxf(fmax3(mc[0], mc[1], mc[2]), mc[3]);
+        }
         // Row max across the two halves.  The exchange slot is reused every
         // tile: the next S tile (and with it this thread's next write) waits on
         // bar_sfree, which every thread passes only after its read below.
@@ -552,7 +567,19 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
         }
         const float2 sc2 = make_float2(scale_log2, scale_log2);
         const float2 nm2 = make_float2(-m_new, -m_new);
-        float2 sum2 = make_float2(0.f, 0.f);
+        // four partial row sums, so the additions do not form one 64-long chain
+        constexpr int NSUM = 4;
+        float2 sum_a = make_float2(0.f, 0.f), sum_b = sum_a, sum_c = sum_a, sum_d = sum_a;
+        auto add_sum = [&](int i, float2 pr) {
+          if (NSUM == 1 || (i & 3) == 0)
+            sum_a = fadd2(sum_a, pr);
+          else if ((i & 3) == 1)
+            sum_b = fadd2(sum_b, pr);
+          else if ((i & 3) == 2)
+            sum_c = fadd2(sum_c, pr);
+          else
+            sum_d = fadd2(sum_d, pr);
+        };
         uint32_t pk[KH / 2];
         if constexpr (PX) {
           // P = 2^(s * scale_log2 - m) on MUFU's packed 16-bit path: the
@@ -572,7 +599,7 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
               asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(p) : "r"(pack_bf16x2(x.x, x.y)));
               pr = make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u));
             }
-            sum2 = fadd2(sum2, pr);
+            add_sum(i, pr);
             pk[i] = p;
           }
         } else {
@@ -589,11 +616,13 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
               pr.x = ex2_approx(x.x);
               pr.y = ex2_approx(x.y);
             }
-            sum2 = fadd2(sum2, pr);
+            add_sum(i, pr);
             pk[i] = KV8 ? pack_f16x2(pr.x, pr.y) : pack_bf16x2(pr.x, pr.y);
           }
         }
-        const float sum = sum2.x + sum2.y;
+        float2 sumv = sum_a;
+        if constexpr (NSUM == 4) sumv = fadd2(fadd2(sum_a, sum_b), fadd2(sum_c, sum_d));
+        const float sum = sumv.x + sumv.y;
         const float alpha = grow ? ex2_approx(m_run - m_new) : 1.f;
         // P and O may only be written once PV_{j-1} has completed.  This
         // parity wait is unambiguous: S_j's commit (one issuing thread, in

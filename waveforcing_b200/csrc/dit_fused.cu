@@ -44,81 +44,21 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// NCH = dim / 256 chunks of 8 elements per lane
+// ---- row helpers: one warp holds a row of NCH * 256 elements, lane l the
+// 8-element chunks l, l + 32, ...; every kernel below is built from these,
+// so fused and unfused paths compute identical values.
+
+// out = LN(v) * (1 + scale[st]) + shift[st], rounded to bf16 (packed)
 template <int NCH>
-__global__ void __launch_bounds__(256) ln_modulate_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs,
-                                                          const float* __restrict__ shift,
-                                                          const float* __restrict__ scale, int64_t mod_stride,
-                                                          __nv_bfloat16* __restrict__ out, int64_t os, int64_t rows,
-                                                          int64_t rows_per_stage, float eps) {
-  const int lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (r >= rows) return;
+__device__ __forceinline__ void row_ln_modulate(const float (&v)[NCH][8], const float* __restrict__ shift,
+                                                const float* __restrict__ scale, int64_t st, int64_t mod_stride,
+                                                float eps, int lane, uint4 (&packed)[NCH]) {
   constexpr int DIM = NCH * 256;
-  float v[NCH][8];
-  const uint4* xr = reinterpret_cast<const uint4*>(x + r * xs);
-  float s = 0.f;
-#pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    unpack8(__ldg(xr + lane + 32 * c), v[c]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += v[c][i];
-  }
-  const float mean = warp_sum(s) * (1.f / DIM);
-  float q = 0.f;
+  float sum = 0.f;
 #pragma unroll
   for (int c = 0; c < NCH; ++c)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float d = v[c][i] - mean;
-      q = fmaf(d, d, q);
-    }
-  const float rstd = rsqrtf(warp_sum(q) * (1.f / DIM) + eps);
-  const int64_t st = r / rows_per_stage;
-  const float4* sh4 = reinterpret_cast<const float4*>(shift + st * mod_stride);
-  const float4* sc4 = reinterpret_cast<const float4*>(scale + st * mod_stride);
-  uint4* orow = reinterpret_cast<uint4*>(out + r * os);
-#pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int e = (lane + 32 * c) * 2;  // float4 index of this chunk's first element
-    const float4 a0 = __ldg(sc4 + e), a1 = __ldg(sc4 + e + 1);
-    const float4 b0 = __ldg(sh4 + e), b1 = __ldg(sh4 + e + 1);
-    const float sc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const float sf[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-    float o[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = fmaf((v[c][i] - mean) * rstd, 1.f + sc[i], sf[i]);
-    orow[lane + 32 * c] = pack8(o);
-  }
-}
-
-// ln_modulate_kernel fused with the per-token W8A8 activation quantiser of
-// the linear that reads its output (the QKV projection, FFN fc_in): the row
-// of bf16-rounded outputs stays in registers, its amax gives the row scale,
-// and only codes (e4m3, or int8 when I8) and the scale are written.  The
-// quantisation is act_quant_kernel's (gemm_w8a8.cu, the same row helpers),
-// so the codes and scales equal wf_act_quant(wf_ln_modulate(x)) bit for bit
-// while the bf16 output is neither written nor read back.
-template <int NCH, bool I8>
-__global__ void __launch_bounds__(256) ln_modulate_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs,
-                                                                const float* __restrict__ shift,
-                                                                const float* __restrict__ scale, int64_t mod_stride,
-                                                                uint8_t* __restrict__ xq, float* __restrict__ x_scale,
-                                                                int64_t rows, int64_t rows_per_stage, float eps) {
-  using namespace wfk::quant;
-  const int lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (r >= rows) return;
-  constexpr int DIM = NCH * 256;
-  float v[NCH][8];
-  const uint4* xr = reinterpret_cast<const uint4*>(x + r * xs);
-  float sum = 0.f;
-#pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    unpack8(__ldg(xr + lane + 32 * c), v[c]);
-#pragma unroll
     for (int i = 0; i < 8; ++i) sum += v[c][i];
-  }
   const float mean = warp_sum(sum) * (1.f / DIM);
   float q2 = 0.f;
 #pragma unroll
@@ -129,14 +69,11 @@ __global__ void __launch_bounds__(256) ln_modulate_quant_kernel(const __nv_bfloa
       q2 = fmaf(d, d, q2);
     }
   const float rstd = rsqrtf(warp_sum(q2) * (1.f / DIM) + eps);
-  const int64_t st = r / rows_per_stage;
   const float4* sh4 = reinterpret_cast<const float4*>(shift + st * mod_stride);
   const float4* sc4 = reinterpret_cast<const float4*>(scale + st * mod_stride);
-  uint4 packed[NCH];
-  uint32_t m2 = 0;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const int e = (lane + 32 * c) * 2;
+    const int e = (lane + 32 * c) * 2;  // float4 index of this chunk's first element
     const float4 a0 = __ldg(sc4 + e), a1 = __ldg(sc4 + e + 1);
     const float4 b0 = __ldg(sh4 + e), b1 = __ldg(sh4 + e + 1);
     const float sc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
@@ -145,10 +82,21 @@ __global__ void __launch_bounds__(256) ln_modulate_quant_kernel(const __nv_bfloa
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = fmaf((v[c][i] - mean) * rstd, 1.f + sc[i], sf[i]);
     packed[c] = pack8(o);
-    m2 = amax8_bits(packed[c], m2);
   }
+}
+
+// Per-token W8A8 quantisation of a bf16 row (act_quant_kernel's arithmetic,
+// gemm_w8a8.cu, from the same quant_rows.cuh helpers): codes to xq_row, the
+// scale to *x_scale (lane 0).
+template <int NCH, bool I8>
+__device__ __forceinline__ void row_quant_store(const uint4 (&packed)[NCH], uint8_t* __restrict__ xq_row,
+                                                float* __restrict__ x_scale, int lane) {
+  using namespace wfk::quant;
+  uint32_t m2 = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) m2 = amax8_bits(packed[c], m2);
   const RowQuant q = make_rowq(warp_amax_bits(m2), I8 ? 127.f : 448.f);
-  uint2* out = reinterpret_cast<uint2*>(xq + r * DIM);
+  uint2* out = reinterpret_cast<uint2*>(xq_row);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const uint4& pv = packed[c];
@@ -174,7 +122,105 @@ __global__ void __launch_bounds__(256) ln_modulate_quant_kernel(const __nv_bfloa
     }
     out[lane + 32 * c] = code;
   }
-  if (lane == 0) x_scale[r] = q.s;
+  if (lane == 0) *x_scale = q.s;
+}
+
+// NCH = dim / 256 chunks of 8 elements per lane
+template <int NCH>
+__global__ void __launch_bounds__(256) ln_modulate_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs,
+                                                          const float* __restrict__ shift,
+                                                          const float* __restrict__ scale, int64_t mod_stride,
+                                                          __nv_bfloat16* __restrict__ out, int64_t os, int64_t rows,
+                                                          int64_t rows_per_stage, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  float v[NCH][8];
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * xs);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) unpack8(__ldg(xr + lane + 32 * c), v[c]);
+  uint4 packed[NCH];
+  row_ln_modulate<NCH>(v, shift, scale, r / rows_per_stage, mod_stride, eps, lane, packed);
+  uint4* orow = reinterpret_cast<uint4*>(out + r * os);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) orow[lane + 32 * c] = packed[c];
+}
+
+// ln_modulate_kernel fused with the per-token W8A8 activation quantiser of
+// the linear that reads its output (the QKV projection, FFN fc_in): the row
+// of bf16-rounded outputs stays in registers, its amax gives the row scale,
+// and only codes (e4m3, or int8 when I8) and the scale are written, equal to
+// wf_act_quant(wf_ln_modulate(x)) bit for bit.
+template <int NCH, bool I8>
+__global__ void __launch_bounds__(256) ln_modulate_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs,
+                                                                const float* __restrict__ shift,
+                                                                const float* __restrict__ scale, int64_t mod_stride,
+                                                                uint8_t* __restrict__ xq, float* __restrict__ x_scale,
+                                                                int64_t rows, int64_t rows_per_stage, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  float v[NCH][8];
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * xs);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) unpack8(__ldg(xr + lane + 32 * c), v[c]);
+  uint4 packed[NCH];
+  row_ln_modulate<NCH>(v, shift, scale, r / rows_per_stage, mod_stride, eps, lane, packed);
+  row_quant_store<NCH, I8>(packed, xq + r * (NCH * 256), x_scale + r, lane);
+}
+
+// The gated residual x = bf16(x + y * gate[st]) (written back), then from the
+// new row in registers, without reading it again:
+//   MODE 0  its per-token quantisation (the cross-attention q projection's
+//           W8A8 input), codes to xq and scales to x_scale;
+//   MODE 1  LN-modulate with (shift, scale) to bf16 `out` (the FFN input, the
+//           next layer's QKV input);
+//   MODE 2  LN-modulate quantised per token (the same for W8A8 linears).
+// Each output equals its two-launch form (wf_gate_residual, then
+// wf_act_quant / wf_ln_modulate / wf_ln_modulate_quant) bit for bit.
+template <int NCH, int MODE, bool I8>
+__global__ void __launch_bounds__(256)
+    gate_residual_then_kernel(__nv_bfloat16* __restrict__ x, int64_t xs, const __nv_bfloat16* __restrict__ y,
+                              int64_t ys, const float* __restrict__ gate, int64_t gate_stride,
+                              const float* __restrict__ shift, const float* __restrict__ scale, int64_t mod_stride,
+                              __nv_bfloat16* __restrict__ out, int64_t os, uint8_t* __restrict__ xq,
+                              float* __restrict__ x_scale, int64_t rows, int64_t gate_rows_per_stage,
+                              int64_t mod_rows_per_stage, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  uint4* xr = reinterpret_cast<uint4*>(x + r * xs);
+  const uint4* yr = reinterpret_cast<const uint4*>(y + r * ys);
+  const float4* g4 = reinterpret_cast<const float4*>(gate + (r / gate_rows_per_stage) * gate_stride);
+  float v[NCH][8];
+  uint4 xn[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float a[8], b[8];
+    unpack8(xr[lane + 32 * c], a);
+    unpack8(__ldg(yr + lane + 32 * c), b);
+    const int e = (lane + 32 * c) * 2;
+    const float4 g0 = __ldg(g4 + e), g1 = __ldg(g4 + e + 1);
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = fmaf(b[i], g[i], a[i]);
+    xn[c] = pack8(a);
+    xr[lane + 32 * c] = xn[c];
+    unpack8(xn[c], v[c]);  // the bf16-rounded row, as a second kernel would read it
+  }
+  if constexpr (MODE == 0) {
+    row_quant_store<NCH, I8>(xn, xq + r * (NCH * 256), x_scale + r, lane);
+  } else {
+    uint4 packed[NCH];
+    row_ln_modulate<NCH>(v, shift, scale, r / mod_rows_per_stage, mod_stride, eps, lane, packed);
+    if constexpr (MODE == 1) {
+      uint4* orow = reinterpret_cast<uint4*>(out + r * os);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) orow[lane + 32 * c] = packed[c];
+    } else {
+      row_quant_store<NCH, I8>(packed, xq + r * (NCH * 256), x_scale + r, lane);
+    }
+  }
 }
 
 // x[r] = bf16(x[r] + y[r] * gate[stage])   (f32 math)
@@ -370,6 +416,55 @@ extern "C" int wf_gate_residual(void* x, int64_t x_stride, const void* y, int64_
     gate_residual_kernel<decltype(n)::value><<<blocks, 256, 0, s>>>(
         static_cast<__nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(y), y_stride, gate,
         gate_stride, rows, rows_per_stage);
+  });
+  if (rc != WF_OK) return rc;
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_gate_residual_then(void* x, int64_t x_stride, const void* y, int64_t y_stride,
+                                     const float* gate, int64_t gate_stride, int64_t gate_rows_per_stage,
+                                     const float* shift, const float* scale, int64_t mod_stride,
+                                     int64_t mod_rows_per_stage, float eps, void* out, int64_t out_stride, void* xq,
+                                     float* x_scale, int qtype, int64_t rows, int64_t dim, void* stream) {
+  const bool mod = shift != nullptr || scale != nullptr;
+  if (!x || !y || !gate || rows < 0 || gate_rows_per_stage < 1 || !aligned16(x) || !aligned16(y) ||
+      !aligned16(gate) || x_stride % 8 || y_stride % 8 || gate_stride % 4)
+    return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: bad residual arguments");
+  if (mod && (!shift || !scale || !aligned16(shift) || !aligned16(scale) || mod_stride % 4 || mod_rows_per_stage < 1))
+    return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: shift and scale go together (16-byte aligned)");
+  if ((out != nullptr) == (xq != nullptr))
+    return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: exactly one of out / xq");
+  if (!mod && !xq) return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: without modulation only xq output");
+  if (out && (!aligned16(out) || out_stride % 8))
+    return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: out must be 16-byte aligned rows");
+  if (xq && (!x_scale || !aligned16(xq)))
+    return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: xq (16-byte aligned) needs x_scale");
+  if (xq && qtype != WF_DTYPE_E4M3 && qtype != WF_DTYPE_S8)
+    return fail(WF_ERR_UNSUPPORTED, "wf_gate_residual_then: qtype must be WF_DTYPE_E4M3 or WF_DTYPE_S8");
+  if (rows == 0) return WF_OK;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int mode = !mod ? 0 : (out ? 1 : 2);
+  const bool i8 = qtype == WF_DTYPE_S8;
+  auto bx = static_cast<__nv_bfloat16*>(x);
+  auto by = static_cast<const __nv_bfloat16*>(y);
+  auto bo = static_cast<__nv_bfloat16*>(out);
+  auto bq = static_cast<uint8_t*>(xq);
+  int rc = by_dim(dim, [&](auto n) {
+    constexpr int N = decltype(n)::value;
+#define WFK_GRT(M, I)                                                                                           \
+  gate_residual_then_kernel<N, M, I><<<blocks, 256, 0, s>>>(bx, x_stride, by, y_stride, gate, gate_stride, shift, \
+                                                            scale, mod_stride, bo, out_stride, bq, x_scale, rows, \
+                                                            gate_rows_per_stage, mod_rows_per_stage, eps)
+    if (mode == 0) {
+      if (i8) WFK_GRT(0, true); else WFK_GRT(0, false);
+    } else if (mode == 1) {
+      WFK_GRT(1, false);
+    } else {
+      if (i8) WFK_GRT(2, true); else WFK_GRT(2, false);
+    }
+#undef WFK_GRT
   });
   if (rc != WF_OK) return rc;
   WFK_CUDA_TRY(cudaGetLastError());

@@ -341,6 +341,46 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, rows_per
     return x
 
 
+def gate_residual_then(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, gate_rows_per_stage: int,
+                       shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+                       mod_rows_per_stage: int = 1, eps: float = 1e-6, quant: bool = False,
+                       qtype: int = L.WF_DTYPE_E4M3):
+    """x += y * gate[s] in place, then from the new rows without reading them
+    back: with shift/scale, LN-modulate to a new bf16 [rows, dim] (or, with
+    ``quant``, its per-token W8A8 codes and scales); without, the per-token
+    quantisation of x itself (``quant`` implied).  Returns the bf16 output or
+    (codes uint8 [rows, dim], scales f32 [rows])."""
+    _check(x.dim() == 2 and y.shape == x.shape and x.dtype == y.dtype == torch.bfloat16,
+           "gate_residual_then: x and y must be bf16 matrices of one shape")
+    rows, dim = x.shape
+    _check(gate.dtype == torch.float32 and gate.shape[-1] == dim and gate.stride(-1) == 1
+           and (gate.dim() == 1 or (gate.dim() == 2 and gate.shape[0] * gate_rows_per_stage >= rows)),
+           "gate_residual_then: gate must be f32 [dim] or [stages, dim]")
+    mod = shift is not None or scale is not None
+    if mod:
+        for t in (shift, scale):
+            _check(t is not None and t.dtype == torch.float32 and t.dim() == 2 and t.shape[1] == dim
+                   and t.stride(1) == 1 and t.shape[0] * mod_rows_per_stage >= rows,
+                   "gate_residual_then: shift/scale must be f32 [stages, dim]")
+        _check(shift.stride(0) == scale.stride(0), "gate_residual_then: shift and scale must share their row stride")
+    _need_cuda(x, y)
+    gs = gate.stride(0) if gate.dim() == 2 else 0
+    quant = quant or not mod
+    out = xq = xs = None
+    if quant:
+        xq = torch.empty((rows, dim), device=x.device, dtype=torch.uint8)
+        xs = torch.empty((rows,), device=x.device, dtype=torch.float32)
+    else:
+        out = torch.empty((rows, dim), device=x.device, dtype=torch.bfloat16)
+    L.check(L.lib().wf_gate_residual_then(
+        x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), gate.data_ptr(), gs, gate_rows_per_stage,
+        shift.data_ptr() if mod else None, scale.data_ptr() if mod else None, shift.stride(0) if mod else 0,
+        mod_rows_per_stage, eps, out.data_ptr() if out is not None else None, dim,
+        xq.data_ptr() if quant else None, xs.data_ptr() if quant else None, qtype, rows, dim, _stream()),
+        "wf_gate_residual_then")
+    return (xq, xs) if quant else out
+
+
 def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor, cos: torch.Tensor,
                  sin: torch.Tensor, head_dim: int, rows_per_stage: int, eps: float, want_unroped: bool = True):
     """Fused RMSNorm(q), RMSNorm(k) + RoPE from the fused QKV GEMM output.
