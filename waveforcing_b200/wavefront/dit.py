@@ -335,13 +335,41 @@ class WanDiT(nn.Module):
                 return lin.gemm_q(xq, xsc)
             return _lin(lin, ln_mod(inp, e_all, k_shift))
 
+        def gate_then_mod(inp, y, gate_all, kg, e_all, k_shift, quant, qtype):
+            """gate_add(inp, y, gate_all, kg) in place, then ln_mod of the new rows
+            (quantised per token when ``quant``) in one kernel."""
+            g = gate_all[:, kg] if gate_all is not None else ones
+            grs = T if gate_all is not None else S * T
+            return kernels.gate_residual_then(inp, y, g, grs, e_all[:, k_shift], e_all[:, k_shift + 1], T, eps,
+                                              quant=quant, qtype=qtype)
+
+        # With the fused kernels each gated residual is applied by the kernel
+        # that reads its result: the FFN's residual of layer li by layer li+1's
+        # LN-modulate (pending), the self-attention's by the cross-attention
+        # q quantiser when that linear is W8A8, the cross-attention's by the
+        # FFN's LN-modulate.
+        pending = None  # (y, e_all) of the previous layer's FFN residual, not yet added (gate e_all[:, 5])
         for li, b in enumerate(self.blocks):
             e_all = (b.modulation.float() + mods).contiguous()  # [S, 6, dim]
             fq = None if (separate_qkv and not fused) else self._fused_qkv(b)
             qkv_w8 = fused and fq is not None and not isinstance(fq[0], torch.Tensor) and w8a8_channel(fq[0])
-            h = None if qkv_w8 else ln_mod(xs, e_all, 0)
-            if fused and fq is not None:
+            if fused and fq is not None and pending is not None:
+                yp, gp_all = pending
+                pending = None
+                if qkv_w8:
+                    xq, xsc = gate_then_mod(xs, yp, gp_all, 5, e_all, 0, True, fq[0].qtype)
+                    qkv = fq[0].gemm_q(xq, xsc)
+                else:
+                    qkv = self._qkv_gemm(fq, gate_then_mod(xs, yp, gp_all, 5, e_all, 0, False, 0))
+            elif fused and fq is not None:
+                h = None if qkv_w8 else ln_mod(xs, e_all, 0)
                 qkv = ln_mod_linear(xs, e_all, 0, fq[0]) if qkv_w8 else self._qkv_gemm(fq, h)
+            else:
+                if pending is not None:
+                    xs = gate_add(xs, pending[0], pending[1], 5)
+                    pending = None
+                h = ln_mod(xs, e_all, 0)
+            if fused and fq is not None:
                 # exchange closures that publish per-token FP8 K/V expose their
                 # destination slots; the kernel that produces K publishes them
                 targets = [getattr(t.exch, "fp8_publish_targets", None) for t in tasks]
@@ -386,25 +414,35 @@ class WanDiT(nn.Module):
                     K, V = rk[None], v[i][None]
                 o[i] = dispatch_attention(rq[None], K, V)[0]
             y = _lin(b.self_attn.o, o.view(S * T, dim))
-            xs = gate_add(xs, y, e_all, 2)
             # cross-attention: all stages share the text K/V -> one call
-            qc = _lin(b.cross_attn.q, xs)
+            if fused and w8a8_channel(b.cross_attn.q):
+                xq, xsc = kernels.gate_residual_then(xs, y, e_all[:, 2], T, quant=True,
+                                                     qtype=b.cross_attn.q.qtype)
+                qc = b.cross_attn.q.gemm_q(xq, xsc)
+            else:
+                xs = gate_add(xs, y, e_all, 2)
+                qc = _lin(b.cross_attn.q, xs)
             qc = (kernels.rms_norm(qc, b.cross_attn.norm_q.weight, eps) if fused
                   else b.cross_attn.norm_q(qc)).view(1, S * T, H, D)
             kc, vc = self._cross_kv[li]
             oc = sdpa_elsewhere(qc, kc, vc)
-            xs = gate_add(xs, _lin(b.cross_attn.o, oc.view(S * T, dim)), None, 0)
+            yc = _lin(b.cross_attn.o, oc.view(S * T, dim))
             fi, fo = b.ffn.fc_in, b.ffn.fc_out
             if fused and w8a8_channel(fi) and getattr(fo, "granularity", None) == "channel" and hasattr(
                     fo, "forward_gelu_input"):
-                # W8A8, per-token: LN-modulate quantised in one kernel, plain
-                # fc_in GEMM, GELU(tanh) inside fc_out's input quantiser
-                y = fo.forward_gelu_input(ln_mod_linear(xs, e_all, 3, fi))
-                xs = gate_add(xs, y, e_all, 5)
+                # W8A8, per-token: residual + LN-modulate quantised in one
+                # kernel, plain fc_in GEMM, GELU(tanh) inside fc_out's input
+                # quantiser; the FFN residual goes to the next layer's kernel
+                xq, xsc = gate_then_mod(xs, yc, None, 0, e_all, 3, True, fi.qtype)
+                pending = (fo.forward_gelu_input(fi.gemm_q(xq, xsc)), e_all)
                 if layer_hook is not None:
                     layer_hook(li)
                 continue
-            h = ln_mod(xs, e_all, 3)
+            if fused:
+                h = gate_then_mod(xs, yc, None, 0, e_all, 3, False, 0)
+            else:
+                xs = gate_add(xs, yc, None, 0)
+                h = ln_mod(xs, e_all, 3)
             if fused and type(fi) is nn.Linear:
                 a = torch._addmm_activation(fi.bias, h, fi.weight.t(), use_gelu=True)  # cuBLASLt bias+GELU(tanh)
                 y = _lin(fo, a)
@@ -415,11 +453,17 @@ class WanDiT(nn.Module):
                 y = _lin(fo, fi.forward_gelu(h))  # W8A8 GEMM with GELU(tanh) in its epilogue
             else:
                 y = _lin(fo, F.gelu(_lin(fi, h), approximate="tanh"))
-            xs = gate_add(xs, y, e_all, 5)
+            if fused:
+                pending = (y, e_all)
+            else:
+                xs = gate_add(xs, y, e_all, 5)
             if layer_hook is not None:
                 layer_hook(li)
         eh = (self.head_norm_mod.float() + torch.stack(heads_e)).contiguous()  # [S, 2, dim]
-        h = ln_mod(xs, eh, 0)
+        if pending is not None:
+            h = kernels.gate_residual_then(xs, pending[0], pending[1][:, 5], T, eh[:, 0], eh[:, 1], T, eps)
+        else:
+            h = ln_mod(xs, eh, 0)
         out = _lin(self.head, h).view(S, T, -1)
         return [self.unpatchify(out[i].float(), cfg.frames_per_block) for i in range(S)]
 
