@@ -84,7 +84,8 @@ def parse():
                          "batched cross-attention of six stages)")
     ap.add_argument("--gemm-nk", default="", help="--kernel gemm: N,K (default the FFN fc_in)")
     ap.add_argument("--act-k", type=int, default=0, help="--kernel actq: row length K (default the FFN width)")
-    ap.add_argument("--act-gelu", action="store_true", help="--kernel actq: quantise GELU_tanh(x) (fc_out's input)")
+    ap.add_argument("--act-gelu", action="store_true",
+                    help="--kernel actq: quantise GELU_tanh(x) (fc_out's input); --kernel gemm: GELU epilogue")
     ap.add_argument("--library", action="store_true",
                     help="--kernel attn: also time torch SDPA, the reference's attention call, on the same buffers")
     ap.add_argument("--trace", action="store_true",
@@ -873,7 +874,9 @@ def run_kernel_bench(args):
             wq, ws = kernels.weight_quant(w)
             xq, xs = kernels.act_quant(x)
             out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-            fns.append(lambda xq=xq, xs=xs, wq=wq, ws=ws, out=out: kernels.gemm_w8a8(xq, xs, wq, ws, None, out=out))
+            gact = L.WF_ACT_GELU_TANH if args.act_gelu else L.WF_ACT_NONE
+            fns.append(lambda xq=xq, xs=xs, wq=wq, ws=ws, out=out: kernels.gemm_w8a8(xq, xs, wq, ws, None, out=out,
+                                                                                      activation=gact))
             if args.library:
                 ob = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
                 lib_fns.append(lambda x=x, w=w, ob=ob: torch.matmul(x, w.t(), out=ob))
@@ -884,7 +887,7 @@ def run_kernel_bench(args):
             else:
                 del x, w
         work, unit, bound = 2.0 * M * N * K / 1e12, "TFLOP/s", "tensor"
-        name = f"gemm_w8a8 e4m3 {M}x{N}x{K}"
+        name = f"gemm_w8a8 e4m3 {M}x{N}x{K}" + (" + GELU(tanh) epilogue" if args.act_gelu else "")
     elif args.kernel == "actq":
         # per-token activation quantiser: M = --q-len (default the N=1 tick's
         # six stages), K = --act-k; bytes = bf16 read + codes + scales
@@ -1133,6 +1136,21 @@ def run_vae_bench(args):
     ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
     p50 = statistics.median(ms)
     flops = 3 * sum(dec.unit_flops(lh, lw))
+    shares = None
+    if args.trace:
+        # kernel families of one more chunk (CUPTI, in-stream durations)
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            s.push(z[:, f:f + 3]) if f + 3 <= n else s.push(z[:, 1:4])
+            torch.cuda.synchronize()
+        by: dict = {}
+        for e in prof.events():
+            if e.device_type == torch.autograd.DeviceType.CUDA and e.time_range.end > e.time_range.start:
+                k = e.name.split("(")[0][:90]
+                by[k] = by.get(k, 0.0) + (e.time_range.end - e.time_range.start) / 1e3
+        tot = sum(by.values())
+        shares = [{"kernel": k, "ms": v, "share": v / tot} for k, v in sorted(by.items(), key=lambda kv: -kv[1])[:14]]
     peaks, src = _peaks()
     ach = flops / (p50 * 1e-3) / 1e12
     print(json.dumps({"kernel": "streaming VAE decode, one 3-latent-frame chunk (60x104 -> 12 frames of 480x832)",
@@ -1140,7 +1158,8 @@ def run_vae_bench(args):
                       "peak": peaks["bf16_tflops"], "frac": ach / peaks["bf16_tflops"],
                       "peak_source": src + " bf16_tflops", "flops_per_chunk": flops,
                       "output_frames": out_frames, "steps": args.steps,
-                      "note": "cuDNN convolutions and torch SDPA (library calls); FLOPs counted analytically"}),
+                      "note": "cuDNN convolutions and torch SDPA (library calls); FLOPs counted analytically",
+                      **({"trace_shares": shares} if shares else {})}),
           flush=True)
 
 

@@ -256,6 +256,14 @@ int wf_gate_residual_then(void* x, int64_t x_stride, const void* y, int64_t y_st
                           int64_t mod_stride, int64_t mod_rows_per_stage, float eps, void* out, int64_t out_stride,
                           void* xq, float* x_scale, int qtype, int64_t rows, int64_t dim, void* stream);
 
+/* Streaming VAE decode: the channel RMSNorm of channels-last bf16
+ * activations, rows [rows, C] contiguous (C a multiple of 8, at most 1024):
+ * out = x / max(||x||_2, eps) * sqrt(C) * gamma (bf16 [C]), then SiLU when
+ * silu != 0 (naive_rt/rolling_forcing/wan/modules/vae.py:39-54 with the
+ * SiLU of :178-192); f32 math, out may alias x. */
+int wf_channel_rmsnorm(const void* x, void* out, int64_t rows, int64_t C, const void* gamma, float eps, int silu,
+                       void* stream);
+
 /* From the fused QKV GEMM output qkv [rows, ld] (q at column 0, k at dim):
  * RMSNorm over dim (rounded to bf16, then times the bf16 weight, as
  * naive_rt/rolling_forcing/wan/modules/model.py:70-88) followed by interleaved

@@ -39,3 +39,23 @@ def test_gpu_chunked_equals_framewise():
     got = torch.cat([s.push(z[:, a:b]) for a, b in ((0, 3), (3, 6), (6, 7))], 1).float()
     assert tuple(got.shape) == (3, 25, 96, 160)
     assert _cos(got, want) >= 0.9999
+
+
+@pytest.mark.parametrize("C", [16, 96, 192, 384])
+@pytest.mark.parametrize("silu", [False, True])
+def test_channel_rmsnorm_matches_f32(C, silu):
+    """wf_channel_rmsnorm against normalize * sqrt(C) * gamma (+ SiLU) in f32 on
+    the bf16 inputs: within one bf16 rounding; a zero row stays zero."""
+    from waveforcing_b200 import kernels
+
+    g = torch.Generator(device="cuda").manual_seed(C)
+    x = (torch.randn(3, 5, 7, 9, C, device="cuda", generator=g) * 4).bfloat16()
+    x[0, 0, 0, 0] = 0
+    gamma = (1 + 0.2 * torch.randn(C, device="cuda", generator=g)).bfloat16()
+    got = kernels.channel_rmsnorm(x, gamma, silu).float()
+    xf = x.float()
+    ref = torch.nn.functional.normalize(xf, dim=-1) * C ** 0.5 * gamma.float()
+    if silu:
+        ref = torch.nn.functional.silu(ref)
+    assert torch.all((got - ref).abs() <= ref.abs() * 2.0**-7 + 1e-3)
+    assert torch.all(got[0, 0, 0, 0] == 0)

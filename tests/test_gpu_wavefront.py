@@ -95,8 +95,9 @@ def test_fused_context_assembly_is_bit_identical(fp8):
 @pytest.mark.parametrize("qtype", ["e4m3", "int8"])
 def test_w8a8_ffn_fusion_matches_unfused(qtype):
     """W8A8 linears (per-channel weights, per-token activations): the fused
-    FFN (plain fc_in GEMM, GELU(tanh) inside fc_out's input quantiser) against
-    the unfused block (torch GELU between two W8A8 linears)."""
+    block (residual + LN-modulate + quantiser in one kernel, GELU(tanh) in the
+    fc_in GEMM epilogue) against the unfused block (torch GELU between two
+    W8A8 linears)."""
     from waveforcing_b200.wavefront import dit
 
     orig = dit.WanDiT.forward_stages

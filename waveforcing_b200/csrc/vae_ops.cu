@@ -1,0 +1,112 @@
+// Row ops of the streaming VAE decoder (waveforcing_b200/pipelines/vae.py)
+// on channels-last activations: every position's C channels are one
+// contiguous bf16 row.
+//   wf_channel_rmsnorm  out = x / max(||x||_2, eps) * sqrt(C) * gamma, then
+//                       optionally SiLU -- the Wan VAE's RMS_norm over the
+//                       channel dimension (naive_rt/rolling_forcing/wan/
+//                       modules/vae.py:39-54) fused with the SiLU that
+//                       follows it in every residual block and the head
+//                       (:178-192, :466-470).
+// f32 arithmetic, one bf16 rounding at the end.  16 threads per row: thread
+// j handles the 16-byte chunks j, j + 16, ... of the row, and the row's
+// sum of squares is reduced among the 16 lanes by shuffles.
+#include <cuda_runtime.h>
+
+#include <type_traits>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace wfk {
+namespace vae {
+
+constexpr int TPR = 16;  // threads per row
+
+template <int CPT, bool SILU>
+__global__ void __launch_bounds__(256)
+    channel_rmsnorm_kernel(const __nv_bfloat16* x, __nv_bfloat16* out,  // may alias: a row is read before it is written
+                           const __nv_bfloat16* __restrict__ gamma, int64_t rows, int C, float scale, float eps) {
+  const int sub = threadIdx.x & (TPR - 1);
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / TPR;
+  const bool live = row < rows;
+  const int nch = C / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (live ? row : 0) * C);
+  uint4 v[CPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) {
+    const int c = sub + i * TPR;
+    v[i] = (live && c < nch) ? __ldcs(xr + c) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float a = __uint_as_float(w[k] << 16), b = __uint_as_float(w[k] & 0xFFFF0000u);
+      ss = fmaf(a, a, fmaf(b, b, ss));
+    }
+  }
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (!live) return;
+  const float inv = scale / fmaxf(sqrtf(ss), eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + row * C);
+  const uint4* g4 = reinterpret_cast<const uint4*>(gamma);
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) {
+    const int c = sub + i * TPR;
+    if (c >= nch) continue;
+    const uint4 g = __ldg(g4 + c);
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float a = __uint_as_float(w[k] << 16) * inv * __uint_as_float(gw[k] << 16);
+      float b = __uint_as_float(w[k] & 0xFFFF0000u) * inv * __uint_as_float(gw[k] & 0xFFFF0000u);
+      if constexpr (SILU) {
+        a = a / (1.f + __expf(-a));
+        b = b / (1.f + __expf(-b));
+      }
+      o[k] = pack_bf16x2(a, b);
+    }
+    orow[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+}  // namespace vae
+}  // namespace wfk
+
+using namespace wfk;
+using namespace wfk::vae;
+
+extern "C" int wf_channel_rmsnorm(const void* x, void* out, int64_t rows, int64_t C, const void* gamma, float eps,
+                                  int silu, void* stream) {
+  if (!x || !out || !gamma || rows < 0 || C < 8 || C % 8 || C > 8 * TPR * 8 || !aligned16(x) || !aligned16(out) ||
+      !aligned16(gamma))
+    return fail(WF_ERR_INVALID_ARG, "wf_channel_rmsnorm: need C a multiple of 8 up to 1024 and 16-byte aligned rows");
+  if (rows == 0) return WF_OK;
+  const int64_t threads = rows * TPR;
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int cpt = static_cast<int>((C / 8 + TPR - 1) / TPR);
+  const float scale = sqrtf(static_cast<float>(C));
+  auto xb = static_cast<const __nv_bfloat16*>(x);
+  auto ob = static_cast<__nv_bfloat16*>(out);
+  auto gb = static_cast<const __nv_bfloat16*>(gamma);
+  const int c = static_cast<int>(C);
+  auto go = [&](auto cp) {
+    constexpr int CP = decltype(cp)::value;
+    if (silu)
+      channel_rmsnorm_kernel<CP, true><<<blocks, 256, 0, s>>>(xb, ob, gb, rows, c, scale, eps);
+    else
+      channel_rmsnorm_kernel<CP, false><<<blocks, 256, 0, s>>>(xb, ob, gb, rows, c, scale, eps);
+  };
+  switch (cpt) {
+    case 1: go(std::integral_constant<int, 1>()); break;
+    case 2: go(std::integral_constant<int, 2>()); break;
+    case 3: go(std::integral_constant<int, 3>()); break;
+    case 4: go(std::integral_constant<int, 4>()); break;
+    default: go(std::integral_constant<int, 8>()); break;
+  }
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}

@@ -381,6 +381,25 @@ def gate_residual_then(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, gat
     return (xq, xs) if quant else out
 
 
+def channel_rmsnorm(x: torch.Tensor, gamma: torch.Tensor, silu: bool, eps: float = 1e-12,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """x / max(||x||, eps) * sqrt(C) * gamma over the LAST dimension of a
+    contiguous bf16 tensor (the channel rows of channels-last activations),
+    then SiLU when ``silu``; ``out`` may be x itself."""
+    _check(x.dtype == torch.bfloat16 and x.is_contiguous(), "channel_rmsnorm: x must be contiguous bf16")
+    C = x.shape[-1]
+    _check(gamma.dtype == torch.bfloat16 and gamma.numel() == C and gamma.is_contiguous(),
+           "channel_rmsnorm: gamma must be contiguous bf16 [C]")
+    _check(out is None or (out.shape == x.shape and out.dtype == x.dtype and out.is_contiguous()),
+           "channel_rmsnorm: out must match x")
+    _need_cuda(x)
+    if out is None:
+        out = torch.empty_like(x)
+    L.check(L.lib().wf_channel_rmsnorm(x.data_ptr(), out.data_ptr(), x.numel() // C, C, gamma.data_ptr(), eps,
+                                       1 if silu else 0, _stream()), "wf_channel_rmsnorm")
+    return out
+
+
 def qk_norm_rope(qkv: torch.Tensor, dim: int, wq: torch.Tensor, wk: torch.Tensor, cos: torch.Tensor,
                  sin: torch.Tensor, head_dim: int, rows_per_stage: int, eps: float, want_unroped: bool = True):
     """Fused RMSNorm(q), RMSNorm(k) + RoPE from the fused QKV GEMM output.
