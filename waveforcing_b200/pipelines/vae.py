@@ -27,10 +27,11 @@ This module restates that decoder for the wavefront's chunks:
     hands activations to the next rank (the reference's ``vae_stage``).
     ``partition_units`` balances the groups by FLOPs.
 
-Layout: NCDHW tensors in bf16 on the GPU, made channels-last (NDHWC) for
-cuDNN's implicit-GEMM convolutions.  The decoder is convolution-bound; its
-convolutions run on cuDNN and its attention on torch SDPA, both library
-calls.  It sits outside the DiT hot path and counts only for FPS with VAE.
+Layout: NCDHW tensors in bf16 on the GPU, stored channels-last (NDHWC) all
+the way through, for cuDNN's implicit-GEMM convolutions.  The convolutions
+run on cuDNN and the attention on torch SDPA (library calls); the channel
+RMSNorm + SiLU is a libwfk kernel.  The decoder sits outside the DiT hot path
+and counts only for FPS with VAE.
 """
 
 from __future__ import annotations
@@ -41,6 +42,8 @@ from dataclasses import dataclass
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+
+from waveforcing_b200 import kernels
 
 
 @dataclass(frozen=True)
@@ -77,24 +80,53 @@ class _CausalConv(nn.Module):
         if kt > 1:
             prev = state.get(key)
             if prev is None:
-                prev = x.new_zeros((x.shape[0], x.shape[1], kt - 1) + tuple(x.shape[3:]))
-            x = torch.cat([prev, x], 2)
+                prev = _like_layout(x, torch.zeros((x.shape[0], x.shape[1], kt - 1) + tuple(x.shape[3:]),
+                                                   dtype=x.dtype, device=x.device))
+            x = _like_layout(prev, torch.cat([prev, x], 2))
             state[key] = x[:, :, -(kt - 1):].clone()
         return F.conv3d(x, self.weight, self.bias, padding=(0, self.k[1] // 2, self.k[2] // 2))
 
 
+def _like_layout(ref: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+    """On the GPU every activation stays channels-last (NDHWC): a tensor in
+    another layout reaching a convolution is converted by a strided copy of
+    the whole activation, which cost three quarters of the decode time."""
+    if t.is_cuda and t.dim() == 5 and not t.is_contiguous(memory_format=torch.channels_last_3d):
+        return t.contiguous(memory_format=torch.channels_last_3d)
+    return t
+
+
 class _RMSNorm(nn.Module):
     """L2-normalise over channels, times sqrt(C) and a per-channel gain
-    (RMS_norm, vae.py:39-54)."""
+    (RMS_norm, vae.py:39-54), optionally followed by SiLU.  On the GPU
+    (channels-last bf16) one libwfk kernel does both (wf_channel_rmsnorm):
+    torch's normalize on channels-last activations runs as strided
+    elementwise passes, three quarters of the decoder's time."""
 
     def __init__(self, dim: int) -> None:
         super().__init__()
         self.gain = nn.Parameter(torch.ones(dim))
         self.scale = dim ** 0.5
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, silu: bool = False) -> torch.Tensor:
+        if x.is_cuda:
+            return _channel_rows(x, lambda r: kernels.channel_rmsnorm(r, self.gain, silu))
         g = self.gain.view((1, -1) + (1,) * (x.dim() - 2))
-        return F.normalize(x, dim=1) * self.scale * g
+        y = F.normalize(x, dim=1) * self.scale * g
+        return F.silu(y) if silu else y
+
+
+def _channel_rows(x: torch.Tensor, fn) -> torch.Tensor:
+    """Apply a row op over the channels of an NC... tensor stored channels-last
+    (the channel rows contiguous) and return the result in the same layout."""
+    nd = x.dim()
+    perm = (0,) + tuple(range(2, nd)) + (1,)
+    rows = x.permute(*perm)
+    if not rows.is_contiguous():
+        rows = rows.contiguous()
+    out = fn(rows)
+    inv = (0, nd - 1) + tuple(range(1, nd - 1))
+    return out.permute(*inv)
 
 
 class _ResBlock(nn.Module):
@@ -109,8 +141,8 @@ class _ResBlock(nn.Module):
 
     def forward(self, x, state, key):
         h = self.short(x, state, key + ".s") if self.short is not None else x
-        y = self.c1(F.silu(self.n1(x)), state, key + ".c1")
-        y = self.c2(F.silu(self.n2(y)), state, key + ".c2")
+        y = self.c1(self.n1(x, silu=True), state, key + ".c1")
+        y = self.c2(self.n2(y, silu=True), state, key + ".c2")
         return y + h
 
 
@@ -129,7 +161,10 @@ class _FrameAttention(nn.Module):
     def forward(self, x, state, key):
         b, c, t, h, w = x.shape
         f = x.permute(0, 2, 3, 4, 1).reshape(b * t, h * w, c)  # tokens of each frame
-        n = F.normalize(f, dim=-1) * self.norm.scale * self.norm.gain
+        if f.is_cuda:
+            n = kernels.channel_rmsnorm(f.contiguous(), self.norm.gain, False)
+        else:
+            n = F.normalize(f, dim=-1) * self.norm.scale * self.norm.gain
         q, k, v = F.linear(n, self.qkv, self.qkv_b).chunk(3, dim=-1)
         o = F.scaled_dot_product_attention(q[:, None], k[:, None], v[:, None])[:, 0]
         o = F.linear(o, self.proj, self.proj_b)
@@ -155,7 +190,13 @@ class _Upsample(nn.Module):
             if state.get(key + ".seen"):
                 b, c, t, h, w = x.shape
                 y = self.tconv(x, state, key + ".t")  # [b, 2c, t, h, w]
-                x = y.view(b, 2, c, t, h, w).permute(0, 2, 3, 1, 4, 5).reshape(b, c, 2 * t, h, w)
+                if y.is_cuda:
+                    # channels-last: frame i's two channel halves become frames 2i, 2i+1;
+                    # one copy into [b, t, 2, h, w, c] memory order, viewed back as NCDHW
+                    m = y.permute(0, 2, 3, 4, 1).reshape(b, t, h, w, 2, c).permute(0, 1, 4, 2, 3, 5).contiguous()
+                    x = m.view(b, 2 * t, h, w, c).permute(0, 4, 1, 2, 3)
+                else:
+                    x = y.view(b, 2, c, t, h, w).permute(0, 2, 3, 1, 4, 5).reshape(b, c, 2 * t, h, w)
             else:
                 state[key + ".seen"] = True
         b, c, t, h, w = x.shape
@@ -192,7 +233,7 @@ class _Head(nn.Module):
         self.conv = _CausalConv(dim, 3, 3)
 
     def forward(self, x, state, key):
-        return self.conv(F.silu(self.norm(x)), state, key + ".conv").clamp(-1, 1)
+        return self.conv(self.norm(x, silu=True), state, key + ".conv").clamp(-1, 1)
 
 
 # ----------------------------------------------------------------- decoder
