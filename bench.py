@@ -1141,9 +1141,16 @@ def run_vae_bench(args):
         # kernel families of one more chunk (CUPTI, in-stream durations)
         from torch.profiler import ProfilerActivity, profile
 
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
             s.push(z[:, f:f + 3]) if f + 3 <= n else s.push(z[:, 1:4])
             torch.cuda.synchronize()
+        ops = []
+        for a in prof.key_averages(group_by_input_shape=True):
+            dt = getattr(a, "device_time_total", None) or getattr(a, "cuda_time_total", 0)
+            if a.key.startswith("aten::") and dt > 0:
+                ops.append((dt / 1e3, a.key, str(a.input_shapes)[:120], a.count))
+        ops.sort(key=lambda r: -r[0])
+        op_shares = [{"op": k, "ms": ms, "shapes": sh, "calls": c} for ms, k, sh, c in ops[:16]]
         by: dict = {}
         for e in prof.events():
             if e.device_type == torch.autograd.DeviceType.CUDA and e.time_range.end > e.time_range.start:
@@ -1159,7 +1166,7 @@ def run_vae_bench(args):
                       "peak_source": src + " bf16_tflops", "flops_per_chunk": flops,
                       "output_frames": out_frames, "steps": args.steps,
                       "note": "cuDNN convolutions and torch SDPA (library calls); FLOPs counted analytically",
-                      **({"trace_shares": shares} if shares else {})}),
+                      **({"trace_shares": shares, "trace_ops": op_shares} if shares else {})}),
           flush=True)
 
 

@@ -264,6 +264,12 @@ int wf_gate_residual_then(void* x, int64_t x_stride, const void* y, int64_t y_st
 int wf_channel_rmsnorm(const void* x, void* out, int64_t rows, int64_t C, const void* gamma, float eps, int silu,
                        void* stream);
 
+/* Streaming VAE decode, temporal x2 on channels-last rows: src [frames, hw,
+ * 2C] (bf16) becomes dst [2 * frames, hw, C], frame 2i from channels [0, C)
+ * of src frame i and frame 2i + 1 from [C, 2C)
+ * (naive_rt/rolling_forcing/wan/modules/vae.py:127-131). */
+int wf_interleave_time2(const void* src, void* dst, int64_t frames, int64_t hw, int64_t C, void* stream);
+
 /* From the fused QKV GEMM output qkv [rows, ld] (q at column 0, k at dim):
  * RMSNorm over dim (rounded to bf16, then times the bf16 weight, as
  * naive_rt/rolling_forcing/wan/modules/model.py:70-88) followed by interleaved

@@ -59,3 +59,18 @@ def test_channel_rmsnorm_matches_f32(C, silu):
         ref = torch.nn.functional.silu(ref)
     assert torch.all((got - ref).abs() <= ref.abs() * 2.0**-7 + 1e-3)
     assert torch.all(got[0, 0, 0, 0] == 0)
+
+
+def test_interleave_time2_matches_reference_reshape():
+    """wf_interleave_time2 against the reference's view/stack of the temporal
+    conv output (vae.py:127-131): frame 2i from channels [0, C), 2i + 1 from
+    [C, 2C)."""
+    from waveforcing_b200 import kernels
+
+    b, c, t, h, w = 1, 24, 3, 5, 7
+    y = torch.randn(b, 2 * c, t, h, w, device="cuda").bfloat16().contiguous(memory_format=torch.channels_last_3d)
+    got = kernels.interleave_time2(y)
+    v = y.view(b, 2, c, t, h, w)
+    want = torch.stack((v[:, 0], v[:, 1]), 3).reshape(b, c, 2 * t, h, w)
+    assert got.is_contiguous(memory_format=torch.channels_last_3d)
+    assert torch.equal(got, want)

@@ -76,6 +76,7 @@ _SIGS = {
     "wf_ln_modulate_quant": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _vp]),
     "wf_gate_residual": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
     "wf_channel_rmsnorm": (_i32, [_vp, _vp, _i64, _i64, _vp, _f32, _i32, _vp]),
+    "wf_interleave_time2": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp]),
     "wf_gate_residual_then": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _f32, _vp, _i64,
                                      _vp, _vp, _i32, _i64, _i64, _vp]),
     "wf_qk_norm_rope": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),

@@ -72,6 +72,23 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Temporal x2 of the upsampling blocks on channels-last rows: src holds, per
+// (frame i, position p), 2C channels [half 0 | half 1]; dst holds frames 2i
+// (half 0) and 2i + 1 (half 1), each position's C channels contiguous.  One
+// thread per 16-byte chunk of the output.
+__global__ void __launch_bounds__(256) interleave_time2_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                               int64_t frames, int64_t hw, int64_t c16) {
+  const int64_t n = frames * 2 * hw * c16;
+  for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < n;
+       o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t k = o % c16;
+    const int64_t p = (o / c16) % hw;
+    const int64_t j = (o / (c16 * hw)) & 1;
+    const int64_t i = o / (c16 * hw * 2);
+    dst[o] = __ldcs(src + ((i * hw + p) * 2 + j) * c16 + k);
+  }
+}
+
 }  // namespace vae
 }  // namespace wfk
 
@@ -107,6 +124,21 @@ extern "C" int wf_channel_rmsnorm(const void* x, void* out, int64_t rows, int64_
     case 4: go(std::integral_constant<int, 4>()); break;
     default: go(std::integral_constant<int, 8>()); break;
   }
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_interleave_time2(const void* src, void* dst, int64_t frames, int64_t hw, int64_t C, void* stream) {
+  if (!src || !dst || frames < 0 || hw < 1 || C < 8 || C % 8 || !aligned16(src) || !aligned16(dst) || src == dst)
+    return fail(WF_ERR_INVALID_ARG, "wf_interleave_time2: need C a multiple of 8, 16-byte aligned distinct buffers");
+  if (frames == 0) return WF_OK;
+  const int64_t n = frames * 2 * hw * (C / 8);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n + 255) / 256, cap = static_cast<int64_t>(sms) * 16;
+  interleave_time2_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), frames, hw, C / 8);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

@@ -382,7 +382,7 @@ def gate_residual_then(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, gat
 
 
 def channel_rmsnorm(x: torch.Tensor, gamma: torch.Tensor, silu: bool, eps: float = 1e-12,
-                    out: torch.Tensor | None = None) -> torch.Tensor:
+                    out: torch.Tensor | None = None) -> torch.Tensor:  # out: any contiguous bf16 of x's shape
     """x / max(||x||, eps) * sqrt(C) * gamma over the LAST dimension of a
     contiguous bf16 tensor (the channel rows of channels-last activations),
     then SiLU when ``silu``; ``out`` may be x itself."""
@@ -397,6 +397,20 @@ def channel_rmsnorm(x: torch.Tensor, gamma: torch.Tensor, silu: bool, eps: float
         out = torch.empty_like(x)
     L.check(L.lib().wf_channel_rmsnorm(x.data_ptr(), out.data_ptr(), x.numel() // C, C, gamma.data_ptr(), eps,
                                        1 if silu else 0, _stream()), "wf_channel_rmsnorm")
+    return out
+
+
+def interleave_time2(y: torch.Tensor) -> torch.Tensor:
+    """[b, 2C, T, H, W] channels-last bf16 -> [b, C, 2T, H, W] channels-last:
+    frame 2i from channels [0, C) of frame i, frame 2i + 1 from [C, 2C)."""
+    _check(y.dim() == 5 and y.dtype == torch.bfloat16 and y.is_contiguous(memory_format=torch.channels_last_3d)
+           and y.shape[1] % 2 == 0, "interleave_time2: y must be channels-last bf16 [b, 2C, T, H, W]")
+    b, c2, t, h, w = y.shape
+    _need_cuda(y)
+    out = torch.empty((b, c2 // 2, 2 * t, h, w), device=y.device, dtype=y.dtype,
+                      memory_format=torch.channels_last_3d)
+    L.check(L.lib().wf_interleave_time2(y.data_ptr(), out.data_ptr(), b * t, h * w, c2 // 2, _stream()),
+            "wf_interleave_time2")
     return out
 
 

@@ -86,6 +86,13 @@ class _CausalConv(nn.Module):
             state[key] = x[:, :, -(kt - 1):].clone()
         return F.conv3d(x, self.weight, self.bias, padding=(0, self.k[1] // 2, self.k[2] // 2))
 
+    def run_buffer(self, buf: torch.Tensor, state: dict, key: str) -> torch.Tensor:
+        """The same convolution on an input that already carries the stream's
+        kt - 1 frames in front (``_RMSNorm.into_causal``): no concatenation."""
+        p = self.k[0] - 1
+        state[key] = buf[:, :, -p:].clone()
+        return F.conv3d(buf, self.weight, self.bias, padding=(0, self.k[1] // 2, self.k[2] // 2))
+
 
 def _like_layout(ref: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
     """On the GPU every activation stays channels-last (NDHWC): a tensor in
@@ -116,6 +123,26 @@ class _RMSNorm(nn.Module):
         return F.silu(y) if silu else y
 
 
+    def into_causal(self, x: torch.Tensor, silu: bool, conv: "_CausalConv", state: dict, key: str) -> torch.Tensor:
+        """GPU, batch 1: norm (+ SiLU) of x written straight into the input
+        buffer of the causal ``conv`` that follows, behind the kt - 1 frames the
+        stream carries for it (``conv.run_buffer``), so the convolution input is
+        never concatenated."""
+        p = conv.k[0] - 1
+        b, c, t, h, w = x.shape
+        buf = torch.empty((b, t + p, h, w, c), device=x.device, dtype=x.dtype)
+        prev = state.get(key)
+        if prev is None:
+            buf[:, :p].zero_()
+        else:
+            buf[:, :p].copy_(prev.permute(0, 2, 3, 4, 1))
+        rows = x.permute(0, 2, 3, 4, 1)
+        if not rows.is_contiguous():
+            rows = rows.contiguous()
+        kernels.channel_rmsnorm(rows, self.gain, silu, out=buf[:, p:])
+        return buf.permute(0, 4, 1, 2, 3)
+
+
 def _channel_rows(x: torch.Tensor, fn) -> torch.Tensor:
     """Apply a row op over the channels of an NC... tensor stored channels-last
     (the channel rows contiguous) and return the result in the same layout."""
@@ -141,8 +168,12 @@ class _ResBlock(nn.Module):
 
     def forward(self, x, state, key):
         h = self.short(x, state, key + ".s") if self.short is not None else x
-        y = self.c1(self.n1(x, silu=True), state, key + ".c1")
-        y = self.c2(self.n2(y, silu=True), state, key + ".c2")
+        if x.is_cuda and x.shape[0] == 1:
+            y = self.c1.run_buffer(self.n1.into_causal(x, True, self.c1, state, key + ".c1"), state, key + ".c1")
+            y = self.c2.run_buffer(self.n2.into_causal(y, True, self.c2, state, key + ".c2"), state, key + ".c2")
+        else:
+            y = self.c1(self.n1(x, silu=True), state, key + ".c1")
+            y = self.c2(self.n2(y, silu=True), state, key + ".c2")
         return y + h
 
 
@@ -191,10 +222,9 @@ class _Upsample(nn.Module):
                 b, c, t, h, w = x.shape
                 y = self.tconv(x, state, key + ".t")  # [b, 2c, t, h, w]
                 if y.is_cuda:
-                    # channels-last: frame i's two channel halves become frames 2i, 2i+1;
-                    # one copy into [b, t, 2, h, w, c] memory order, viewed back as NCDHW
-                    m = y.permute(0, 2, 3, 4, 1).reshape(b, t, h, w, 2, c).permute(0, 1, 4, 2, 3, 5).contiguous()
-                    x = m.view(b, 2 * t, h, w, c).permute(0, 4, 1, 2, 3)
+                    # channels-last: frame i's two channel halves become frames
+                    # 2i, 2i+1 in one vectorised pass (wf_interleave_time2)
+                    x = kernels.interleave_time2(_like_layout(y, y))
                 else:
                     x = y.view(b, 2, c, t, h, w).permute(0, 2, 3, 1, 4, 5).reshape(b, c, 2 * t, h, w)
             else:
@@ -233,7 +263,12 @@ class _Head(nn.Module):
         self.conv = _CausalConv(dim, 3, 3)
 
     def forward(self, x, state, key):
-        return self.conv(self.norm(x, silu=True), state, key + ".conv").clamp(-1, 1)
+        if x.is_cuda and x.shape[0] == 1:
+            y = self.conv.run_buffer(self.norm.into_causal(x, True, self.conv, state, key + ".conv"), state,
+                                     key + ".conv")
+        else:
+            y = self.conv(self.norm(x, silu=True), state, key + ".conv")
+        return y.clamp(-1, 1)
 
 
 # ----------------------------------------------------------------- decoder

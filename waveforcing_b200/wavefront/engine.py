@@ -4,9 +4,9 @@ Schedule and data flow follow wave_rt/denoiser/engine.py:
   * activity       -- _act_denoise/_act_store :214-219, roles :303-311
   * one tick       -- :287-597: denoise/store forwards with the paged exchange
                       closure installed, drain, clean-KV promotion (anchor
-                      broadcast at cid 0 :449-488, store slot otherwise
-                      :489-515), latent migration + deterministic re-noise
-                      :221-235, :516-555
+                      sent to the stage ranks at cid 0 :449-488, store slot
+                      otherwise :489-515), latent migration point to point +
+                      deterministic re-noise :221-235, :516-555
   * ticks          -- num_blocks + stages (engine.py:53 with world = stages)
 The reference needs one rank per stage (wave_rt/config.py:79-83).  Here
 ``place_stages`` maps the rf_step denoise stages and the store onto any
@@ -244,14 +244,26 @@ class WavefrontEngine:
         # store_kv[L] = (roped_key, unroped_key, value) as [1, T, H, D] (copies,
         # see _StoreKV); store_slot[L] = [2, T, H, D] copy of the live slot
         if cid == 0:
-            # anchor: the store's unroped key and value for every layer (engine.py:449-488)
+            # anchor: the store's unroped key and value for every layer
+            # (engine.py:449-488, a world broadcast there), sent point to point
+            # to the ranks that host stages; a rank without stages keeps no
+            # clean pages and is free for other work (the VAE pipeline)
+            if not self.local:
+                return
+            src = self.stage_rank[self.store]
             if hosts_store:
                 blob = torch.stack([torch.stack([store_kv[L][1][0] for L in range(Ln)]),
                                     torch.stack([store_kv[L][2][0] for L in range(Ln)])]).contiguous()
             else:
                 blob = torch.empty((2, Ln, self.T, self.H, self.D), device=self.device, dtype=torch.bfloat16)
-            if self.world > 1:
-                dist.broadcast(blob, src=self.stage_rank[self.store], group=self.group)
+            peers = sorted(set(self.stage_rank) - {src})
+            if self.world > 1 and peers:
+                if self.rank == src:
+                    ops = [dist.P2POp(dist.isend, blob, self._peer(r), group=self.group) for r in peers]
+                else:
+                    ops = [dist.P2POp(dist.irecv, blob, self._peer(src), group=self.group)]
+                for req in dist.batch_isend_irecv(ops):
+                    req.wait()
             self._append_clean([dict(ku=blob[0, L], v=blob[1, L], cid=cid) for L in range(Ln)])
         elif hosts_store:
             self._append_clean([dict(kr=store_kv[L][0][0], v=store_kv[L][2][0], cid=cid) for L in range(Ln)])
