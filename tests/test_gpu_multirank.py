@@ -54,7 +54,8 @@ def _worker(rank, world, port, fp8, q):
                             timeout=datetime.timedelta(seconds=60))
     try:
         final, status = _engine_run(rank, world, fp8)
-        q.put((rank, final, status))
+        # numpy, not tensors: a queued tensor's shared storage dies with its sender
+        q.put((rank, {c: x.numpy() for c, x in final.items()}, status))
     except Exception as e:  # report, then leave the group without further collectives
         q.put((rank, repr(e), -1))
     finally:
@@ -95,7 +96,7 @@ def test_two_gpu_wavefront_matches_single_gpu(fp8):
         assert st == 0, f"rank {r}: a bounded wait gave up"
     store_final = {}
     for final, _ in multi.values():
-        store_final.update(final)
+        store_final.update({c: torch.from_numpy(x) for c, x in final.items()})
     assert sorted(store_final) == sorted(single)
     a = torch.cat([single[c] for c in sorted(single)], 1).double().flatten()
     b = torch.cat([store_final[c] for c in sorted(single)], 1).double().flatten()

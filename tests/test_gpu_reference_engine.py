@@ -91,7 +91,8 @@ def _run(engine, rank, dev, name):
     if arm == "wf":
         den._pg.check_timeouts()
     den.close()
-    return {c: x.float().cpu() for c, x in final.items()}, status
+    # numpy, not tensors: a queued tensor's shared storage dies with its sender
+    return {c: x.float().cpu().numpy() for c, x in final.items()}, status
 
 
 def _worker(rank, world, port, q):
@@ -127,8 +128,8 @@ def _port():
 def _cos(a, b):
     keys = sorted(a)
     assert keys == sorted(b) and keys
-    x = torch.cat([a[c] for c in keys], 1).double().flatten()
-    y = torch.cat([b[c] for c in keys], 1).double().flatten()
+    x = torch.cat([torch.as_tensor(a[c]) for c in keys], 1).double().flatten()
+    y = torch.cat([torch.as_tensor(b[c]) for c in keys], 1).double().flatten()
     return torch.nn.functional.cosine_similarity(x, y, dim=0).item()
 
 

@@ -115,7 +115,8 @@ def _worker(rank, world, port, q, delay_release):
             eng.inputs.clear()
             eng._migrate(t, out)
             for s, x in eng.inputs.items():
-                got[(t, s)] = x.clone()
+                # numpy, not tensors: a queued tensor's shared storage dies with its sender
+                got[(t, s)] = x.float().numpy().copy()
         q.put((rank, eng.local, got, waited, int(eng.xport.timeout_word.item()),
                eng.xport.remote_consumers(), eng.stage_rank))
         eng.close()
@@ -172,8 +173,8 @@ def test_p2p_migration_delivers_every_hand_off(world):
             s = d - 1
             x0 = _result(s, t, shape)
             want = ref_eng._renoise(x0, s, t - s) if s < S - 1 else x0
-            got = res[dst][1][(t, d)]
-            assert torch.equal(got, want), (t, d)
+            got = torch.from_numpy(res[dst][1][(t, d)])
+            assert torch.equal(got, want.float()), (t, d)
             n_checked += 1
         # nothing else arrived anywhere
         arrived = sum(1 for r in res for (tt, _d) in res[r][1] if tt == t)

@@ -126,7 +126,8 @@ def _worker(rank, world, port, q):
             q.put((rank, cuts, None))
         else:
             outs = st.serve()
-            q.put((rank, cuts, torch.cat(outs, 1) if outs else None))
+            # numpy, not a tensor: a queued tensor's shared storage dies with its sender
+            q.put((rank, cuts, torch.cat(outs, 1).numpy() if outs else None))
     except Exception as e:  # report instead of hanging the others
         q.put((rank, repr(e), None))
     finally:
@@ -162,6 +163,6 @@ def test_pipeline_over_three_ranks_equals_one_process():
     z = torch.randn(CFG.z_dim, 7, 3, 5, generator=torch.Generator().manual_seed(9))
     s = V.DecodeStream(dec)
     want = torch.cat([s.push(z[:, a:b]) for a, b in ((0, 3), (3, 6), (6, 7))], 1)
-    got = res[2][1]
+    got = torch.from_numpy(res[2][1]) if res[2][1] is not None else None
     assert got is not None and tuple(got.shape) == tuple(want.shape) == (3, 25, 24, 40)
     assert torch.equal(got, want)
