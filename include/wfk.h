@@ -270,6 +270,18 @@ int wf_channel_rmsnorm(const void* x, void* out, int64_t rows, int64_t C, const 
  * (naive_rt/rolling_forcing/wan/modules/vae.py:127-131). */
 int wf_interleave_time2(const void* src, void* dst, int64_t frames, int64_t hw, int64_t C, void* stream);
 
+/* Streaming VAE decode, on channels-last bf16 rows [rows, C] (C a multiple
+ * of 8): out = x + bias[c], then + res when res is not NULL, each sum rounded
+ * to bf16 (the convolution bias that cuDNN leaves to a separate pass, and the
+ * residual blocks' skip add, vae.py:194-214); out may alias x. */
+int wf_channel_bias_add(const void* x, const void* bias, const void* res, void* out, int64_t rows, int64_t C,
+                        void* stream);
+
+/* Streaming VAE decode: nearest x2 in H and W of channels-last bf16 images
+ * src [images, h, w, C] into dst [images, 2h, 2w, C] (vae.py:62-66, 77-80). */
+int wf_upsample2x_nearest(const void* src, void* dst, int64_t images, int64_t h, int64_t w, int64_t C,
+                          void* stream);
+
 /* From the fused QKV GEMM output qkv [rows, ld] (q at column 0, k at dim):
  * RMSNorm over dim (rounded to bf16, then times the bf16 weight, as
  * naive_rt/rolling_forcing/wan/modules/model.py:70-88) followed by interleaved

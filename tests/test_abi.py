@@ -106,6 +106,8 @@ def test_constants_match_the_header():
     ("wf_rms_norm", (None, 16, None, None, 16, 4, 16, 1e-6, None), 1),
     ("wf_channel_rmsnorm", (16, 16, 4, 12, 16, 1e-12, 1, None), 1),         # C not a multiple of 8
     ("wf_interleave_time2", (16, 16, 2, 4, 16, None), 1),                    # in place
+    ("wf_channel_bias_add", (16, 16, None, 16, 4, 12, None), 1),            # C not a multiple of 8
+    ("wf_upsample2x_nearest", (16, 16, 1, 4, 4, 16, None), 1),              # in place
     ("wf_ipc_close", (None,), 1),
     ("wf_stream_write_u32", (None, 18, 1), 1),                                # misaligned flag address
     ("wf_wait_flag", (16, 1, 0, None, None), 1),                              # zero timeout

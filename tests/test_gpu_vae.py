@@ -74,3 +74,31 @@ def test_interleave_time2_matches_reference_reshape():
     want = torch.stack((v[:, 0], v[:, 1]), 3).reshape(b, c, 2 * t, h, w)
     assert got.is_contiguous(memory_format=torch.channels_last_3d)
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("with_res", [False, True])
+def test_channel_bias_add_matches_torch(with_res):
+    """wf_channel_bias_add against torch's bias add and skip add in bf16
+    (each sum rounded), bit for bit, in place."""
+    from waveforcing_b200 import kernels
+
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(1, 96, 3, 10, 12, device="cuda", generator=g).bfloat16()
+    x = x.contiguous(memory_format=torch.channels_last_3d)
+    b = torch.randn(96, device="cuda", generator=g).bfloat16()
+    r = torch.randn(1, 96, 3, 10, 12, device="cuda", generator=g).bfloat16().contiguous(
+        memory_format=torch.channels_last_3d)
+    want = x + b.view(1, -1, 1, 1, 1)
+    if with_res:
+        want = want + r
+    got = kernels.channel_bias_add(x.clone(memory_format=torch.channels_last_3d), b, r if with_res else None)
+    assert torch.equal(got, want)
+
+
+def test_upsample2x_nearest_matches_interpolate():
+    from waveforcing_b200 import kernels
+
+    f = torch.randn(5, 48, 7, 9, device="cuda").bfloat16().contiguous(memory_format=torch.channels_last)
+    got = kernels.upsample2x_nearest(f)
+    want = torch.nn.functional.interpolate(f, scale_factor=2.0, mode="nearest")
+    assert torch.equal(got, want)

@@ -77,6 +77,8 @@ _SIGS = {
     "wf_gate_residual": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
     "wf_channel_rmsnorm": (_i32, [_vp, _vp, _i64, _i64, _vp, _f32, _i32, _vp]),
     "wf_interleave_time2": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    "wf_channel_bias_add": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "wf_upsample2x_nearest": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "wf_gate_residual_then": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _f32, _vp, _i64,
                                      _vp, _vp, _i32, _i64, _i64, _vp]),
     "wf_qk_norm_rope": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),

@@ -89,6 +89,62 @@ __global__ void __launch_bounds__(256) interleave_time2_kernel(const uint4* __re
   }
 }
 
+// out = x + bias[c] (+ res): the convolutions' bias (cuDNN returns 3-D
+// convolutions without it) and the residual blocks' skip add in one
+// vectorised pass over channels-last rows.  out may alias x.
+__global__ void __launch_bounds__(256) bias_add_kernel(const uint4* x, const uint4* __restrict__ res,
+                                                       const uint4* __restrict__ bias, uint4* out, int64_t n16,
+                                                       int64_t c16) {
+  for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < n16;
+       o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 a = x[o], b = __ldg(bias + o % c16);
+    const uint4 r = res ? __ldcs(res + o) : make_uint4(0, 0, 0, 0);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w}, rw[4] = {r.x, r.y, r.z, r.w};
+    uint32_t ow[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      // (x + bias) + res, each sum rounded as torch's separate bias and skip adds would
+      float lo = __uint_as_float(aw[k] << 16) + __uint_as_float(bw[k] << 16);
+      float hi = __uint_as_float(aw[k] & 0xFFFF0000u) + __uint_as_float(bw[k] & 0xFFFF0000u);
+      if (res) {
+        lo = __bfloat162float(__float2bfloat16_rn(lo)) + __uint_as_float(rw[k] << 16);
+        hi = __bfloat162float(__float2bfloat16_rn(hi)) + __uint_as_float(rw[k] & 0xFFFF0000u);
+      }
+      ow[k] = pack_bf16x2(lo, hi);
+    }
+    out[o] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+}
+
+// Nearest x2 in H and W on channels-last rows: dst[n, y, x] = src[n, y / 2,
+// x / 2] for every channel; each thread copies one 16-byte chunk of a source
+// pixel to its four destination pixels.
+__global__ void __launch_bounds__(256) upsample2x_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                         int64_t nimg, int64_t h, int64_t w, int64_t c16) {
+  const int64_t n = nimg * h * w * c16;
+  for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < n;
+       o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t k = o % c16;
+    const int64_t px = (o / c16) % w;
+    const int64_t py = (o / (c16 * w)) % h;
+    const int64_t im = o / (c16 * w * h);
+    const uint4 v = __ldcs(src + o);
+    const int64_t row0 = (im * 2 * h + 2 * py) * 2 * w + 2 * px;  // destination pixel (2py, 2px)
+    dst[row0 * c16 + k] = v;
+    dst[(row0 + 1) * c16 + k] = v;
+    dst[(row0 + 2 * w) * c16 + k] = v;
+    dst[(row0 + 2 * w + 1) * c16 + k] = v;
+  }
+}
+
+static unsigned grid_for(int64_t n) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n + 255) / 256, cap = static_cast<int64_t>(sms) * 16;
+  return static_cast<unsigned>(want < cap ? want : cap);
+}
+
 }  // namespace vae
 }  // namespace wfk
 
@@ -139,6 +195,33 @@ extern "C" int wf_interleave_time2(const void* src, void* dst, int64_t frames, i
   const int64_t want = (n + 255) / 256, cap = static_cast<int64_t>(sms) * 16;
   interleave_time2_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), static_cast<uint4*>(dst), frames, hw, C / 8);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_channel_bias_add(const void* x, const void* bias, const void* res, void* out, int64_t rows,
+                                   int64_t C, void* stream) {
+  if (!x || !bias || !out || rows < 0 || C < 8 || C % 8 || !aligned16(x) || !aligned16(bias) || !aligned16(out) ||
+      (res && !aligned16(res)))
+    return fail(WF_ERR_INVALID_ARG, "wf_channel_bias_add: need C a multiple of 8 and 16-byte aligned rows");
+  if (rows == 0) return WF_OK;
+  const int64_t n16 = rows * (C / 8);
+  bias_add_kernel<<<grid_for(n16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(x), static_cast<const uint4*>(res), static_cast<const uint4*>(bias),
+      static_cast<uint4*>(out), n16, C / 8);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_upsample2x_nearest(const void* src, void* dst, int64_t images, int64_t h, int64_t w, int64_t C,
+                                     void* stream) {
+  if (!src || !dst || images < 0 || h < 1 || w < 1 || C < 8 || C % 8 || !aligned16(src) || !aligned16(dst) ||
+      src == dst)
+    return fail(WF_ERR_INVALID_ARG, "wf_upsample2x_nearest: need C a multiple of 8, 16-byte aligned distinct buffers");
+  if (images == 0) return WF_OK;
+  const int64_t n = images * h * w * (C / 8);
+  upsample2x_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), images, h, w, C / 8);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

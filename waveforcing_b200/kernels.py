@@ -400,6 +400,38 @@ def channel_rmsnorm(x: torch.Tensor, gamma: torch.Tensor, silu: bool, eps: float
     return out
 
 
+def channel_bias_add(x: torch.Tensor, bias: torch.Tensor, res: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """x + bias (over the channel dim 1) [+ res] for channels-last bf16 x of 4 or
+    5 dims; out may be x.  Returns a tensor in x's layout."""
+    cl = torch.channels_last_3d if x.dim() == 5 else torch.channels_last
+    _check(x.dtype == torch.bfloat16 and x.dim() in (4, 5) and x.is_contiguous(memory_format=cl),
+           "channel_bias_add: x must be channels-last bf16 of 4 or 5 dims")
+    C = x.shape[1]
+    _check(bias.dtype == torch.bfloat16 and bias.numel() == C and bias.is_contiguous(),
+           "channel_bias_add: bias must be contiguous bf16 [C]")
+    _check(res is None or (res.shape == x.shape and res.dtype == x.dtype and res.is_contiguous(memory_format=cl)),
+           "channel_bias_add: res must match x (channels-last)")
+    _need_cuda(x)
+    if out is None:
+        out = torch.empty_like(x, memory_format=cl)
+    L.check(L.lib().wf_channel_bias_add(x.data_ptr(), bias.data_ptr(), res.data_ptr() if res is not None else None,
+                                        out.data_ptr(), x.numel() // C, C, _stream()), "wf_channel_bias_add")
+    return out
+
+
+def upsample2x_nearest(f: torch.Tensor) -> torch.Tensor:
+    """Nearest x2 in H and W of channels-last bf16 images [N, C, H, W]."""
+    _check(f.dtype == torch.bfloat16 and f.dim() == 4 and f.is_contiguous(memory_format=torch.channels_last),
+           "upsample2x_nearest: f must be channels-last bf16 [N, C, H, W]")
+    n, c, h, w = f.shape
+    _need_cuda(f)
+    out = torch.empty((n, c, 2 * h, 2 * w), device=f.device, dtype=f.dtype, memory_format=torch.channels_last)
+    L.check(L.lib().wf_upsample2x_nearest(f.data_ptr(), out.data_ptr(), n, h, w, c, _stream()),
+            "wf_upsample2x_nearest")
+    return out
+
+
 def interleave_time2(y: torch.Tensor) -> torch.Tensor:
     """[b, 2C, T, H, W] channels-last bf16 -> [b, C, 2T, H, W] channels-last:
     frame 2i from channels [0, C) of frame i, frame 2i + 1 from [C, 2C)."""

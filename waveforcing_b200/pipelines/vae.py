@@ -84,14 +84,25 @@ class _CausalConv(nn.Module):
                                                    dtype=x.dtype, device=x.device))
             x = _like_layout(prev, torch.cat([prev, x], 2))
             state[key] = x[:, :, -(kt - 1):].clone()
-        return F.conv3d(x, self.weight, self.bias, padding=(0, self.k[1] // 2, self.k[2] // 2))
+        return self._conv(x)
 
-    def run_buffer(self, buf: torch.Tensor, state: dict, key: str) -> torch.Tensor:
+    def run_buffer(self, buf: torch.Tensor, state: dict, key: str, res: torch.Tensor | None = None) -> torch.Tensor:
         """The same convolution on an input that already carries the stream's
-        kt - 1 frames in front (``_RMSNorm.into_causal``): no concatenation."""
+        kt - 1 frames in front (``_RMSNorm.into_causal``): no concatenation.
+        ``res`` is added to the result (the residual block's skip)."""
         p = self.k[0] - 1
         state[key] = buf[:, :, -p:].clone()
-        return F.conv3d(buf, self.weight, self.bias, padding=(0, self.k[1] // 2, self.k[2] // 2))
+        return self._conv(buf, res)
+
+    def _conv(self, x: torch.Tensor, res: torch.Tensor | None = None) -> torch.Tensor:
+        pad = (0, self.k[1] // 2, self.k[2] // 2)
+        if x.is_cuda and self.weight.shape[0] % 8 == 0:
+            # cuDNN leaves a 3-D convolution's bias to a strided broadcast add;
+            # one libwfk pass adds it, and the skip, on channels-last rows
+            y = _like_layout(x, F.conv3d(x, self.weight, None, padding=pad))
+            return kernels.channel_bias_add(y, self.bias, _like_layout(y, res) if res is not None else None, out=y)
+        y = F.conv3d(x, self.weight, self.bias, padding=pad)
+        return y + res if res is not None else y
 
 
 def _like_layout(ref: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
@@ -170,7 +181,8 @@ class _ResBlock(nn.Module):
         h = self.short(x, state, key + ".s") if self.short is not None else x
         if x.is_cuda and x.shape[0] == 1:
             y = self.c1.run_buffer(self.n1.into_causal(x, True, self.c1, state, key + ".c1"), state, key + ".c1")
-            y = self.c2.run_buffer(self.n2.into_causal(y, True, self.c2, state, key + ".c2"), state, key + ".c2")
+            return self.c2.run_buffer(self.n2.into_causal(y, True, self.c2, state, key + ".c2"), state, key + ".c2",
+                                      res=h)
         else:
             y = self.c1(self.n1(x, silu=True), state, key + ".c1")
             y = self.c2(self.n2(y, silu=True), state, key + ".c2")
@@ -231,8 +243,13 @@ class _Upsample(nn.Module):
                 state[key + ".seen"] = True
         b, c, t, h, w = x.shape
         f = x.transpose(1, 2).reshape(b * t, c, h, w)
-        f = F.interpolate(f, scale_factor=2.0, mode="nearest")
-        f = F.conv2d(f, self.conv_w, self.conv_b, padding=1)
+        if f.is_cuda and c % 8 == 0 and (c // 2) % 8 == 0:
+            f = kernels.upsample2x_nearest(f.contiguous(memory_format=torch.channels_last))
+            f = F.conv2d(f, self.conv_w, None, padding=1).contiguous(memory_format=torch.channels_last)
+            f = kernels.channel_bias_add(f, self.conv_b, out=f)
+        else:
+            f = F.interpolate(f, scale_factor=2.0, mode="nearest")
+            f = F.conv2d(f, self.conv_w, self.conv_b, padding=1)
         return f.reshape(b, t, c // 2, 2 * h, 2 * w).transpose(1, 2)
 
 
