@@ -376,10 +376,6 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
       // ----------------------------------------------------------------- MMA
       constexpr uint32_t OPF = KV8 ? FMT_F16 : FMT_BF16;  // operand type (A and B alike)
       constexpr uint32_t idesc_qk = make_idesc(1, OPF, OPF, 0, BM, BN);
-      // A last tile with at most 128 valid keys runs QK^T at N = 128 (S columns
-      // 128-255 keep stale values, which the softmax masks like every key past
-      // Lk), and PV skips the 16-key steps past the last valid key: their P is 0.
-      constexpr uint32_t idesc_qk_half = make_idesc(1, OPF, OPF, 0, BM, KH);
       constexpr uint32_t idesc_pv = make_idesc(1, OPF, OPF, 1, BM, HD);
       const uint32_t aQ = smem_u32(sQ);
       int kt = 0, st = 0, n_it = 0;  // K tiles, S tiles (= PV tiles) issued, items
@@ -400,13 +396,12 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
             }
             tc_fence_after();
             const uint32_t aK = smem_u32(sK + s * KTILE);
-            const uint32_t idq = (Lk - j * BN <= KH) ? idesc_qk_half : idesc_qk;
 #pragma unroll
             for (int kk = 0; kk < HD / 16; ++kk) {
               const uint32_t qoff = (kk >> 2) * QHALF + (kk & 3) * 32;
               const uint32_t koff = (kk >> 2) * KHALF + (kk & 3) * 32;
-              umma_f16_ss(tbase + COL_S, desc_sw128(aQ + qoff, 16, 1024), desc_sw128(aK + koff, 16, 1024), idq,
-                          kk > 0);
+              umma_f16_ss(tbase + COL_S, desc_sw128(aQ + qoff, 16, 1024), desc_sw128(aK + koff, 16, 1024),
+                          idesc_qk, kk > 0);
             }
             umma_commit(&empty_k[s]);
             umma_commit(bar_s);
@@ -424,8 +419,6 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
               ok = false;
               break;
             }
-            // 16-key steps of tile j-1 that hold valid keys (8 per half but in a last tile)
-            const int valid = Lk - (j - 1) * BN;
             for (int half = 0; half < 2; ++half) {
               if (!mbar_wait(&full_v[half], g & 1, abort_flag, ST_ATTN_MMA)) {
                 ok = false;
@@ -434,13 +427,10 @@ __device__ __forceinline__ void attn_body(const CUtensorMap& tmQ, const CUtensor
               tc_fence_after();
               const uint32_t aV = smem_u32(sV + half * VSLOT);
               const uint32_t tP = tbase + COL_P + half * (KH / 2);
-              const int vh = valid - half * KH;
-              const int steps = vh >= KH ? KH / 16 : (vh > 0 ? (vh + 15) / 16 : 0);
 #pragma unroll
               for (int kk = 0; kk < KH / 16; ++kk) {
-                if (kk < steps)
-                  umma_f16_ts(tbase + COL_O, tP + kk * 8, desc_sw128(aV + kk * 2048, VHALF, 1024), idesc_pv,
-                              (j > 1 || half > 0 || kk > 0) ? 1u : 0u);
+                umma_f16_ts(tbase + COL_O, tP + kk * 8, desc_sw128(aV + kk * 2048, VHALF, 1024), idesc_pv,
+                            (j > 1 || half > 0 || kk > 0) ? 1u : 0u);
               }
               umma_commit(&empty_v[half]);
             }
