@@ -385,10 +385,11 @@ import sys, numpy as np, torch
 from waveforcing_b200 import kernels as K
 from waveforcing_b200._lib import WF_DTYPE_E4M3, WF_DTYPE_S8
 qt = WF_DTYPE_E4M3 if sys.argv[1] == "e4m3" else WF_DTYPE_S8
+M, N, K_ = (int(v) for v in sys.argv[3].split(","))
 g = torch.Generator(device="cuda").manual_seed(7)
-x = torch.randn(3000, 1536, device="cuda", generator=g).bfloat16()
-w = (torch.randn(4608, 1536, device="cuda", generator=g) * 0.02).bfloat16()
-b = (torch.randn(4608, device="cuda", generator=g) * 0.1).bfloat16()
+x = torch.randn(M, K_, device="cuda", generator=g).bfloat16()
+w = (torch.randn(N, K_, device="cuda", generator=g) * 0.02).bfloat16()
+b = (torch.randn(N, device="cuda", generator=g) * 0.1).bfloat16()
 wq, ws = K.weight_quant(w, qt)
 xq, xs = K.act_quant(x, qt)
 y = K.gemm_w8a8(xq, xs, wq, ws, b, qt)
@@ -397,7 +398,8 @@ np.save(sys.argv[2], y.float().cpu().numpy())
 
 
 @pytest.mark.parametrize("qtype", ["e4m3", "s8"])
-def test_gemm_pair_matches_single_cta(qtype, tmp_path):
+@pytest.mark.parametrize("shape", ["3000,4608,1536", "8192,512,8960"])  # m-fastest, n-fastest tile order
+def test_gemm_pair_matches_single_cta(qtype, shape, tmp_path):
     """The CTA-pair kernel (WFK_GEMM_PAIR=1) against the one-CTA kernel
     (WFK_GEMM_PAIR=0) on the same inputs, each in its own process: both accumulate every
     output in f32 (s32) over the same k order; outputs agree to one bf16 ulp."""
@@ -408,7 +410,7 @@ def test_gemm_pair_matches_single_cta(qtype, tmp_path):
     for env_pair in ("1", "0"):  # forced on (the shape's K would pick one CTA per tile), then off
         f = tmp_path / f"y{env_pair}.npy"
         env = dict(os.environ, WFK_GEMM_PAIR=env_pair)
-        r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, qtype, str(f)], env=env, capture_output=True,
+        r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, qtype, str(f), shape], env=env, capture_output=True,
                            text=True, timeout=300, cwd=ROOT)
         assert r.returncode == 0, r.stderr[-2000:]
         outs.append(np.load(f))

@@ -334,7 +334,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const float* __restrict__ x_scale, const float* __restrict__ w_scale,
                           const __nv_bfloat16* __restrict__ bias, const __grid_constant__ CUtensorMap tmY, int M,
-                          int N, int K, int per_token, int act) {
+                          int N, int K, int per_token, int act, int n_fast) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sA = smem;
@@ -400,8 +400,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tma_prefetch_desc(&tmB);
       int it = 0;
       for (int t = pair; t < n_total && !*abort_flag; t += npairs) {
-        const int m0 = (t % m_tiles) * 2 * BM + static_cast<int>(rank) * BM;
-        const int n0 = (t / m_tiles) * BN + static_cast<int>(rank) * 128;
+        const int mt = n_fast ? t / n_tiles : t % m_tiles, nt = n_fast ? t % n_tiles : t / m_tiles;
+        const int m0 = mt * 2 * BM + static_cast<int>(rank) * BM;
+        const int n0 = nt * BN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % PNS;
           if (it >= PNS && !mbar_wait(&empty[s], ((it / PNS) - 1) & 1, abort_flag, ST_GEMM_PRODUCER)) {
@@ -468,7 +469,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int buf = local & 1;
       const bool okw =
           __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (local >> 1) & 1, abort_flag, ST_GEMM_EPILOGUE));
-      const int m0 = (t % m_tiles) * 2 * BM + static_cast<int>(rank) * BM, n0 = (t / m_tiles) * BN;
+      const int mt = n_fast ? t / n_tiles : t % m_tiles, nt = n_fast ? t % n_tiles : t / m_tiles;
+      const int m0 = mt * 2 * BM + static_cast<int>(rank) * BM, n0 = nt * BN;
       for (int j = et; j < BN; j += 128) {
         const int n = n0 + j < N ? n0 + j : N - 1;
         sSW[j] = per_token ? __ldg(w_scale + n) : sw_t;
@@ -788,12 +790,20 @@ extern "C" int wf_gemm_w8a8_act(const void* xq, const float* x_scale, const void
     const int pair_tiles = ((N + BN - 1) / BN) * ((M + 2 * BM - 1) / (2 * BM));
     const int pairs = pair_tiles < max_pairs ? pair_tiles : max_pairs;
     const dim3 pgrid(2 * pairs);
+    // Tile order: m fastest keeps the pairs running together on one weight
+    // tile; when the activations exceed half the 126 MB L2 (fc_out at
+    // M = 28080: 251 MB), that order re-reads them from DRAM once per column of
+    // tiles (1.53 GB at fc_out), so walk n fastest there: each activation tile
+    // is then read once and the weights (13.8 MB) stay in L2
+    const int n_fast = static_cast<int64_t>(M) * K > (int64_t{64} << 20) ? 1 : 0;
     if (qtype == WF_DTYPE_S8)
       gemm_w8a8_pair_kernel<true><<<pgrid, THREADS, PSMEM_BYTES, s>>>(
-          ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token, activation);
+          ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token, activation,
+          n_fast);
     else
       gemm_w8a8_pair_kernel<false><<<pgrid, THREADS, PSMEM_BYTES, s>>>(
-          ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token, activation);
+          ta, tb, x_scale, w_scale, static_cast<const __nv_bfloat16*>(bias), ty, M, N, K, per_token, activation,
+          n_fast);
     WFK_CUDA_TRY(cudaGetLastError());
     return WF_OK;
   }

@@ -171,6 +171,9 @@ class StageTask:
     start_frame: int
     stage: int
     exch: object = None  # closure with the wave_rt exchange contract
+    # only the task's per-layer K/V (published through ``exch``) are used, not
+    # its flow output (the store stage: the engine keeps its input latent)
+    kv_only: bool = False
 
 
 class WanDiT(nn.Module):
@@ -282,7 +285,8 @@ class WanDiT(nn.Module):
     def forward_stages(self, tasks: list[StageTask], layer_hook=None, fused: bool = True, rope_fn=None,
                        separate_qkv: bool = False) -> list[torch.Tensor]:
         """Run every task's 30/40-layer forward, layer-interleaved.  Returns the
-        flow prediction of each task as [C, F, H, W] (f32).  ``fused`` selects
+        flow prediction of each task as [C, F, H, W] (f32), None for a
+        ``kv_only`` task, whose last layer stops after its K/V are published.  ``fused`` selects
         the libwfk row kernels for norms/modulation/residuals/RoPE; False runs
         the same math as plain torch ops (used by the tests as a cross-check).
         With ``fused=False``, ``rope_fn(x [T, H, D], cos, sin) -> bf16`` replaces
@@ -296,6 +300,7 @@ class WanDiT(nn.Module):
         T = cfg.tokens_per_chunk
         H, D, dim = cfg.heads, cfg.head_dim, cfg.dim
         order = sorted(range(S), key=lambda i: -tasks[i].stage)  # publish before consume
+        keep = [i for i in range(S) if not tasks[i].kv_only]  # tasks whose flow output is returned
         x = torch.cat([self.patchify(t.latent.to(dt)) for t in tasks], 0)
         x = _lin(self.patch_embedding, x)  # [S*T, dim]
         mods, heads_e = [], []
@@ -400,6 +405,7 @@ class WanDiT(nn.Module):
                 rope = rope_fn if rope_fn is not None else kernels.rope_apply
                 rq_all = torch.stack([rope(q[i], *ropes[i]) for i in range(S)])
                 rk_all = torch.stack([rope(ku_all[i], *ropes[i]) for i in range(S)])
+            last = li == len(self.blocks) - 1
             o = torch.empty((S, T, H, D), device=dev, dtype=dt)
             for i in order:
                 tk = tasks[i]
@@ -413,7 +419,22 @@ class WanDiT(nn.Module):
                                    num_frames_per_block=cfg.frames_per_block)
                 else:
                     K, V = rk[None], v[i][None]
-                o[i] = dispatch_attention(rq[None], K, V)[0]
+                if not (last and tk.kv_only):
+                    o[i] = dispatch_attention(rq[None], K, V)[0]
+            if last and len(keep) < S:
+                # past the last layer's K/V nothing of a K/V-only task is used:
+                # the rest of the layer and the head run on the other tasks' rows
+                if not keep:
+                    return [None] * S
+                rows = torch.tensor(keep, device=dev)
+                xs = xs.view(S, T, dim).index_select(0, rows).reshape(len(keep) * T, dim)
+                o = o.index_select(0, rows)
+                e_all = e_all.index_select(0, rows).contiguous()
+                if pending is not None:
+                    pending = (pending[0].view(S, T, dim).index_select(0, rows).reshape(len(keep) * T, dim),
+                               pending[1].index_select(0, rows).contiguous())
+                heads_e = [heads_e[i] for i in keep]
+                S = len(keep)
             y = _lin(b.self_attn.o, o.view(S * T, dim))
             # cross-attention: all stages share the text K/V -> one call
             if fused and w8a8_channel(b.cross_attn.q):
@@ -468,7 +489,10 @@ class WanDiT(nn.Module):
         else:
             h = ln_mod(xs, eh, 0)
         out = _lin(self.head, h).view(S, T, -1)
-        return [self.unpatchify(out[i].float(), cfg.frames_per_block) for i in range(S)]
+        res = [None] * len(tasks)
+        for j, i in enumerate(keep):
+            res[i] = self.unpatchify(out[j].float(), cfg.frames_per_block)
+        return res
 
 
 class FlowMatch:

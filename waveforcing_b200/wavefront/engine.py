@@ -217,7 +217,9 @@ class WavefrontEngine:
                 c = t - self.store
                 exch = self.xport.make_store_exch(self.clean, store_kv, c, act, t, self._rope,
                                                   rope_tab_fn=self._rope_tab)
-                tasks.append(StageTask(self.inputs[s], cfg.context_noise, c * cfg.npb, s, exch))
+                # the store's flow output is never used (its input chunk is the final latent):
+                # only its K/V are needed, so its last layer stops after the publish
+                tasks.append(StageTask(self.inputs[s], cfg.context_noise, c * cfg.npb, s, exch, kv_only=True))
         # no publish of this tick may land in a slab generation that a remote
         # consumer is still reading (it read that generation two ticks ago)
         self.xport.acquire_slots(t)
