@@ -245,3 +245,50 @@ def test_fp8_compact_slots_cover_received_chunks(golden):
             assert all(0 <= c < S - m for c in got)
             seen += 1
     assert seen > 50
+
+
+def test_kv_only_task_leaves_the_other_stages_unchanged(monkeypatch):
+    """The store stage's flow output is never read (its input chunk is the
+    final latent), so its task is K/V-only: the last layer stops after the
+    K/V publish.  The other stages' outputs must equal a forward where every
+    task runs to the head, the K/V-only task returns None, its last-layer
+    self-attention is skipped, and a batch of K/V-only tasks returns all None.
+    Tiny DiT on CPU with plain torch ops."""
+    from waveforcing_b200 import kernels
+    from waveforcing_b200.runtime import backend
+    from waveforcing_b200.wavefront import dit as D
+
+    def rope_torch(x, cos, sin, out=None):
+        xf = x.float().reshape(*x.shape[:-1], -1, 2)
+        re, im = xf[..., 0], xf[..., 1]
+        c, s = cos[:, None, :], sin[:, None, :]
+        return torch.stack([re * c - im * s, re * s + im * c], -1).flatten(-2).to(x.dtype)
+
+    calls = {"self": 0}
+    orig_self = D.dispatch_attention
+
+    def count_self(*a):
+        calls["self"] += 1
+        return orig_self(*a)
+
+    monkeypatch.setattr(kernels, "rope_apply", rope_torch)
+    monkeypatch.setitem(backend._WAVE_STATE, "attn", "torch_sdpa")
+    monkeypatch.setattr(D, "dispatch_attention", count_self)
+    cfg = D.DiTConfig(dim=256, heads=2, layers=2, ffn=512, text_len=16, text_dim=64, lat_h=4, lat_w=4)
+    m = D.WanDiT.random(cfg, torch.device("cpu"), seed=0)
+    g = torch.Generator().manual_seed(1)
+    m.set_text(torch.randn(cfg.text_len, cfg.text_dim, generator=g))
+    lat = [torch.randn(cfg.in_ch, cfg.frames_per_block, cfg.lat_h, cfg.lat_w, generator=g) for _ in range(3)]
+
+    def tasks(kv_only):
+        return [D.StageTask(lat[i], t, 3 * i, i, kv_only=k)
+                for i, (t, k) in enumerate(zip((900.0, 0.0, 500.0), kv_only))]
+
+    full = m.forward_stages(tasks((False, False, False)), fused=False)
+    calls["self"] = 0
+    part = m.forward_stages(tasks((False, True, False)), fused=False)
+    assert part[1] is None
+    assert calls["self"] == cfg.layers * 3 - 1
+    for i in (0, 2):
+        torch.testing.assert_close(part[i], full[i], rtol=1e-5, atol=1e-5)  # fewer GEMM rows only
+    assert m.forward_stages(tasks((True, True, True))[:1], fused=False) == [None]
