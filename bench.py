@@ -91,6 +91,10 @@ def parse():
     ap.add_argument("--trace", action="store_true",
                     help="profile two steady ticks with torch.profiler (CUPTI): in-stream kernel time, device idle "
                          "inside the tick, per-kernel shares (one JSON line; no bench line)")
+    ap.add_argument("--timeline", default="",
+                    help="after the timed ticks, write a cross-rank device timeline of --steps more steady ticks to "
+                         "this JSON file: globaltimer stamps at every tick phase, layer entry and remote flag wait, "
+                         "aligned at a world all_reduce (no profiler; one extra summary JSON line)")
     ap.add_argument("--forward", action="store_true",
                     help="BASELINE config 2: one full DiT forward of a 3-frame chunk at t=600 with a 6-chunk context")
     return ap.parse_args()
@@ -533,6 +537,47 @@ def trace_ticks(args, make_engine, noise_cpu, fill, dev, rank, n_trace: int = 2)
             flush=True)
 
 
+def timeline_ticks(args, eng, t0, dev, rank, world):
+    """Device stamps (``wf_stamp``) of ``args.steps`` further steady ticks of
+    ``eng`` (from tick ``t0``) on every rank, aligned at a world all_reduce,
+    written to ``args.timeline``.  Per rank and tick they give the stream's
+    phase times (begin, slots acquired, forward done, promotion, migration
+    received) and per layer the entry and the end of each remote flag wait.
+    Run after the timed ticks, so the stamps' launches are not in them."""
+    from waveforcing_b200.wavefront.timeline import Timeline
+
+    torch.cuda.synchronize()
+    tl = Timeline(dev)
+    eng.timeline = tl
+    eng.xport.timeline = tl
+    tl.align()
+    for i in range(args.steps):
+        eng.tick(t0 + i)
+    rows = tl.rows()
+    eng.timeline = eng.xport.timeline = None
+    mine = {"rank": rank, "stages": list(eng.local), "rows": rows}
+    allr = [mine]
+    if world > 1:
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+    if rank == 0:
+        with open(args.timeline, "w") as f:
+            json.dump({"ticks": [t0, t0 + args.steps], "ranks": allr,
+                       "migration": "split" if os.environ.get("WFK_MIGRATE_SPLIT", "0") == "1" else "batched"}, f)
+        span = {}
+        for r in allr:
+            d = dict(r["rows"])
+            for i in range(args.steps):
+                t = t0 + i
+                if f"t{t}.begin" in d and f"t{t}.migrated" in d:
+                    span.setdefault(t, []).append((r["rank"], d[f"t{t}.begin"], d[f"t{t}.forward"],
+                                                   d[f"t{t}.migrated"]))
+        ticks = sorted(span)
+        period = [(max(x[3] for x in span[b]) - max(x[3] for x in span[a])) / 1e3 for a, b in zip(ticks, ticks[1:])]
+        print(json.dumps({"timeline": args.timeline, "ticks": ticks, "stamps_per_rank": [len(r["rows"]) for r in allr],
+                          "tick_period_ms": period}), flush=True)
+
+
 # ---------------------------------------------------------------- GPU side
 def run_gpu_arm(args):
     from waveforcing_b200 import kernels
@@ -557,7 +602,7 @@ def run_gpu_arm(args):
     steps_list = tuple(int(s) for s in args.denoise_steps.split(","))
     S = len(steps_list)
     fill = S + 8  # first tick with every stage active and anchor + 7 clean pages
-    n_ticks = fill + args.warmup + args.steps
+    n_ticks = fill + args.warmup + args.steps * (2 if args.timeline else 1)
     cfg = DiTConfig.preset(args.preset)
     # the 399-frame run; only its first n_ticks ticks are executed (fill, warm-up, timed steady window)
     ecfg = EngineConfig(steps=steps_list, num_frames=399, fp8_kv=(args.kv == "fp8"))
@@ -640,6 +685,8 @@ def run_gpu_arm(args):
     crit = -max_over_ranks([-wait_ms_rank if eng.local else float("-inf")])[0]
     stage0_wait = max_over_ranks([wait_ms_rank if 0 in eng.local else 0.0])[0]
     host_p50 = max_over_ranks([statistics.median(host_ms)])[0]
+    if args.timeline:
+        timeline_ticks(args, eng, fill + args.warmup + args.steps, dev, rank, world)
     eng.close()
     del eng
     torch.cuda.empty_cache()

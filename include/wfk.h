@@ -352,6 +352,13 @@ int wf_stream_wait_u32(void* stream, const void* addr, uint32_t value);
  * wait of wave_rt/denoiser/exchange/paged.py:147-154, which has no timeout. */
 int wf_wait_flag(const void* flag, uint32_t value, uint64_t timeout_ns, uint32_t* timeout_out, void* stream);
 
+/* Diagnostic (no counterpart in the reference): a one-thread kernel on
+ * `stream` writes the device's %globaltimer (ns) to *dst (8-byte aligned
+ * device memory) when the stream reaches it.  Stamps of one tick on every
+ * rank, aligned at a common collective, give the cross-rank timeline of the
+ * wavefront. */
+int wf_stamp(uint64_t* dst, void* stream);
+
 /* Asynchronous device-to-device (or peer) copy of `bytes`; replaces
  * memcpy_dtod_async, wave_rt/distributed/ipc.py:60-67. */
 int wf_memcpy_async(void* dst, const void* src, uint64_t bytes, void* stream);

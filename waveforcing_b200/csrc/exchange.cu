@@ -37,6 +37,9 @@ __global__ void wait_flag_kernel(const unsigned int* __restrict__ flag, unsigned
   }
 }
 
+// Writes the device's %globaltimer (ns) to *dst when the stream reaches it.
+__global__ void stamp_kernel(unsigned long long* __restrict__ dst) { *dst = globaltimer_ns(); }
+
 }  // namespace xchg
 }  // namespace wfk
 
@@ -115,6 +118,13 @@ extern "C" int wf_wait_flag(const void* flag, uint32_t value, uint64_t timeout_n
     return fail(WF_ERR_INVALID_ARG, "wf_wait_flag: timeout must be in (0, 600 s]");
   wait_flag_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const unsigned int*>(flag), value,
                                                                    timeout_ns, timeout_out);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_stamp(uint64_t* dst, void* stream) {
+  if (!dst || (reinterpret_cast<uintptr_t>(dst) & 7)) return fail(WF_ERR_INVALID_ARG, "wf_stamp: bad dst");
+  stamp_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<unsigned long long*>(dst));
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

@@ -147,6 +147,7 @@ class PagedTransport:
         # when a list, every remote flag wait appends its (start, end) CUDA events:
         # the exposed part of the exchange on this rank's compute stream
         self.wait_timer = None
+        self.timeline = None  # optional Timeline: stamps at layer entry and after each remote wait
         # destination tables: consumer stage -> dict of base pointers (local or peer)
         self.dst: dict = {}
         self._exchange_handles()
@@ -362,6 +363,8 @@ class PagedTransport:
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record(cur)
         ipc.wait_flag_bounded(self._cur_stream_handle(), addr, tick, self.timeout_s, self.timeout_word.data_ptr())
+        if self.timeline is not None:
+            self.timeline.mark(f"s{m}.L{layer}.w{src}")
         if sink is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record(cur)
@@ -523,6 +526,8 @@ class PagedTransport:
             v = value[0]
             lp = prof() if prof is not None else None
             e_en = self._lp_mark(lp)
+            if self.timeline is not None:
+                self.timeline.mark(f"s{m}.L{Lh}.in")
             self.publish(m, k, v, send, Lh, gen, tick, prepublished=Lh in getattr(exch, "prepublished", ()))
             e_pub = self._lp_mark(lp)
             if self.fp8:
@@ -600,6 +605,8 @@ class PagedTransport:
             v = value[0]
             lp = prof() if prof is not None else None
             e_en = self._lp_mark(lp)
+            if self.timeline is not None:
+                self.timeline.mark(f"s{self.store}.L{layer_idx}.in")
             self.publish(self.store, k, v, send, layer_idx, gen, tick,
                          prepublished=layer_idx in getattr(exch, "prepublished", ()))
             e_pub = self._lp_mark(lp)

@@ -17,6 +17,8 @@ their linears.  Ranks beyond the stage count stay idle.
 
 from __future__ import annotations
 
+import os
+
 import time
 from dataclasses import dataclass, field
 
@@ -152,6 +154,13 @@ class WavefrontEngine:
             noise = torch.randn((C, cfg.num_frames, mc.lat_h, mc.lat_w), generator=g).to(torch.bfloat16)
         self.noise = noise  # [C, F_total, H, W]; may live on the host (pinned) or the device
         self.mig_shape = (self.S + 1, C, cfg.npb, mc.lat_h, mc.lat_w)
+        self.timeline = None  # optional Timeline (diagnostic): stamps of each tick's phases
+        # WFK_MIGRATE_SPLIT=1: each hand-off is its own send or receive, and the
+        # compute stream waits on the receives only (a batched send/receive
+        # group also holds the sender's next tick until the receiver has
+        # finished its own tick)
+        self.split_migration = os.environ.get("WFK_MIGRATE_SPLIT", "0") == "1"
+        self._sends: list = []  # (work, tensor) of split-mode sends still in flight
 
     # ----------------------------------------------------------------- helpers
     @property
@@ -201,6 +210,9 @@ class WavefrontEngine:
         oldest = (t - max(act)) if act else 0
         tick_csf, tick_qf = oldest * cfg.npb, len(act) * cfg.npb
         store_active = self.act_store(t)
+        tl = self.timeline
+        if tl is not None:
+            tl.mark(f"t{t}.begin")
         if 0 in self.local and self.act_denoise(0, t):
             self.inputs[0] = self.noise_chunk(t)
         tasks = []
@@ -223,9 +235,13 @@ class WavefrontEngine:
         # no publish of this tick may land in a slab generation that a remote
         # consumer is still reading (it read that generation two ticks ago)
         self.xport.acquire_slots(t)
+        if tl is not None:
+            tl.mark(f"t{t}.acquired")
         flows = self.m.forward_stages(tasks) if tasks else []
         self.xport.drain()
         self.xport.release_slots(t)
+        if tl is not None:
+            tl.mark(f"t{t}.forward")
         out = {}
         for task, flow in zip(tasks, flows):
             if task.stage < S:
@@ -234,7 +250,11 @@ class WavefrontEngine:
             else:
                 self.final[task.start_frame // cfg.npb] = task.latent
         self._promote(t, store_active, store_kv, store_slot, bool(tasks))
+        if tl is not None:
+            tl.mark(f"t{t}.promoted")
         self._migrate(t, out)
+        if tl is not None:
+            tl.mark(f"t{t}.migrated")
         return out
 
     def _promote(self, t, store_active, store_kv, store_slot, had_task) -> None:
@@ -306,7 +326,19 @@ class WavefrontEngine:
                 buf = torch.empty(self.mig_shape[1:], device=self.device, dtype=torch.bfloat16)
                 ops.append(dist.P2POp(dist.irecv, buf, self._peer(src_rank), group=self.group))
                 recv[dst_stage] = buf
-        if ops:
+        if ops and self.split_migration:
+            # sends of the previous tick: long complete (their receivers have
+            # since finished a tick); the wait releases their buffers in order
+            for w, _buf in self._sends:
+                w.wait()
+            self._sends = []
+            for op in ops:
+                w = op.op(op.tensor, op.peer, group=op.group)
+                if op.op is dist.irecv:
+                    w.wait()
+                else:
+                    self._sends.append((w, op.tensor))
+        elif ops:
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
         self.inputs.update(recv)
@@ -316,4 +348,7 @@ class WavefrontEngine:
         return r if self.group is None else dist.get_global_rank(self.group, r)
 
     def close(self) -> None:
+        for w, _buf in self._sends:
+            w.wait()
+        self._sends = []
         self.xport.close()
