@@ -562,8 +562,7 @@ def timeline_ticks(args, eng, t0, dev, rank, world):
         dist.all_gather_object(allr, mine)
     if rank == 0:
         with open(args.timeline, "w") as f:
-            json.dump({"ticks": [t0, t0 + args.steps], "ranks": allr,
-                       "migration": "split" if os.environ.get("WFK_MIGRATE_SPLIT", "0") == "1" else "batched"}, f)
+            json.dump({"ticks": [t0, t0 + args.steps], "ranks": allr}, f)
         span = {}
         for r in allr:
             d = dict(r["rows"])

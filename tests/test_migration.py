@@ -92,8 +92,8 @@ def _result(s, t, shape):
     return torch.randn(shape, generator=g).to(torch.bfloat16)
 
 
-def _worker(rank, world, port, q, delay_release, split=False):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WFK_MIGRATE_SPLIT="1" if split else "0")
+def _worker(rank, world, port, q, delay_release):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     paged.ipc = ShmIPC()
     try:
@@ -134,11 +134,11 @@ def _port():
     return p
 
 
-def _run(world, delay_release=False, split=False):
+def _run(world, delay_release=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, q, delay_release, split)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q, delay_release)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -151,13 +151,9 @@ def _run(world, delay_release=False, split=False):
     return res
 
 
-@pytest.mark.parametrize("split", [False, True], ids=["batched", "split"])
 @pytest.mark.parametrize("world", [2, 3])
-def test_p2p_migration_delivers_every_hand_off(world, split):
-    """Both migration modes: one batched send/receive group per rank and
-    tick, or (WFK_MIGRATE_SPLIT=1) separate sends and receives with the
-    stream waiting on the receives only."""
-    res = _run(world, split=split)
+def test_p2p_migration_delivers_every_hand_off(world):
+    res = _run(world)
     for r, (local, got, _w, tw, _rc, _sr) in res.items():
         assert not isinstance(local, str), local
         assert tw == 0, f"rank {r}: a credit wait timed out"

@@ -17,8 +17,6 @@ their linears.  Ranks beyond the stage count stay idle.
 
 from __future__ import annotations
 
-import os
-
 import time
 from dataclasses import dataclass, field
 
@@ -155,12 +153,6 @@ class WavefrontEngine:
         self.noise = noise  # [C, F_total, H, W]; may live on the host (pinned) or the device
         self.mig_shape = (self.S + 1, C, cfg.npb, mc.lat_h, mc.lat_w)
         self.timeline = None  # optional Timeline (diagnostic): stamps of each tick's phases
-        # WFK_MIGRATE_SPLIT=1: each hand-off is its own send or receive, and the
-        # compute stream waits on the receives only (a batched send/receive
-        # group also holds the sender's next tick until the receiver has
-        # finished its own tick)
-        self.split_migration = os.environ.get("WFK_MIGRATE_SPLIT", "0") == "1"
-        self._sends: list = []  # (work, tensor) of split-mode sends still in flight
 
     # ----------------------------------------------------------------- helpers
     @property
@@ -326,19 +318,7 @@ class WavefrontEngine:
                 buf = torch.empty(self.mig_shape[1:], device=self.device, dtype=torch.bfloat16)
                 ops.append(dist.P2POp(dist.irecv, buf, self._peer(src_rank), group=self.group))
                 recv[dst_stage] = buf
-        if ops and self.split_migration:
-            # sends of the previous tick: long complete (their receivers have
-            # since finished a tick); the wait releases their buffers in order
-            for w, _buf in self._sends:
-                w.wait()
-            self._sends = []
-            for op in ops:
-                w = op.op(op.tensor, op.peer, group=op.group)
-                if op.op is dist.irecv:
-                    w.wait()
-                else:
-                    self._sends.append((w, op.tensor))
-        elif ops:
+        if ops:
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
         self.inputs.update(recv)
@@ -348,7 +328,4 @@ class WavefrontEngine:
         return r if self.group is None else dist.get_global_rank(self.group, r)
 
     def close(self) -> None:
-        for w, _buf in self._sends:
-            w.wait()
-        self._sends = []
         self.xport.close()
