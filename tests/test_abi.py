@@ -96,18 +96,28 @@ def test_constants_match_the_header():
     ("wf_rope_apply", (None, None, None, None, 4, 2, 128, 256, 256, None), 1),
     ("wf_ln_modulate", (None, 16, None, None, 16, None, 16, 4, 16, 4, 1e-6, None), 1),
     ("wf_gate_residual", (None, 16, None, 16, None, 16, 4, 16, 4, None), 1),
-    # gate_residual_then: both outputs, shift without scale, unknown qtype
-    ("wf_gate_residual_then", (16, 16, 16, 16, 16, 16, 4, 16, 16, 16, 4, 1e-6, 16, 16, 16, 16, 1, 4, 1536, None),
-     1),
-    ("wf_gate_residual_then", (16, 16, 16, 16, 16, 16, 4, 16, None, 16, 4, 1e-6, 16, 16, None, None, 1, 4, 1536,
+    # gate_residual_then: both outputs, shift without scale, unknown qtype, row strides below dim
+    ("wf_gate_residual_then", (16, 1536, 16, 1536, 16, 16, 4, 16, 16, 16, 4, 1e-6, 16, 1536, 16, 16, 1, 4, 1536,
                                None), 1),
-    ("wf_gate_residual_then", (16, 16, 16, 16, 16, 16, 4, None, None, 0, 1, 1e-6, None, 16, 16, 16, 7, 4, 1536,
-                               None), 2),
+    ("wf_gate_residual_then", (16, 1536, 16, 1536, 16, 16, 4, 16, None, 16, 4, 1e-6, 16, 1536, None, None, 1, 4,
+                               1536, None), 1),
+    ("wf_gate_residual_then", (16, 1536, 16, 1536, 16, 16, 4, None, None, 0, 1, 1e-6, None, 1536, 16, 16, 7, 4,
+                               1536, None), 2),
+    ("wf_gate_residual_then", (16, 16, 16, 1536, 16, 16, 4, None, None, 0, 1, 1e-6, None, 1536, 16, 16, 1, 4,
+                               1536, None), 1),
+    ("wf_gate_residual_then", (16, 1536, 16, 1536, 16, 16, 4, 16, 16, 16, 4, 1e-6, 16, 8, None, None, 1, 4, 1536,
+                               None), 1),
     ("wf_rms_norm", (None, 16, None, None, 16, 4, 16, 1e-6, None), 1),
     ("wf_channel_rmsnorm", (16, 16, 4, 12, 16, 1e-12, 1, None), 1),         # C not a multiple of 8
     ("wf_interleave_time2", (16, 16, 2, 4, 16, None), 1),                    # in place
     ("wf_channel_bias_add", (16, 16, None, 16, 4, 12, None), 1),            # C not a multiple of 8
     ("wf_upsample2x_nearest", (16, 16, 1, 4, 4, 16, None), 1),              # in place
+    # sizes whose element count overflows (rejected before any launch)
+    ("wf_channel_rmsnorm", (16, 32, 1 << 62, 16, 48, 1e-12, 0, None), 1),
+    ("wf_interleave_time2", (16, 32, 1 << 40, 1 << 20, 16, None), 1),
+    ("wf_channel_bias_add", (16, 16, None, 32, 1 << 61, 64, None), 1),
+    ("wf_upsample2x_nearest", (16, 32, 1 << 30, 1 << 20, 1 << 20, 16, None), 1),
+    ("wf_stamp", (12, None), 1),                                              # misaligned destination
     ("wf_ipc_close", (None,), 1),
     ("wf_stream_write_u32", (None, 18, 1), 1),                                # misaligned flag address
     ("wf_wait_flag", (16, 1, 0, None, None), 1),                              # zero timeout

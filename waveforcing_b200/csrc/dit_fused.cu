@@ -429,14 +429,15 @@ extern "C" int wf_gate_residual_then(void* x, int64_t x_stride, const void* y, i
                                      float* x_scale, int qtype, int64_t rows, int64_t dim, void* stream) {
   const bool mod = shift != nullptr || scale != nullptr;
   if (!x || !y || !gate || rows < 0 || gate_rows_per_stage < 1 || !aligned16(x) || !aligned16(y) ||
-      !aligned16(gate) || x_stride % 8 || y_stride % 8 || gate_stride % 4)
+      !aligned16(gate) || x_stride % 8 || y_stride % 8 || gate_stride % 4 || x_stride < dim || y_stride < dim ||
+      gate_stride < 0 || rows > (int64_t{1} << 34))
     return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: bad residual arguments");
   if (mod && (!shift || !scale || !aligned16(shift) || !aligned16(scale) || mod_stride % 4 || mod_rows_per_stage < 1))
     return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: shift and scale go together (16-byte aligned)");
   if ((out != nullptr) == (xq != nullptr))
     return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: exactly one of out / xq");
   if (!mod && !xq) return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: without modulation only xq output");
-  if (out && (!aligned16(out) || out_stride % 8))
+  if (out && (!aligned16(out) || out_stride % 8 || out_stride < dim))
     return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: out must be 16-byte aligned rows");
   if (xq && (!x_scale || !aligned16(xq)))
     return fail(WF_ERR_INVALID_ARG, "wf_gate_residual_then: xq (16-byte aligned) needs x_scale");

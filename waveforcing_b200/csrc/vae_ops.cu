@@ -137,6 +137,19 @@ __global__ void __launch_bounds__(256) upsample2x_kernel(const uint4* __restrict
   }
 }
 
+// Rejects element counts whose product would overflow int64 or exceed 2^46
+// 16-byte chunks (1 PiB): no device buffer is that large, so such sizes are
+// caller errors, reported before any launch.
+static bool too_big(int64_t a, int64_t b, int64_t c = 1, int64_t d = 1) {
+  constexpr int64_t LIM = int64_t{1} << 46;
+  int64_t p = 1;
+  for (int64_t f : {a, b, c, d}) {
+    if (f < 0 || (f > 0 && p > LIM / f)) return true;
+    p *= f;
+  }
+  return false;
+}
+
 static unsigned grid_for(int64_t n) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -156,6 +169,8 @@ extern "C" int wf_channel_rmsnorm(const void* x, void* out, int64_t rows, int64_
   if (!x || !out || !gamma || rows < 0 || C < 8 || C % 8 || C > 8 * TPR * 8 || !aligned16(x) || !aligned16(out) ||
       !aligned16(gamma))
     return fail(WF_ERR_INVALID_ARG, "wf_channel_rmsnorm: need C a multiple of 8 up to 1024 and 16-byte aligned rows");
+  if (rows > (int64_t{0x7fffffff} * 256) / TPR)
+    return fail(WF_ERR_INVALID_ARG, "wf_channel_rmsnorm: rows beyond one launch's grid");
   if (rows == 0) return WF_OK;
   const int64_t threads = rows * TPR;
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
@@ -187,6 +202,7 @@ extern "C" int wf_channel_rmsnorm(const void* x, void* out, int64_t rows, int64_
 extern "C" int wf_interleave_time2(const void* src, void* dst, int64_t frames, int64_t hw, int64_t C, void* stream) {
   if (!src || !dst || frames < 0 || hw < 1 || C < 8 || C % 8 || !aligned16(src) || !aligned16(dst) || src == dst)
     return fail(WF_ERR_INVALID_ARG, "wf_interleave_time2: need C a multiple of 8, 16-byte aligned distinct buffers");
+  if (too_big(frames, 2 * hw, C / 8)) return fail(WF_ERR_INVALID_ARG, "wf_interleave_time2: size overflows");
   if (frames == 0) return WF_OK;
   const int64_t n = frames * 2 * hw * (C / 8);
   int dev = 0, sms = 148;
@@ -204,6 +220,7 @@ extern "C" int wf_channel_bias_add(const void* x, const void* bias, const void* 
   if (!x || !bias || !out || rows < 0 || C < 8 || C % 8 || !aligned16(x) || !aligned16(bias) || !aligned16(out) ||
       (res && !aligned16(res)))
     return fail(WF_ERR_INVALID_ARG, "wf_channel_bias_add: need C a multiple of 8 and 16-byte aligned rows");
+  if (too_big(rows, C / 8)) return fail(WF_ERR_INVALID_ARG, "wf_channel_bias_add: size overflows");
   if (rows == 0) return WF_OK;
   const int64_t n16 = rows * (C / 8);
   bias_add_kernel<<<grid_for(n16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -218,6 +235,7 @@ extern "C" int wf_upsample2x_nearest(const void* src, void* dst, int64_t images,
   if (!src || !dst || images < 0 || h < 1 || w < 1 || C < 8 || C % 8 || !aligned16(src) || !aligned16(dst) ||
       src == dst)
     return fail(WF_ERR_INVALID_ARG, "wf_upsample2x_nearest: need C a multiple of 8, 16-byte aligned distinct buffers");
+  if (too_big(images, 4 * h, w, C / 8)) return fail(WF_ERR_INVALID_ARG, "wf_upsample2x_nearest: size overflows");
   if (images == 0) return WF_OK;
   const int64_t n = images * h * w * (C / 8);
   upsample2x_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
