@@ -754,6 +754,7 @@ def run_gpu_arm(args):
         line = {
             "metric": metric_name(args), "value": fps, "unit": "FPS", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "tick_ms_p50": p50,
+            "tick_ms": [round(x, 2) for x in tick_ms],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init N(0,0.02) weights, N(0,1) text, seed-0 Gaussian noise)",
             "config": bench_config(args, world),
