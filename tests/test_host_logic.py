@@ -194,9 +194,9 @@ def test_dit_routes_only_self_attention_through_the_backend(monkeypatch):
     calls = {"self": 0, "cross": 0}
     orig_self, orig_cross = D.dispatch_attention, D.sdpa_elsewhere
 
-    def count_self(*a):
+    def count_self(*a, **kw):
         calls["self"] += 1
-        return orig_self(*a)
+        return orig_self(*a, **kw)
 
     def count_cross(*a):
         calls["cross"] += 1
@@ -267,9 +267,9 @@ def test_kv_only_task_leaves_the_other_stages_unchanged(monkeypatch):
     calls = {"self": 0}
     orig_self = D.dispatch_attention
 
-    def count_self(*a):
+    def count_self(*a, **kw):
         calls["self"] += 1
-        return orig_self(*a)
+        return orig_self(*a, **kw)
 
     monkeypatch.setattr(kernels, "rope_apply", rope_torch)
     monkeypatch.setitem(backend._WAVE_STATE, "attn", "torch_sdpa")

@@ -35,11 +35,12 @@ def set_exchange_fn(fn: Callable | None) -> None:
 
 
 def wf_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
-                 softmax_scale: float | None = None) -> torch.Tensor:
-    """flash_attn_func-compatible call: q [B, Lq, H, D], k/v [B, Lk, H, D] -> [B, Lq, H, D]."""
+                 softmax_scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """flash_attn_func-compatible call: q [B, Lq, H, D], k/v [B, Lk, H, D] -> [B, Lq, H, D]
+    (written into ``out`` when given, e.g. a caller's batched output rows)."""
     if causal:
         raise ValueError("wf_b200 attention is non-causal; block causality comes from the K/V context")
-    return kernels.attention(q, k, v, softmax_scale=softmax_scale)
+    return kernels.attention(q, k, v, softmax_scale=softmax_scale, out=out)
 
 
 def enable_wf_b200() -> None:
@@ -83,15 +84,23 @@ def set_attention_timer(sink: list | None) -> None:
     _WAVE_STATE["attn_timer"] = sink
 
 
-def dispatch_attention(roped_query: torch.Tensor, ctx_k: torch.Tensor, ctx_v: torch.Tensor) -> torch.Tensor:
-    """The branch of wave_rt/runtime/backend.py:141-148 with wf_b200 added."""
+def dispatch_attention(roped_query: torch.Tensor, ctx_k: torch.Tensor, ctx_v: torch.Tensor,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """The branch of wave_rt/runtime/backend.py:141-148 with wf_b200 added.
+    With ``out`` the result lands there: the wf_b200 kernel writes it
+    directly, other backends copy into it."""
     sink = _WAVE_STATE.get("attn_timer")
     if sink is not None:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-    if _WAVE_STATE["attn"] == "wf_b200":
-        out = _WAVE_STATE["fa_func"](roped_query, ctx_k, ctx_v, causal=False)
+    if _WAVE_STATE["attn"] == "wf_b200" and _WAVE_STATE["fa_func"] is wf_attention:
+        out = wf_attention(roped_query, ctx_k, ctx_v, causal=False, out=out)
+    elif _WAVE_STATE["attn"] == "wf_b200":
+        res = _WAVE_STATE["fa_func"](roped_query, ctx_k, ctx_v, causal=False)
+        out = res if out is None else out.copy_(res)
+    elif out is not None:
+        out.copy_(_torch_sdpa(roped_query, ctx_k, ctx_v))
     else:
         out = _torch_sdpa(roped_query, ctx_k, ctx_v)
     if sink is not None:

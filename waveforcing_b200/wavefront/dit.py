@@ -355,8 +355,10 @@ class WanDiT(nn.Module):
         # q quantiser when that linear is W8A8, the cross-attention's by the
         # FFN's LN-modulate.
         pending = None  # (y, e_all) of the previous layer's FFN residual, not yet added (gate e_all[:, 5])
+        # every layer's modulation in two launches: [layers, S, 6, dim] f32
+        e_layers = (torch.stack([b.modulation.float() for b in self.blocks]) + mods[None]).contiguous()
         for li, b in enumerate(self.blocks):
-            e_all = (b.modulation.float() + mods).contiguous()  # [S, 6, dim]
+            e_all = e_layers[li]  # [S, 6, dim], contiguous
             fq = None if (separate_qkv and not fused) else self._fused_qkv(b)
             qkv_w8 = fused and fq is not None and not isinstance(fq[0], torch.Tensor) and w8a8_channel(fq[0])
             if fused and fq is not None and pending is not None:
@@ -420,7 +422,7 @@ class WanDiT(nn.Module):
                 else:
                     K, V = rk[None], v[i][None]
                 if not (last and tk.kv_only):
-                    o[i] = dispatch_attention(rq[None], K, V)[0]
+                    dispatch_attention(rq[None], K, V, out=o[i][None])  # written in place
             if last and len(keep) < S:
                 # past the last layer's K/V nothing of a K/V-only task is used:
                 # the rest of the layer and the head run on the other tasks' rows
