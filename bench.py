@@ -583,6 +583,7 @@ def run_gpu_arm(args):
     from waveforcing_b200.runtime import backend
     from waveforcing_b200.runtime.fp8 import quantize_transformer_w8a8
     from waveforcing_b200.wavefront.dit import DiTConfig, WanDiT
+    from waveforcing_b200.wavefront import engine as engine_mod
     from waveforcing_b200.wavefront.engine import EngineConfig, WavefrontEngine
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -653,11 +654,12 @@ def run_gpu_arm(args):
     host_ms = []
     evs[0].record()
     torch.cuda.nvtx.range_push("timed")
-    for i in range(args.steps):
-        h0 = time.perf_counter()
-        eng.tick(fill + args.warmup + i)
-        host_ms.append((time.perf_counter() - h0) * 1e3)
-        evs[i + 1].record()
+    with engine_mod.steady_host():
+        for i in range(args.steps):
+            h0 = time.perf_counter()
+            eng.tick(fill + args.warmup + i)
+            host_ms.append((time.perf_counter() - h0) * 1e3)
+            evs[i + 1].record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
@@ -707,13 +709,14 @@ def run_gpu_arm(args):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(nt + 1)]
         ev[0].record()
         d2h = 0
-        for t in range(nt):
-            eng.tick(t)  # copies its noise chunk from pinned host memory (engine.noise_chunk)
-            c = t - eng.store
-            if c in eng.final:
-                out_host.copy_(eng.final.pop(c), non_blocking=True)
-                d2h += out_host.numel() * out_host.element_size()
-            ev[t + 1].record()
+        with engine_mod.steady_host():
+            for t in range(nt):
+                eng.tick(t)  # copies its noise chunk from pinned host memory (engine.noise_chunk)
+                c = t - eng.store
+                if c in eng.final:
+                    out_host.copy_(eng.final.pop(c), non_blocking=True)
+                    d2h += out_host.numel() * out_host.element_size()
+                ev[t + 1].record()
         torch.cuda.synchronize()
         barrier()
         tms = max_over_ranks([ev[i].elapsed_time(ev[i + 1]) for i in range(nt)])

@@ -352,6 +352,14 @@ int wf_stream_wait_u32(void* stream, const void* addr, uint32_t value);
  * wait of wave_rt/denoiser/exchange/paged.py:147-154, which has no timeout. */
 int wf_wait_flag(const void* flag, uint32_t value, uint64_t timeout_ns, uint32_t* timeout_out, void* stream);
 
+/* wf_wait_flag over n (0..32) flags in one launch: `flags` is a HOST array of
+ * n device addresses (4-byte aligned); the stream continues once every flag
+ * is >= value or its wait timed out (same timeout report as wf_wait_flag).
+ * A consumer's waits for all its producers of one layer, which the reference
+ * issues one per producer (wave_rt/denoiser/exchange/paged.py:147-154). */
+int wf_wait_flags(const void* const* flags, int n, uint32_t value, uint64_t timeout_ns, uint32_t* timeout_out,
+                  void* stream);
+
 /* Diagnostic (no counterpart in the reference): a one-thread kernel on
  * `stream` writes the device's %globaltimer (ns) to *dst (8-byte aligned
  * device memory) when the stream reaches it.  Stamps of one tick on every

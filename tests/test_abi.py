@@ -121,6 +121,9 @@ def test_constants_match_the_header():
     ("wf_ipc_close", (None,), 1),
     ("wf_stream_write_u32", (None, 18, 1), 1),                                # misaligned flag address
     ("wf_wait_flag", (16, 1, 0, None, None), 1),                              # zero timeout
+    ("wf_wait_flags", (None, 2, 1, 1000, None, None), 1),                     # no address array
+    ("wf_wait_flags", ((C.c_void_p * 1)(18), 1, 1, 1000, None, None), 1),  # misaligned flag
+    ("wf_wait_flags", ((C.c_void_p * 1)(16), 33, 1, 1000, None, None), 1),  # more than 32 flags
     ("wf_memcpy_async", (None, None, 16, None), 1),
 ])
 def test_entry_points_reject_bad_arguments(name, args, code):

@@ -72,6 +72,10 @@ class ShmIPC:
     def stream_write_u32(self, stream, addr, value):
         ctypes.c_uint32.from_address(addr).value = value
 
+    def wait_flags_bounded(self, stream, addrs, value, timeout_s, word_ptr):
+        for a in addrs:
+            self.wait_flag_bounded(stream, a, value, timeout_s, word_ptr)
+
     def wait_flag_bounded(self, stream, addr, value, timeout_s, word_ptr):
         t0 = time.monotonic()
         while ctypes.c_int32.from_address(addr).value < value:

@@ -93,6 +93,7 @@ _SIGS = {
     "wf_stream_wait_u32": (_i32, [_vp, _vp, _u32]),
     "wf_wait_flag": (_i32, [_vp, _u32, _u64, _vp, _vp]),
     "wf_stamp": (_i32, [_vp, _vp]),
+    "wf_wait_flags": (_i32, [_vp, _i32, _u32, _u64, _vp, _vp]),
     "wf_memcpy_async": (_i32, [_vp, _vp, _u64, _vp]),
     "wf_publish": (_i32, [C.POINTER(_vp), _vp, _u64, C.POINTER(_vp), _i32, _u32, _vp]),
 }

@@ -37,6 +37,33 @@ __global__ void wait_flag_kernel(const unsigned int* __restrict__ flag, unsigned
   }
 }
 
+// Up to 32 flags in one launch: lane i spins on flags.p[i] like
+// wait_flag_kernel; the kernel ends when every lane has seen its flag or
+// given up.
+constexpr int MAX_WAIT_FLAGS = 32;
+struct FlagList {
+  const unsigned int* p[MAX_WAIT_FLAGS];
+};
+__global__ void wait_flags_kernel(FlagList flags, int n, unsigned int value, unsigned long long timeout_ns,
+                                  unsigned int* __restrict__ timeout_out) {
+  const int i = threadIdx.x;
+  if (i >= n) return;
+  const uint64_t t0 = globaltimer_ns();
+  unsigned int ns = 32;
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags.p[i]) : "memory");
+    if (static_cast<int>(v - value) >= 0) return;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      if (timeout_out) *timeout_out = 1u;
+      status_raise(ST_FLAG_TIMEOUT);
+      return;
+    }
+    __nanosleep(ns);
+    if (ns < 1024) ns <<= 1;
+  }
+}
+
 // Writes the device's %globaltimer (ns) to *dst when the stream reaches it.
 __global__ void stamp_kernel(unsigned long long* __restrict__ dst) { *dst = globaltimer_ns(); }
 
@@ -118,6 +145,24 @@ extern "C" int wf_wait_flag(const void* flag, uint32_t value, uint64_t timeout_n
     return fail(WF_ERR_INVALID_ARG, "wf_wait_flag: timeout must be in (0, 600 s]");
   wait_flag_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const unsigned int*>(flag), value,
                                                                    timeout_ns, timeout_out);
+  WFK_CUDA_TRY(cudaGetLastError());
+  return WF_OK;
+}
+
+extern "C" int wf_wait_flags(const void* const* flags, int n, uint32_t value, uint64_t timeout_ns,
+                             uint32_t* timeout_out, void* stream) {
+  if (!flags || n < 0 || n > MAX_WAIT_FLAGS)
+    return fail(WF_ERR_INVALID_ARG, "wf_wait_flags: need a host array of 0..32 flag addresses");
+  if (timeout_ns == 0 || timeout_ns > 600ull * 1000000000ull)
+    return fail(WF_ERR_INVALID_ARG, "wf_wait_flags: timeout must be in (0, 600 s]");
+  FlagList fl{};
+  for (int i = 0; i < n; ++i) {
+    if (!flags[i] || (reinterpret_cast<uintptr_t>(flags[i]) & 3))
+      return fail(WF_ERR_INVALID_ARG, "wf_wait_flags: flag %d is null or misaligned", i);
+    fl.p[i] = static_cast<const unsigned int*>(flags[i]);
+  }
+  if (n == 0) return WF_OK;
+  wait_flags_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, n, value, timeout_ns, timeout_out);
   WFK_CUDA_TRY(cudaGetLastError());
   return WF_OK;
 }

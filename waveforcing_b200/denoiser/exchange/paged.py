@@ -370,6 +370,26 @@ class PagedTransport:
             e1.record(cur)
             sink.append((e0, e1))
 
+    def wait_all(self, m: int, srcs, layer: int, gen: int, tick: int) -> None:
+        """``wait`` for every producer in ``srcs`` of (gen, layer), the remote
+        ones in one bounded launch (``wf_wait_flags``)."""
+        addrs = [self.flags[m][self.src_index[m][src], gen, layer].data_ptr()
+                 for src in srcs if self.stage_rank[src] != self.rank]
+        if not addrs:
+            return
+        sink = self.wait_timer if self.device.type == "cuda" else None
+        if sink is not None:
+            cur = torch.cuda.current_stream(self.device)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+        ipc.wait_flags_bounded(self._cur_stream_handle(), addrs, tick, self.timeout_s, self.timeout_word.data_ptr())
+        if self.timeline is not None:
+            self.timeline.mark(f"s{m}.L{layer}.w")
+        if sink is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(cur)
+            sink.append((e0, e1))
+
     def remote_consumers(self) -> list[int]:
         """Consumer stages on other ranks that a stage on this rank publishes to."""
         return [m for m in range(self.store) if self.stage_rank[m] != self.rank
@@ -538,8 +558,7 @@ class PagedTransport:
                 parts = self.anchor_working_parts(clean[Lh], tick_csf, tick_qf)
                 if (0 if parts is None else 1 + len(parts[1])) != naw:
                     raise RuntimeError(f"[paged stage {m}] anchor+working != naw={naw} (t={tick})")
-                for src in recv:
-                    self.wait(m, src, Lh, gen, tick)
+                self.wait_all(m, recv, Lh, gen, tick)
                 e_wt = self._lp_mark(lp)
                 deq = []
                 if self.fp8:
@@ -561,8 +580,7 @@ class PagedTransport:
                     off += T
                 Kb[self_off:self_off + T].copy_(k)
                 Vb[self_off:self_off + T].copy_(v)
-                for src in recv:
-                    self.wait(m, src, Lh, gen, tick)
+                self.wait_all(m, recv, Lh, gen, tick)
                 e_wt = self._lp_mark(lp)
                 if self.fp8:
                     HD = self.H * self.D

@@ -31,6 +31,14 @@ def wait_flag_bounded(stream_handle: int, addr: int, value: int, timeout_s: floa
             "wait_flag_bounded")
 
 
+def wait_flags_bounded(stream_handle: int, addrs: list[int], value: int, timeout_s: float,
+                       timeout_out: int = 0) -> None:
+    """wait_flag_bounded over several flags in one launch (at most 32)."""
+    arr = (C.c_void_p * max(1, len(addrs)))(*addrs)
+    L.check(L.lib().wf_wait_flags(arr, len(addrs), value, int(timeout_s * 1e9), timeout_out or None, stream_handle),
+            "wait_flags_bounded")
+
+
 def memcpy_dtod_async(dst_ptr: int, src_ptr: int, nbytes: int, stream_handle: int) -> None:
     """ipc.py:60-67."""
     L.check(L.lib().wf_memcpy_async(dst_ptr, src_ptr, nbytes, stream_handle), "memcpy_dtod_async")
