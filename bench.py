@@ -583,7 +583,6 @@ def run_gpu_arm(args):
     from waveforcing_b200.runtime import backend
     from waveforcing_b200.runtime.fp8 import quantize_transformer_w8a8
     from waveforcing_b200.wavefront.dit import DiTConfig, WanDiT
-    from waveforcing_b200.wavefront import engine as engine_mod
     from waveforcing_b200.wavefront.engine import EngineConfig, WavefrontEngine
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -652,14 +651,13 @@ def run_gpu_arm(args):
     launches0 = kernels.LAUNCHES[0]
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     host_ms = []
-    with engine_mod.steady_host():  # (its entry collection runs before the first event)
-        evs[0].record()
-        torch.cuda.nvtx.range_push("timed")
-        for i in range(args.steps):
-            h0 = time.perf_counter()
-            eng.tick(fill + args.warmup + i)
-            host_ms.append((time.perf_counter() - h0) * 1e3)
-            evs[i + 1].record()
+    evs[0].record()
+    torch.cuda.nvtx.range_push("timed")
+    for i in range(args.steps):
+        h0 = time.perf_counter()
+        eng.tick(fill + args.warmup + i)
+        host_ms.append((time.perf_counter() - h0) * 1e3)
+        evs[i + 1].record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
@@ -707,16 +705,15 @@ def run_gpu_arm(args):
         barrier()
         torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(nt + 1)]
+        ev[0].record()
         d2h = 0
-        with engine_mod.steady_host():
-            ev[0].record()
-            for t in range(nt):
-                eng.tick(t)  # copies its noise chunk from pinned host memory (engine.noise_chunk)
-                c = t - eng.store
-                if c in eng.final:
-                    out_host.copy_(eng.final.pop(c), non_blocking=True)
-                    d2h += out_host.numel() * out_host.element_size()
-                ev[t + 1].record()
+        for t in range(nt):
+            eng.tick(t)  # copies its noise chunk from pinned host memory (engine.noise_chunk)
+            c = t - eng.store
+            if c in eng.final:
+                out_host.copy_(eng.final.pop(c), non_blocking=True)
+                d2h += out_host.numel() * out_host.element_size()
+            ev[t + 1].record()
         torch.cuda.synchronize()
         barrier()
         tms = max_over_ranks([ev[i].elapsed_time(ev[i + 1]) for i in range(nt)])

@@ -293,21 +293,3 @@ def test_kv_only_task_leaves_the_other_stages_unchanged(monkeypatch):
         torch.testing.assert_close(part[i], full[i], rtol=1e-5, atol=1e-5)  # fewer GEMM rows only
     assert m.forward_stages(tasks((True, True, True))[:1], fused=False) == [None]
 
-
-def test_steady_host_restores_the_collector():
-    """steady_host turns the cyclic collector off inside and restores it on
-    exit, also when the block raises."""
-    import gc
-
-    from waveforcing_b200.wavefront.engine import steady_host
-
-    assert gc.isenabled()
-    with steady_host():
-        assert not gc.isenabled()
-    assert gc.isenabled()
-    try:
-        with steady_host():
-            raise RuntimeError("tick failed")
-    except RuntimeError:
-        pass
-    assert gc.isenabled()

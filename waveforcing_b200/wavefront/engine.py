@@ -17,8 +17,6 @@ their linears.  Ranks beyond the stage count stay idle.
 
 from __future__ import annotations
 
-import contextlib
-import gc
 import time
 from dataclasses import dataclass, field
 
@@ -123,27 +121,6 @@ class _StoreKV(list):
 @dataclass
 class TickStats:
     tick_ms: list = field(default_factory=list)
-
-
-@contextlib.contextmanager
-def steady_host():
-    """Keeps Python's cyclic garbage collector out of a run of ticks.
-
-    The host issues a tick's ~1,400 launches only a little ahead of the
-    device, so a collector pause of tens of milliseconds (it walks every live
-    object once the young generations fill) leaves the GPU idle and lengthens
-    that tick.  Inside this context the collector is off (after one collection
-    at entry); on exit its previous state is restored and one collection runs.
-    Reference counting still frees tensors as usual."""
-    was = gc.isenabled()
-    gc.collect()
-    gc.disable()
-    try:
-        yield
-    finally:
-        if was:
-            gc.enable()
-        gc.collect()
 
 
 class WavefrontEngine:
