@@ -653,8 +653,11 @@ def run_gpu_arm(args):
     host_ms = []
     evs[0].record()
     torch.cuda.nvtx.range_push("timed")
+    ahead = 0  # ticks whose issue began while the device was still on earlier work
     for i in range(args.steps):
         h0 = time.perf_counter()
+        if i > 0:  # evs[i] closes tick i - 1
+            ahead += 0 if evs[i].query() else 1
         eng.tick(fill + args.warmup + i)
         host_ms.append((time.perf_counter() - h0) * 1e3)
         evs[i + 1].record()
@@ -684,6 +687,8 @@ def run_gpu_arm(args):
     crit = -max_over_ranks([-wait_ms_rank if eng.local else float("-inf")])[0]
     stage0_wait = max_over_ranks([wait_ms_rank if 0 in eng.local else 0.0])[0]
     host_p50 = max_over_ranks([statistics.median(host_ms)])[0]
+    # lowest over ranks: 1.0 means the host was ahead at every tick (device-bound)
+    host_ahead = -max_over_ranks([-ahead / max(1, args.steps - 1) if eng.local else float("-inf")])[0]
     if args.timeline:
         timeline_ticks(args, eng, fill + args.warmup + args.steps, dev, rank, world)
     eng.close()
@@ -780,6 +785,7 @@ def run_gpu_arm(args):
                                  "the critical rank is the active rank that waits least (the busiest: its "
                                  "waits are on the critical path); lighter ranks wait for slower producers"},
             "host_issue_ms_per_tick_p50": host_p50,
+            "host_ahead_frac": host_ahead,
             "gpu_launches": launches,
             "clocks": clocks,
         }
