@@ -210,12 +210,14 @@ class WavefrontEngine:
         tasks = []
         store_kv = _StoreKV(self.Ln, anchor=(t - self.store == 0))
         store_slot: dict = {}
+        slot_sink_given = False  # one stage per rank copies the store's live slot (all hold the same)
         for s in sorted(self.local, reverse=True):
             if s < S and self.act_denoise(s, t):
                 c = t - s
                 exch = self.xport.make_denoise_exch(s, self.clean, act, tick_csf, tick_qf, store_active, t,
-                                                    self._rope, store_slot if not store_slot else None,
+                                                    self._rope, None if slot_sink_given else store_slot,
                                                     rope_tab_fn=self._rope_tab)
+                slot_sink_given = True
                 tasks.append(StageTask(self.inputs[s], self.fm.timestep(cfg.steps[s]), c * cfg.npb, s, exch))
             elif s == self.store and store_active:
                 c = t - self.store
