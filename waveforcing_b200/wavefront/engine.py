@@ -210,7 +210,10 @@ class WavefrontEngine:
         tasks = []
         store_kv = _StoreKV(self.Ln, anchor=(t - self.store == 0))
         store_slot: dict = {}
-        slot_sink_given = False  # one stage per rank copies the store's live slot (all hold the same)
+        # one stage per rank copies the store's live slot (all hold the same);
+        # none when the store is idle or on this rank (_promote then keeps the
+        # store's own K/V and never reads the slot)
+        slot_sink_given = not store_active or self.store in self.local
         for s in sorted(self.local, reverse=True):
             if s < S and self.act_denoise(s, t):
                 c = t - s
